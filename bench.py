@@ -1,0 +1,378 @@
+"""Benchmark of the decoder token loop: decoder tokens/s on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+One bench step is one pass of the hot path over one batch of synthetic input:
+for every window on the GPU, the sequence start (cross-attention keys and
+values from the encoder rows), the prompt step, and greedy single-token steps
+until `steps` tokens per window are sampled -- WhisperEACP's decodeTranscript
+with no end-of-text stop.  The metric counts sampled tokens.
+
+Multi-GPU (torchrun, one process per GPU): every rank decodes its own batch
+of windows (weak scaling, no collective on the data path); the time is the
+maximum over ranks and the value is all ranks' tokens over that time.
+
+`--impl reference` times the reference's own CPU decoder (its scalar test
+decoder, compiled from its sources into oracle/_ref/libref_decoder.so) on the
+host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decoder tokens/s"
+UNIT = "tokens/s"
+DEFAULT_CONFIG = "base_en_b1"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--config", default=DEFAULT_CONFIG)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sm, sm_max, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.file.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[5:9]):
+                if value.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.file.name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(sm_max),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------- measurement
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            data = json.load(f)
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic(kernel: str, config: str):
+    """dram bytes per launch of `kernel` from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_{config}.md")
+    if not os.path.exists(path):
+        return None
+    match = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(match.group(1)) if match else None
+
+
+def step_bytes(run, mean_keys: float) -> dict:
+    """Algorithmic bytes of one single-token step (16-bit weights and caches):
+    w_b*(L*(6d^2 + 2dF) + V*d) + B*L*2d*(X + t + 1)*kv_b."""
+    s = run.shape
+    d, L, F, V, X = s.width, s.layers, s.feed_forward_width, s.vocabulary_size, s.cross_positions
+    weights = 2 * (L * (6 * d * d + 2 * d * F) + V * d)
+    kv = run.windows * L * 2 * d * (X + mean_keys) * 2
+    return {"weights": weights, "kv": kv, "logits_launch": 2 * V * d, "cross_launch": run.windows * 2 * d * X * 2}
+
+
+def cpu_baseline_port(run, tensors, encoder, threads: int) -> dict:
+    """The oracle (the reference's decoder restated, KV-cached, threaded) on a
+    bounded sample: the sequence start and 8 single-token steps of one window."""
+    from oracle import oracle as O
+    shape = O.Shape(**run.shape.__dict__)
+    session = O.Session(shape, tensors, threads=threads)
+    t0 = time.perf_counter()
+    session.begin(encoder[0])
+    t_begin = time.perf_counter() - t0
+    session.step(list(run.prompt), want_logits=True)
+    sample = 8
+    t0 = time.perf_counter()
+    for k in range(sample):
+        session.step([int(50 + k)], want_logits=True)
+    t_step = (time.perf_counter() - t0) / sample
+    per_window = t_begin + run.steps * t_step
+    return {"value": run.steps / per_window, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": (f"oracle/wsp_oracle.c on one window: sequence start ({t_begin:.2f} s) + "
+                       f"{sample} single-token steps ({t_step * 1e3:.1f} ms each), extrapolated to "
+                       f"{run.steps} tokens per window")}
+
+
+# --------------------------------------------------------------------- ours
+
+def run_ours(args, run):
+    import torch
+    from whispereacp_b200 import Decoder, synthetic as S
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    shape = run.shape
+    tensors = S.normal_weights(shape, seed=0)
+    encoder = S.encoder_output(run.windows, shape.cross_positions, shape.width, seed=1 + rank)
+    first, later = S.suppression_masks(shape.vocabulary_size)
+
+    decoder = Decoder(shape, windows=run.windows, device=local, storage=run.storage)
+    decoder.load_weights(tensors)
+    decoder.set_generation(run.prompt, first, later, maximum_tokens=run.steps,
+                           end_of_text=S.END_OF_TEXT, stop_at_end_of_text=False)
+    stream = torch.cuda.ExternalStream(decoder.stream, device=local)
+    device_rows = torch.from_numpy(encoder).to(f"cuda:{local}")
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{local}")
+    torch.cuda.synchronize()
+
+    def one_step():
+        decoder.enqueue_transcribe(device_rows.data_ptr(), run.steps)
+
+    for _ in range(args.warmup):
+        one_step()
+    decoder.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    for i in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()              # L2 flush, outside the timed intervals
+            starts[i].record(stream)
+        one_step()
+        stops[i].record(stream)
+    decoder.synchronize()
+    torch.cuda.synchronize()
+    clock_record = clocks.stop()
+    if world > 1:
+        torch.distributed.barrier()
+    elapsed_ms = sum(s.elapsed_time(e) for s, e in zip(starts, stops))
+    transcript = decoder.read_transcript()
+    assert all(len(t) == run.steps for t in transcript)
+
+    # End to end through the public call: pinned host rows in, token ids out.
+    pinned = torch.from_numpy(encoder).pin_memory()
+    e2e_ms = []
+    for i in range(max(2, min(args.steps, 5)) + 1):
+        start = torch.cuda.Event(enable_timing=True)
+        stop = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        decoder.transcribe(pinned.data_ptr())
+        stop.record(stream)
+        stop.synchronize()
+        if i > 0:
+            e2e_ms.append(start.elapsed_time(stop))
+    e2e_step_ms = statistics.median(e2e_ms)
+
+    # Per-kernel launch durations, measured live (events around each launch).
+    decoder.enqueue_transcribe(device_rows.data_ptr(), 2)
+    per_kernel = decoder.time_kernels(min(64, shape.max_positions - len(run.prompt) - 2))
+    decoder.synchronize()
+
+    step_ms = elapsed_ms / args.steps
+    if world > 1:
+        t = torch.tensor([step_ms, e2e_step_ms], device=f"cuda:{local}")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        step_ms, e2e_step_ms = t.tolist()
+
+    tokens = run.windows * run.steps * world
+    result = None
+    if rank == 0:
+        peak, peak_kind = peaks()
+        ms_logits = per_kernel["logits_argmax"][0]
+        ms_cross = per_kernel["cross_attention"][0]
+        mean_keys = len(run.prompt) + run.steps / 2
+        nbytes = step_bytes(run, mean_keys)
+        # The dominant kernel: whichever of the two streaming kernels takes
+        # more of a step.
+        launches = per_kernel
+        share = {k: v[0] * v[1] for k, v in launches.items()}
+        dominant = max(("logits_argmax", "cross_attention"), key=lambda k: share[k])
+        if dominant == "logits_argmax":
+            algorithmic, duration = nbytes["logits_launch"], ms_logits
+        else:
+            algorithmic, duration = nbytes["cross_launch"], ms_cross
+        achieved = algorithmic / (duration * 1e-3) / 1e9
+        step_ms_single = sum(v[0] * v[1] for v in launches.values())
+        h2d = encoder.nbytes
+        d2h = run.windows * (shape.max_positions + 1) * 4
+        result = {
+            "metric": METRIC, "value": tokens / (step_ms * 1e-3), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16" if run.storage == "float16" else "bf16",
+            "data": "synthetic (random-init weights N(0,0.02), encoder rows N(0,1))",
+            "config": {"workload": run.description, "name": run.name, "windows_per_gpu": run.windows,
+                       "tokens_per_window": run.steps, "prompt": list(run.prompt),
+                       "cross_positions": shape.cross_positions, "d_model": shape.width,
+                       "decoder_layers": shape.layers, "vocabulary": shape.vocabulary_size,
+                       "step": "sequence start + prompt step + greedy single-token steps (graph)",
+                       "l2": "flushed (256 MiB write) between timed steps, outside the timed intervals",
+                       "parallelism": f"dp{world} (independent windows per GPU)"},
+            "batch1_ms_per_token_step": step_ms / run.steps,
+            "e2e": {"value": tokens / (e2e_step_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * (1 + decoder.step_launches() * run.steps),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": committed_traffic(dominant, run.name),
+                         "kernel": dominant, "peak_source": f"{peak_kind} hbm_gbs (burst)",
+                         "algorithmic_bytes_per_launch": algorithmic,
+                         "launch_ms": duration},
+            "step_roofline": {"algorithmic_bytes": nbytes["weights"] + nbytes["kv"],
+                              "single_step_ms_launch_by_launch": step_ms_single,
+                              "graph_step_ms": step_ms / run.steps,
+                              "frac_of_peak": (nbytes["weights"] + nbytes["kv"]) /
+                              (step_ms / run.steps * 1e-3) / 1e9 / peak},
+            "kernels_ms_per_launch": {k: {"ms": v[0], "launches_per_step": v[1]} for k, v in launches.items()},
+            "clocks": clock_record,
+        }
+        if not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            result["cpu_baseline"] = cpu_baseline_port(run, tensors_for_oracle(tensors, run.storage),
+                                                       encoder, threads)
+    decoder.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return result
+
+
+def tensors_for_oracle(tensors, storage):
+    from tests.helpers import stored_tensors
+    return stored_tensors(tensors, storage)
+
+
+# ---------------------------------------------------------------- reference
+
+def run_reference(args, run):
+    """The reference's own CPU decoder (Tests/Decoder/Common.h:360-468, compiled
+    from its sources) as a greedy decoder: each generated token is one
+    referenceDecode over the prefix, which is how that implementation decodes.
+    All host threads decode independent windows at once (ctypes releases the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import oracle as O
+    from whispereacp_b200 import synthetic as S
+    from tests.golden.make_golden import load_reference, ref_decode
+
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return None
+    path = os.path.join(ROOT, "oracle", "_ref", "libref_decoder.so")
+    if not os.path.exists(path):
+        return {"impl": "reference", "unavailable": "oracle/_ref/libref_decoder.so was not built"}
+    ref, _ = load_reference()
+    shape = O.Shape(**run.shape.__dict__)
+    tensors = tensors_for_oracle(S.normal_weights(run.shape, seed=0), run.storage)
+    encoder = S.encoder_output(1, shape.cross_positions, shape.width, seed=1)[0]
+    threads = os.cpu_count() or 1
+    prefix = [*run.prompt, 50, 51]
+
+    def one_token(_):
+        ref_decode(ref, shape, tensors, encoder, prefix)
+        return 1
+
+    pool = ThreadPoolExecutor(max_workers=threads)
+    for _ in range(args.warmup):
+        list(pool.map(one_token, range(threads)))
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        list(pool.map(one_token, range(threads)))
+        times.append(time.perf_counter() - t0)
+    pool.shutdown()
+    step_s = sum(times) / len(times)
+    value = threads / step_s
+    sample = (f"{threads} concurrent referenceDecode calls (one per host thread), each over a "
+              f"{len(prefix)}-token prefix with {shape.cross_positions} encoder rows: one generated "
+              f"token each, the cost of one greedy step in that implementation")
+    return {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": run.description, "name": run.name}, "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse_args()
+    from whispereacp_b200.synthetic import CONFIGS
+    run = CONFIGS[args.config]
+    result = run_reference(args, run) if args.impl == "reference" else run_ours(args, run)
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,213 @@
+/*
+ * wsp_decoder.h -- the C ABI of the B200 decoder token loop.
+ *
+ * This is the thin layer the C++ host code of a Whisper runtime reaches CUDA
+ * through: plain pointers, sizes and int status codes, no C++ or torch types.
+ * Each entry point names the WhisperEACP interface (path:line within that
+ * project) whose role it takes over; INTEGRATION.md shows the binding a
+ * maintainer adds on the reference side.
+ *
+ * Conventions
+ *   - Every function returns a wsp_status.  A failure leaves the decoder as it
+ *     was (validation happens on the host before anything is launched, as in
+ *     Decoder.cpp:276-289) and its text is readable through wsp_last_error()
+ *     on the calling thread.
+ *   - Pointers to data (encoder rows, tokens, logits, masks) may be host or
+ *     device pointers; unified addressing decides which, and host buffers are
+ *     copied in/out inside the call.
+ *   - A decoder is bound to one device and is not thread-safe.  Several GPUs
+ *     are driven by several decoders, one host thread (or process) each.
+ *   - "windows" is the batch: independent 30 s windows decoded in lockstep,
+ *     each with its own self- and cross-attention caches.  WhisperEACP decodes
+ *     one window at a time; windows == 1 is its behaviour.
+ */
+#ifndef WSP_DECODER_H
+#define WSP_DECODER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WSP_ABI_VERSION 1
+
+typedef enum wsp_status {
+    WSP_OK = 0,
+    WSP_MODEL_ERROR = 1,      /* WSP::ModelError: shapes, capacities, tensors  */
+    WSP_LOGIC_ERROR = 2,      /* std::logic_error: misuse (e.g. step before begin) */
+    WSP_INVALID_ARGUMENT = 3, /* std::invalid_argument (Argmax.cpp:54-58)     */
+    WSP_CUDA_ERROR = 4,
+    WSP_OUT_OF_MEMORY = 5
+} wsp_status;
+
+/* Element types of tensors handed in, and the decoder's 16-bit storage. */
+typedef enum wsp_dtype {
+    WSP_FLOAT32 = 0,
+    WSP_FLOAT16 = 1,
+    WSP_BFLOAT16 = 2
+} wsp_dtype;
+
+/* DecoderShape, Lib/WhisperEACP/Decoder/DecoderShape.h:20-31. */
+typedef struct wsp_decoder_shape {
+    int32_t width;
+    int32_t heads;
+    int32_t layers;
+    int32_t feed_forward_width;
+    int32_t vocabulary_size;
+    int32_t max_positions;   /* max_target_positions: the self-attention capacity */
+    int32_t cross_positions; /* encoder rows a sequence may attend to            */
+} wsp_decoder_shape;
+
+typedef struct wsp_decoder wsp_decoder;
+
+/* Text of the last failure on this thread ("" when none). */
+const char* wsp_last_error(void);
+
+/* Library build and device queries. */
+int wsp_abi_version(void);
+int wsp_device_count(int* count);
+
+/*
+ * Decoder construction and Decoder::prepare
+ * (Lib/WhisperEACP/Decoder/Decoder.h:49-66, Decoder.cpp:179-227): sizes every
+ * cache and intermediate once, for `windows` windows, on `device`.  storage
+ * is the 16-bit type weights, activations and caches are kept in
+ * (WSP_FLOAT16 or WSP_BFLOAT16); products accumulate in fp32.
+ */
+int wsp_decoder_create(const wsp_decoder_shape* shape, int device, int windows,
+                       wsp_dtype storage, wsp_decoder** out);
+void wsp_decoder_destroy(wsp_decoder* decoder);
+
+/*
+ * One tensor of a decoder checkpoint under its HuggingFace name, the role of
+ * DecoderWeights / DecoderLayerWeights (Lib/WhisperEACP/Decoder/
+ * DecoderWeights.h:25-160, DecoderWeights.cpp:74-178): "model.decoder.
+ * layers.3.encoder_attn.q_proj.weight" and the rest.  The data (host memory)
+ * is narrowed to the decoder's storage type and laid out for the kernels.  A
+ * wrong rank or extent is WSP_MODEL_ERROR naming the tensor; a name outside
+ * "model.decoder." is ignored (a full Whisper file carries the encoder too).
+ */
+int wsp_decoder_set_tensor(wsp_decoder* decoder, const char* name, wsp_dtype dtype,
+                           const int64_t* extents, int rank, const void* data);
+
+/* WSP_MODEL_ERROR naming the first decoder tensor not yet set, else WSP_OK. */
+int wsp_decoder_check_weights(const wsp_decoder* decoder);
+
+/*
+ * Decoder::beginSequence (Decoder.h:67-73, Decoder.cpp:229-268;
+ * recordSequenceStart Decoder.cpp:121-146): for every window, projects the
+ * cross-attention keys and values of every layer out of its encoder rows and
+ * resets the position to zero.  encoder_rows is fp32
+ * [windows, shape.cross_positions, width]; cross_positions is how many of
+ * each window's rows the sequence attends to (0 = all).
+ */
+int wsp_decoder_begin_sequence(wsp_decoder* decoder, const float* encoder_rows,
+                               int cross_positions);
+
+/*
+ * Decoder::step (Decoder.h:75-98, Decoder.cpp:270-308; recordDecoderStep
+ * Decoder.cpp:151-177): appends token_count tokens to every window.
+ *   tokens  uint32 [windows, token_count]
+ *   logits  fp32 [windows, token_count, vocabulary] or NULL
+ *   hidden  fp32 [windows, token_count, width] (the rows after the final layer
+ *           norm, Decoder.h:109-115) or NULL
+ *   argmax  uint32 [windows, token_count]: the unmasked greedy token of each
+ *           row (the DecoderRun harness's Argmax, Tests/Decoder/Common.h:
+ *           618-660), or NULL
+ * A step past max_positions is WSP_MODEL_ERROR before anything is launched.
+ */
+int wsp_decoder_step(wsp_decoder* decoder, const uint32_t* tokens, int token_count,
+                     float* logits, float* hidden, uint32_t* argmax);
+
+/* Decoder::position / Decoder::crossPositions (Decoder.h:100-107). */
+int wsp_decoder_position(const wsp_decoder* decoder, int* position);
+int wsp_decoder_cross_positions(const wsp_decoder* decoder, int* cross_positions);
+
+/*
+ * Greedy search configuration, the generation config Whisper::load builds
+ * (Lib/WhisperEACP/Whisper/Whisper.cpp:148-254): the prompt
+ * (buildPrompt, :207-225), the two suppression masks (buildSuppressionMasks,
+ * :227-254; fp32 [vocabulary], nonzero = suppressed; the first applies to the
+ * prompt step only), the token limit (maximumTokens, 448 - prompt) and the
+ * end-of-text id that stops a window.
+ */
+typedef struct wsp_generation_config {
+    const uint32_t* prompt;
+    int32_t prompt_length;
+    const float* first_step_mask;
+    const float* later_step_mask;
+    int32_t maximum_tokens;
+    uint32_t end_of_text;
+    int32_t stop_at_end_of_text; /* 0: run every step (benchmarks)          */
+} wsp_generation_config;
+
+int wsp_decoder_set_generation(wsp_decoder* decoder, const wsp_generation_config* config);
+
+/*
+ * Whisper::decodeTranscript (Whisper.cpp:1361-1449) with encodeStep and
+ * encodeSampling (:1169-1213) for every window: begins the sequence over
+ * encoder_rows, decodes the prompt in one step, then one token a step, each
+ * sampled by masked argmax straight into the device token ring the next step
+ * embeds.  The step limit is min(maximum_tokens, max_positions - prompt + 1)
+ * (Whisper.cpp:1375-1377).  tokens receives uint32 [windows, step limit] (the
+ * sampled ids, end-of-text excluded) and counts int32 [windows] (each
+ * window's transcript length: up to its first end-of-text when stopping on
+ * it).  The single-token step runs as one CUDA graph.
+ */
+int wsp_decoder_transcribe(wsp_decoder* decoder, const float* encoder_rows,
+                           int cross_positions, uint32_t* tokens, int32_t* counts);
+
+/*
+ * The same search split for timing: enqueue begins the sequence and queues
+ * `steps` sampled steps on the decoder's stream without waiting (no early
+ * stop); read waits and copies the transcript out as transcribe does.
+ */
+int wsp_decoder_enqueue_transcribe(wsp_decoder* decoder, const float* encoder_rows,
+                                   int cross_positions, int steps);
+int wsp_decoder_read_transcript(wsp_decoder* decoder, uint32_t* tokens, int32_t* counts);
+
+/* The CUDA stream every launch of this decoder goes to (a cudaStream_t). */
+void* wsp_decoder_stream(wsp_decoder* decoder);
+int wsp_decoder_synchronize(wsp_decoder* decoder);
+
+/*
+ * Per-kernel timing for measurement: runs `steps` single-token greedy steps
+ * launch by launch with CUDA events around each kernel, and writes the mean
+ * milliseconds per launch of each kernel class into ms[WSP_KERNEL_CLASSES]
+ * and the number of launches per step into launches[WSP_KERNEL_CLASSES].
+ */
+enum {
+    WSP_KERNEL_EMBED = 0,
+    WSP_KERNEL_LAYER_NORM = 1,
+    WSP_KERNEL_PROJECTION = 2,
+    WSP_KERNEL_SELF_ATTENTION = 3,
+    WSP_KERNEL_CROSS_ATTENTION = 4,
+    WSP_KERNEL_ATTENTION_COMBINE = 5,
+    WSP_KERNEL_LOGITS_ARGMAX = 6,
+    WSP_KERNEL_ARGMAX_FINAL = 7,
+    WSP_KERNEL_OTHER = 8,
+    WSP_KERNEL_CLASSES = 9
+};
+int wsp_decoder_time_kernels(wsp_decoder* decoder, int steps, float* ms, int* launches);
+
+/* Launches of this library's kernels per single-token step (graph nodes). */
+int wsp_decoder_step_launches(const wsp_decoder* decoder, int* launches);
+
+/*
+ * Argmax::encode (Lib/WhisperEACP/Kernels/Argmax.h:207-262,
+ * Argmax.cpp:47-80): indices[row] = the first j maximising
+ * logits[row*row_length + j] over mask[j] == 0; a row with everything
+ * suppressed gives 0.  logits, mask and indices are device pointers; stream
+ * is a cudaStream_t (NULL: the legacy stream).  The call waits for its
+ * result.
+ */
+int wsp_argmax(const float* logits, const float* mask, uint32_t* indices, int row_count,
+               int row_length, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,136 @@
+"""Seeded synthetic models and inputs for the benchmark configurations.
+
+No checkpoint or dataset is available offline, so every configuration runs on
+random-init weights of the named architecture: N(0, 0.02) for every matrix,
+embedding and bias, layer-norm gains 1 and offsets 0; encoder outputs N(0, 1).
+Normals come from an explicit Box-Muller transform over numpy's PCG64
+uniforms, seeded per tensor from a CRC of its name, so the values do not
+depend on any library's normal sampler.
+"""
+from __future__ import annotations
+
+import zlib
+from dataclasses import dataclass
+
+import numpy as np
+
+from .decoder import DecoderShape
+
+START_OF_TRANSCRIPT = 50257
+NO_TIMESTAMPS = 50362
+END_OF_TEXT = 50256
+LEADING_SPACE = 220
+
+
+@dataclass(frozen=True)
+class RunConfig:
+    """One benchmark configuration (the decoder part of it)."""
+    name: str
+    shape: DecoderShape
+    windows: int          # windows on one GPU
+    storage: str          # 16-bit type of weights, activations and caches
+    prompt: tuple         # prompt token ids
+    steps: int            # sampled steps per window (the prompt step included)
+    description: str
+
+
+def _shape(d, heads, layers, vocab=51864):
+    return DecoderShape(width=d, heads=heads, layers=layers, feed_forward_width=4 * d,
+                        vocabulary_size=vocab, max_positions=448, cross_positions=1500)
+
+
+ENGLISH_PROMPT = (START_OF_TRANSCRIPT, NO_TIMESTAMPS)
+# A multilingual four-special-token prompt: start, language, task, no-timestamps.
+MULTILINGUAL_PROMPT = (50258, 50259, 50360, 50364)
+
+CONFIGS = {
+    "tiny_en_b1": RunConfig("tiny_en_b1", _shape(384, 6, 4), 1, "float16", ENGLISH_PROMPT, 224,
+                            "tiny.en decoder, 1 window"),
+    "base_en_b1": RunConfig("base_en_b1", _shape(512, 8, 6), 1, "float16", ENGLISH_PROMPT, 224,
+                            "base.en decoder, 1 window"),
+    "small_en_b32": RunConfig("small_en_b32", _shape(768, 12, 12), 32, "float16", ENGLISH_PROMPT, 224,
+                              "small.en decoder, 32 windows, fp16"),
+    "medium_en_b64": RunConfig("medium_en_b64", _shape(1024, 16, 24), 64, "bfloat16", ENGLISH_PROMPT,
+                               224, "medium.en decoder, 64 windows, bf16"),
+    "large_v3_b128": RunConfig("large_v3_b128", _shape(1280, 20, 32, vocab=51866), 128, "bfloat16",
+                               MULTILINGUAL_PROMPT, 444, "large-v3 decoder, 128 windows, bf16"),
+}
+
+
+def _seed(name: str, base_seed: int) -> int:
+    return (zlib.crc32(name.encode()) ^ (base_seed * 0x9E3779B1)) & 0xFFFFFFFF
+
+
+def box_muller(count: int, seed: int, std: float = 1.0) -> np.ndarray:
+    """count normals N(0, std^2) from PCG64 uniforms, cos branch of Box-Muller."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    u1 = 1.0 - rng.random(count)  # (0, 1]
+    u2 = rng.random(count)
+    return (std * np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * np.pi * u2)).astype(np.float32)
+
+
+def decoder_tensor_extents(shape: DecoderShape) -> dict[str, tuple[int, ...]]:
+    """Every decoder tensor of a HuggingFace Whisper checkpoint, with its extents."""
+    d, f = shape.width, shape.feed_forward_width
+    out = {"model.decoder.embed_tokens.weight": (shape.vocabulary_size, d),
+           "model.decoder.embed_positions.weight": (shape.max_positions, d),
+           "model.decoder.layer_norm.weight": (d,), "model.decoder.layer_norm.bias": (d,)}
+    for layer in range(shape.layers):
+        p = f"model.decoder.layers.{layer}."
+        for attention, norm in (("self_attn", "self_attn_layer_norm"),
+                                ("encoder_attn", "encoder_attn_layer_norm")):
+            out[p + norm + ".weight"] = (d,)
+            out[p + norm + ".bias"] = (d,)
+            for proj in ("q_proj", "k_proj", "v_proj", "out_proj"):
+                out[p + attention + "." + proj + ".weight"] = (d, d)
+                if proj != "k_proj":
+                    out[p + attention + "." + proj + ".bias"] = (d,)
+        out[p + "final_layer_norm.weight"] = (d,)
+        out[p + "final_layer_norm.bias"] = (d,)
+        out[p + "fc1.weight"] = (f, d)
+        out[p + "fc1.bias"] = (f,)
+        out[p + "fc2.weight"] = (d, f)
+        out[p + "fc2.bias"] = (d,)
+    return out
+
+
+def normal_weights(shape: DecoderShape, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
+    """Random-init decoder: N(0, std) everywhere but layer norms (gain 1, offset 0)."""
+    tensors = {}
+    for name, extents in decoder_tensor_extents(shape).items():
+        count = int(np.prod(extents))
+        if "layer_norm" in name:
+            tensors[name] = np.full(extents, 1.0 if name.endswith("weight") else 0.0, np.float32)
+        else:
+            tensors[name] = box_muller(count, _seed(name, seed), std).reshape(extents)
+    return tensors
+
+
+def encoder_output(windows: int, positions: int, width: int, seed: int = 1) -> np.ndarray:
+    """Seeded N(0, 1) stand-in for the encoder's output, [windows, positions, width]."""
+    return box_muller(windows * positions * width, _seed("encoder_output", seed)).reshape(
+        windows, positions, width)
+
+
+def teacher_tokens(count: int, seed: int = 2, high: int = END_OF_TEXT) -> np.ndarray:
+    """Seeded uniform token ids in [0, high] for teacher-forced steps."""
+    rng = np.random.Generator(np.random.PCG64(_seed("teacher_tokens", seed)))
+    return rng.integers(0, high + 1, size=count, dtype=np.int64).astype(np.uint32)
+
+
+def suppression_masks(vocabulary: int, seed: int = 3) -> tuple[np.ndarray, np.ndarray]:
+    """(first-step mask, later-step mask) in the shape of Whisper's generation config.
+
+    The later mask suppresses 90 ids -- <|startoftranscript|> and 89 seeded ids
+    below <|endoftext|> -- at every step; the first mask adds the two
+    begin-suppress ids, a leading space and <|endoftext|>
+    (Tests/Whisper/WhisperTests.cpp:171-213 states the rule).
+    """
+    rng = np.random.Generator(np.random.PCG64(_seed("suppress_tokens", seed)))
+    candidates = np.setdiff1d(np.arange(1, END_OF_TEXT), [LEADING_SPACE])
+    ids = np.concatenate([[START_OF_TRANSCRIPT], rng.choice(candidates, 89, replace=False)])
+    later = np.zeros(vocabulary, np.float32)
+    later[ids[ids < vocabulary]] = 1.0
+    first = later.copy()
+    first[[LEADING_SPACE, END_OF_TEXT]] = 1.0
+    return first, later
