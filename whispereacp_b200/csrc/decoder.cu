@@ -7,6 +7,7 @@
 //   greedy search                                      Lib/WhisperEACP/Whisper/Whisper.cpp:148-254,1158-1449
 #include "../../include/wsp_decoder.h"
 #include "kernels.cuh"
+#include "step_launch.h"
 
 #include <cublas_v2.h>
 #include <cuda_bf16.h>
@@ -138,36 +139,6 @@ struct LayerBuffers {
     DeviceBuffer ln3_w, ln3_b, fc1_w, fc1_b, fc2_w, fc2_b;
 };
 
-// Per-kernel-class CUDA event timing for measurement runs.
-struct KernelTimer {
-    cudaStream_t stream;
-    std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> marks;
-    int open_class = -1;
-    cudaEvent_t open_start = nullptr;
-
-    cudaEvent_t make() {
-        cudaEvent_t e;
-        CUDA_CHECK(cudaEventCreate(&e));
-        return e;
-    }
-    void begin(int cls) {
-        open_class = cls;
-        open_start = make();
-        CUDA_CHECK(cudaEventRecord(open_start, stream));
-    }
-    void end() {
-        cudaEvent_t stop = make();
-        CUDA_CHECK(cudaEventRecord(stop, stream));
-        marks.push_back({open_class, {open_start, stop}});
-    }
-    ~KernelTimer() {
-        for (auto& m : marks) {
-            cudaEventDestroy(m.second.first);
-            cudaEventDestroy(m.second.second);
-        }
-    }
-};
-
 class Decoder {
 public:
     Decoder(const wsp_decoder_shape& shape, int device, int windows, Storage storage)
@@ -185,10 +156,8 @@ public:
 
     ~Decoder() {
         cudaSetDevice(device_);
-        drop_graph();
         if (cublas_) cublasDestroy(cublas_);
         if (stream_) cudaStreamDestroy(stream_);
-        if (pinned_ring_) cudaFreeHost(pinned_ring_);
     }
 
     // ---------------------------------------------------------------- weights
@@ -209,7 +178,7 @@ public:
         if (global >= 0) {
             if (global == 0) {
                 require_extents(name, extents, rank, {shape_.vocabulary_size, d});
-                upload_matrix(token_table_, 0, shape_.vocabulary_size, d, padded(d), dtype, data);
+                upload_packed(token_table_, 0, shape_.vocabulary_size, d, padded(d), dtype, data);
             } else if (global == 1) {
                 // A model may carry more positions than a run needs; fewer is an error.
                 if (rank != 2 || extents[1] != d || extents[0] < shape_.max_positions)
@@ -248,16 +217,16 @@ public:
         switch (which) {
         case 0: require_extents(name, extents, rank, {d}); upload_floats(L.ln1_w, 0, d, dtype, data); break;
         case 1: require_extents(name, extents, rank, {d}); upload_floats(L.ln1_b, 0, d, dtype, data); break;
-        case 2: require_extents(name, extents, rank, {d, d}); upload_matrix(L.qkv_w, 0, d, d, kpd, dtype, data); break;
+        case 2: require_extents(name, extents, rank, {d, d}); upload_packed(L.qkv_w, 0, d, d, kpd, dtype, data); break;
         case 3: require_extents(name, extents, rank, {d}); upload_floats(L.qkv_b, 0, d, dtype, data); break;
-        case 4: require_extents(name, extents, rank, {d, d}); upload_matrix(L.qkv_w, d, d, d, kpd, dtype, data); break;
-        case 5: require_extents(name, extents, rank, {d, d}); upload_matrix(L.qkv_w, 2 * d, d, d, kpd, dtype, data); break;
+        case 4: require_extents(name, extents, rank, {d, d}); upload_packed(L.qkv_w, d, d, d, kpd, dtype, data); break;
+        case 5: require_extents(name, extents, rank, {d, d}); upload_packed(L.qkv_w, 2 * d, d, d, kpd, dtype, data); break;
         case 6: require_extents(name, extents, rank, {d}); upload_floats(L.qkv_b, 2 * d, d, dtype, data); break;
-        case 7: require_extents(name, extents, rank, {d, d}); upload_matrix(L.o_w, 0, d, d, kpd, dtype, data); break;
+        case 7: require_extents(name, extents, rank, {d, d}); upload_packed(L.o_w, 0, d, d, kpd, dtype, data); break;
         case 8: require_extents(name, extents, rank, {d}); upload_floats(L.o_b, 0, d, dtype, data); break;
         case 9: require_extents(name, extents, rank, {d}); upload_floats(L.ln2_w, 0, d, dtype, data); break;
         case 10: require_extents(name, extents, rank, {d}); upload_floats(L.ln2_b, 0, d, dtype, data); break;
-        case 11: require_extents(name, extents, rank, {d, d}); upload_matrix(L.qc_w, 0, d, d, kpd, dtype, data); break;
+        case 11: require_extents(name, extents, rank, {d, d}); upload_packed(L.qc_w, 0, d, d, kpd, dtype, data); break;
         case 12: require_extents(name, extents, rank, {d}); upload_floats(L.qc_b, 0, d, dtype, data); break;
         case 13:  // cross keys: rows [l*2d, l*2d+d) of the all-layer projection
             require_extents(name, extents, rank, {d, d});
@@ -268,13 +237,13 @@ public:
             upload_matrix(cross_kv_w_, (size_t)layer * 2 * d + d, d, d, d, dtype, data);
             break;
         case 15: require_extents(name, extents, rank, {d}); upload_floats(L.vc_b, 0, d, dtype, data); break;
-        case 16: require_extents(name, extents, rank, {d, d}); upload_matrix(L.oc_w, 0, d, d, kpd, dtype, data); break;
+        case 16: require_extents(name, extents, rank, {d, d}); upload_packed(L.oc_w, 0, d, d, kpd, dtype, data); break;
         case 17: require_extents(name, extents, rank, {d}); upload_floats(L.oc_b, 0, d, dtype, data); break;
         case 18: require_extents(name, extents, rank, {d}); upload_floats(L.ln3_w, 0, d, dtype, data); break;
         case 19: require_extents(name, extents, rank, {d}); upload_floats(L.ln3_b, 0, d, dtype, data); break;
-        case 20: require_extents(name, extents, rank, {f, d}); upload_matrix(L.fc1_w, 0, f, d, kpd, dtype, data); break;
+        case 20: require_extents(name, extents, rank, {f, d}); upload_packed(L.fc1_w, 0, f, d, kpd, dtype, data); break;
         case 21: require_extents(name, extents, rank, {f}); upload_floats(L.fc1_b, 0, f, dtype, data); break;
-        case 22: require_extents(name, extents, rank, {d, f}); upload_matrix(L.fc2_w, 0, d, f, kpf, dtype, data); break;
+        case 22: require_extents(name, extents, rank, {d, f}); upload_packed(L.fc2_w, 0, d, f, kpf, dtype, data); break;
         case 23: require_extents(name, extents, rank, {d}); upload_floats(L.fc2_b, 0, d, dtype, data); break;
         }
         present_[4 + 24 * layer + which] = true;
@@ -323,9 +292,8 @@ public:
                          type, n, (long long)shape_.cross_positions * n, windows_, CUBLAS_COMPUTE_32F,
                          CUBLAS_GEMM_DEFAULT),
                      "cross key/value projection");
-        CUDA_CHECK(cudaMemsetAsync(state_.get(), 0, 2 * sizeof(int), stream_));
+        CUDA_CHECK(cudaMemsetAsync(state_.get(), 0, kStateWords * sizeof(int), stream_));
         CUDA_CHECK(cudaGetLastError());
-        if (rows != active_cross_) drop_graph();
         active_cross_ = rows;
         position_ = 0;
         started_ = true;
@@ -359,21 +327,15 @@ public:
         const bool hidden_on_device = hidden && is_device_pointer(hidden);
         if (logits && !logits_on_device) ensure_staging(logits_staging_, (size_t)R * shape_.vocabulary_size * 4);
         if (hidden && !hidden_on_device) ensure_staging(hidden_staging_, (size_t)R * shape_.width * 4);
-        StepPlan plan;
-        plan.tokens = count;
-        plan.sample_last_only = false;
-        plan.mask = nullptr;
-        plan.logits = logits ? (logits_on_device ? logits : logits_staging_.get<float>()) : nullptr;
-        plan.hidden = hidden ? (hidden_on_device ? hidden : hidden_staging_.get<float>()) : nullptr;
-        plan.row_tokens = row_tokens_.get<uint32_t>();
-        plan.write_ring = false;
-        record_step(plan, nullptr);
-        CUDA_CHECK(cudaGetLastError());
+        float* logits_dev = logits ? (logits_on_device ? logits : logits_staging_.get<float>()) : nullptr;
+        float* hidden_dev = hidden ? (hidden_on_device ? hidden : hidden_staging_.get<float>()) : nullptr;
+        launch_steps(count, /*sample=*/false, nullptr, logits_dev, hidden_dev, row_tokens_.get<uint32_t>(), 1,
+                     /*stop=*/false, nullptr);
         if (logits && !logits_on_device)
-            CUDA_CHECK(cudaMemcpyAsync(logits, plan.logits, (size_t)R * shape_.vocabulary_size * 4,
+            CUDA_CHECK(cudaMemcpyAsync(logits, logits_dev, (size_t)R * shape_.vocabulary_size * 4,
                                        cudaMemcpyDeviceToHost, stream_));
         if (hidden && !hidden_on_device)
-            CUDA_CHECK(cudaMemcpyAsync(hidden, plan.hidden, (size_t)R * shape_.width * 4, cudaMemcpyDeviceToHost,
+            CUDA_CHECK(cudaMemcpyAsync(hidden, hidden_dev, (size_t)R * shape_.width * 4, cudaMemcpyDeviceToHost,
                                        stream_));
         if (argmax)
             CUDA_CHECK(cudaMemcpyAsync(argmax, row_tokens_.get(), (size_t)R * 4, cudaMemcpyDefault, stream_));
@@ -426,21 +388,25 @@ public:
         begin_sequence(encoder_rows, cross_positions);
         CUDA_CHECK(cudaMemcpyAsync(ring_.get(), ring_prompt_.get(), ring_prompt_.bytes(), cudaMemcpyDeviceToDevice,
                                    stream_));
-        StepPlan plan = sampling_plan((int)prompt_.size(), masks_.get<float>());
-        record_step(plan, nullptr);
-        CUDA_CHECK(cudaGetLastError());
+        CUDA_CHECK(cudaMemsetAsync(ended_.get(), 0, ended_.bytes(), stream_));
+        ensure_row_capacity((int)prompt_.size());
+        launch_steps((int)prompt_.size(), /*sample=*/true, masks_.get<float>(), nullptr, nullptr, nullptr, 1,
+                     stop_at_end_of_text_, nullptr);
         position_ = (int)prompt_.size();
         sampled_steps_ = 1;
+        queued_steps_ = 0;
     }
 
-    // encodeStep for step k > 0 (Whisper.cpp:1207-1212), replayed as a graph.
+    // encodeStep for steps k > 0 (Whisper.cpp:1207-1212): `steps` single-token
+    // steps in one launch of the decode kernel, each sampling into the slot
+    // the next one embeds.
     void enqueue_steps(int steps) {
-        for (int i = 0; i < steps; ++i) {
-            if (position_ + 1 > shape_.max_positions) throw ModelError("the window is full");
-            launch_single_step_graph();
-            ++position_;
-            ++sampled_steps_;
-        }
+        if (steps <= 0) return;
+        if (position_ + steps > shape_.max_positions) throw ModelError("the window is full");
+        launch_steps(1, /*sample=*/true, masks_.get<float>() + shape_.vocabulary_size, nullptr, nullptr, nullptr,
+                     steps, stop_at_end_of_text_, nullptr);
+        position_ += steps;
+        queued_steps_ += steps;
     }
 
     void enqueue_transcribe(const float* encoder_rows, int cross_positions, int steps) {
@@ -453,12 +419,22 @@ public:
 
     void read_transcript(uint32_t* tokens, int32_t* counts) {
         CUDA_CHECK(cudaSetDevice(device_));
+        CUDA_CHECK(cudaStreamSynchronize(stream_));
+        check_device_errors();
+        int state[kStateWords];
+        CUDA_CHECK(cudaMemcpy(state, state_.get(), sizeof state, cudaMemcpyDeviceToHost));
+        if (queued_steps_ > 0) {
+            // With the stop enabled the kernel returns once every window has
+            // ended; the steps it ran are the ones sampled.
+            const int ran = state[kStepsDone];
+            sampled_steps_ += ran;
+            position_ -= queued_steps_ - ran;
+            queued_steps_ = 0;
+        }
         const int steps = sampled_steps_;
         const int p = (int)prompt_.size();
         std::vector<uint32_t> ring((size_t)windows_ * ring_stride());
-        CUDA_CHECK(cudaMemcpyAsync(ring.data(), ring_.get(), ring.size() * 4, cudaMemcpyDeviceToHost, stream_));
-        CUDA_CHECK(cudaStreamSynchronize(stream_));
-        check_device_errors();
+        CUDA_CHECK(cudaMemcpy(ring.data(), ring_.get(), ring.size() * 4, cudaMemcpyDeviceToHost));
         for (int b = 0; b < windows_; ++b) {
             int count = 0;
             for (int k = 0; k < steps; ++k) {
@@ -471,27 +447,13 @@ public:
         }
     }
 
-    // Whisper::decodeTranscript (Whisper.cpp:1361-1449).  The host checks for
-    // end-of-text every few steps rather than every step: the steps queued
-    // past a window's end are computed and ignored, as the reference's
-    // in-flight steps are.
+    // Whisper::decodeTranscript (Whisper.cpp:1361-1449): the prompt step,
+    // then every later step in one launch that stops by itself once every
+    // window has sampled end-of-text (with stop_at_end_of_text).
     void transcribe(const float* encoder_rows, int cross_positions, uint32_t* tokens, int32_t* counts) {
         const int limit = step_limit();
         enqueue_start(encoder_rows, cross_positions);
-        if (stop_at_end_of_text_) {
-            if (!pinned_ring_) CUDA_CHECK(cudaMallocHost(&pinned_ring_, (size_t)windows_ * ring_stride() * 4));
-            const int batch = 16;
-            while (sampled_steps_ < limit) {
-                const int n = std::min(batch, limit - sampled_steps_);
-                enqueue_steps(n);
-                CUDA_CHECK(cudaMemcpyAsync(pinned_ring_, ring_.get(), (size_t)windows_ * ring_stride() * 4,
-                                           cudaMemcpyDeviceToHost, stream_));
-                CUDA_CHECK(cudaStreamSynchronize(stream_));
-                if (all_windows_ended(pinned_ring_)) break;
-            }
-        } else {
-            enqueue_steps(limit - 1);
-        }
+        enqueue_steps(limit - 1);
         read_transcript(tokens, counts);
     }
 
@@ -503,54 +465,42 @@ public:
         check_device_errors();
     }
 
-    // Launch-by-launch timing of single-token sampled steps.
+    // Per-op timing of single-token sampled steps: the decode kernel stamps
+    // %globaltimer after each op's grid barrier; one launch per step.
     void time_kernels(int steps, float* ms, int* launches) {
         if (!generation_set_ || !started_) throw LogicError("time_kernels needs a transcription in progress");
         if (position_ + steps > shape_.max_positions) throw ModelError("not enough room left in the window");
         CUDA_CHECK(cudaSetDevice(device_));
-        KernelTimer timer{stream_};
-        for (int i = 0; i < steps; ++i) {
-            StepPlan plan = sampling_plan(1, masks_.get<float>() + shape_.vocabulary_size);
-            record_step(plan, &timer);
-            ++position_;
-        }
-        CUDA_CHECK(cudaStreamSynchronize(stream_));
         std::vector<double> total(WSP_KERNEL_CLASSES, 0.0);
         std::vector<int> count(WSP_KERNEL_CLASSES, 0);
-        for (auto& m : timer.marks) {
-            float t = 0.f;
-            CUDA_CHECK(cudaEventElapsedTime(&t, m.second.first, m.second.second));
-            total[m.first] += t;
-            count[m.first] += 1;
+        std::vector<unsigned long long> stamps;
+        for (int i = 0; i < steps; ++i) {
+            const std::vector<StepOp>& ops = launch_steps(1, true, masks_.get<float>() + shape_.vocabulary_size,
+                                                          nullptr, nullptr, nullptr, 1, false,
+                                                          profile_.get<unsigned long long>());
+            stamps.resize(ops.size() + 1);
+            CUDA_CHECK(cudaMemcpyAsync(stamps.data(), profile_.get(), stamps.size() * 8, cudaMemcpyDeviceToHost,
+                                       stream_));
+            CUDA_CHECK(cudaStreamSynchronize(stream_));
+            for (size_t o = 0; o < ops.size(); ++o) {
+                const int cls = op_class(ops[o].kind);
+                total[cls] += (stamps[o + 1] - stamps[o]) * 1e-6;
+                count[cls] += 1;
+            }
+            ++position_;
         }
+        check_device_errors();
         for (int c = 0; c < WSP_KERNEL_CLASSES; ++c) {
             if (ms) ms[c] = count[c] ? (float)(total[c] / count[c]) : 0.f;
             if (launches) launches[c] = steps ? count[c] / steps : 0;
         }
     }
 
-    int step_launches() const { return 5 + 13 * shape_.layers; }
+    // Kernel launches of this library per transcription: the encoder-row
+    // narrowing, the prompt step, and the launch that runs every later step.
+    int step_launches() const { return 3; }
 
 private:
-    struct StepPlan {
-        int tokens = 1;
-        bool sample_last_only = true;
-        const float* mask = nullptr;
-        float* logits = nullptr;
-        float* hidden = nullptr;
-        uint32_t* row_tokens = nullptr;
-        bool write_ring = true;
-    };
-
-    StepPlan sampling_plan(int tokens, const float* mask) {
-        StepPlan plan;
-        plan.tokens = tokens;
-        plan.sample_last_only = true;
-        plan.mask = mask;
-        plan.write_ring = true;
-        return plan;
-    }
-
     int ring_stride() const { return shape_.max_positions + 1; }
 
     void validate_shape() {
@@ -567,10 +517,12 @@ private:
             throw InvalidArgument("storage must be float16 or bfloat16");
     }
 
+    static size_t round16(size_t n) { return (n + 15) / 16 * 16; }
+
     void allocate_weights() {
         const size_t d = shape_.width, f = shape_.feed_forward_width, L = shape_.layers;
         const size_t kpd = padded(d), kpf = padded(f);
-        token_table_.allocate((size_t)shape_.vocabulary_size * kpd * 2);
+        token_table_.allocate(round16(shape_.vocabulary_size) * kpd * 2);
         position_table_.allocate((size_t)shape_.max_positions * d * 4);
         final_w_.allocate(d * 4);
         final_b_.allocate(d * 4);
@@ -579,14 +531,14 @@ private:
         for (size_t i = 0; i < L; ++i) {
             LayerBuffers& l = layers_[i];
             l.ln1_w.allocate(d * 4); l.ln1_b.allocate(d * 4);
-            l.qkv_w.allocate(3 * d * kpd * 2); l.qkv_b.allocate(3 * d * 4);
-            l.o_w.allocate(d * kpd * 2); l.o_b.allocate(d * 4);
+            l.qkv_w.allocate(round16(3 * d) * kpd * 2); l.qkv_b.allocate(3 * d * 4);
+            l.o_w.allocate(round16(d) * kpd * 2); l.o_b.allocate(d * 4);
             l.ln2_w.allocate(d * 4); l.ln2_b.allocate(d * 4);
-            l.qc_w.allocate(d * kpd * 2); l.qc_b.allocate(d * 4); l.vc_b.allocate(d * 4);
-            l.oc_w.allocate(d * kpd * 2); l.oc_b.allocate(d * 4);
+            l.qc_w.allocate(round16(d) * kpd * 2); l.qc_b.allocate(d * 4); l.vc_b.allocate(d * 4);
+            l.oc_w.allocate(round16(d) * kpd * 2); l.oc_b.allocate(d * 4);
             l.ln3_w.allocate(d * 4); l.ln3_b.allocate(d * 4);
-            l.fc1_w.allocate(f * kpd * 2); l.fc1_b.allocate(f * 4);
-            l.fc2_w.allocate(d * kpf * 2); l.fc2_b.allocate(d * 4);
+            l.fc1_w.allocate(round16(f) * kpd * 2); l.fc1_b.allocate(f * 4);
+            l.fc2_w.allocate(round16(d) * kpf * 2); l.fc2_b.allocate(d * 4);
         }
         present_.assign(4 + 24 * L, false);
     }
@@ -601,288 +553,240 @@ private:
         encoder16_.allocate(B * X * d * 2);
         ring_.allocate(B * ring_stride() * 4);
         ring_prompt_.allocate(B * ring_stride() * 4);
-        state_.allocate(2 * sizeof(int));
+        state_.allocate(kStateWords * sizeof(int));
+        barrier_.allocate(64);
+        ended_.allocate((size_t)windows_);
+        profile_.allocate((size_t)(8 * shape_.layers + 8) * sizeof(unsigned long long));
         masks_.allocate(2 * (size_t)shape_.vocabulary_size * 4);
-        self_splits_ = (shape_.max_positions + kSelfChunk - 1) / kSelfChunk;
     }
 
-    static constexpr int kSelfChunk = 64;
-
-    int cross_splits(int cross_rows) const {
-        const int pairs = windows_ * shape_.heads;
-        int s = (2 * sm_count_ + pairs - 1) / pairs;
-        s = std::max(s, (cross_rows + 2047) / 2048);
-        s = std::min(s, std::max(1, (cross_rows + 31) / 32));
-        return std::max(1, s);
+    // Most cross-attention splits a step can use: enough items for the grid
+    // at one row, never chunks under 32 keys or over 2048.
+    int max_cross_splits() const {
+        const int X = shape_.cross_positions;
+        int s = (kMaxBlocksPerSm * sm_count_ + shape_.heads - 1) / shape_.heads;
+        s = std::min(s, std::max(1, (X + 31) / 32));
+        return std::max({1, s, (X + kMaxCrossChunk - 1) / kMaxCrossChunk});
     }
 
     void ensure_row_capacity(int tokens) {
         if (tokens <= token_capacity_) return;
-        drop_graph();
         token_capacity_ = std::max(tokens, token_capacity_);
         const size_t R = (size_t)windows_ * token_capacity_;
         const size_t d = shape_.width, f = shape_.feed_forward_width, H = shape_.heads, D = d / H;
-        const size_t splits = std::max(self_splits_, cross_splits(shape_.cross_positions));
         hidden_.allocate(R * d * 4);
-        normalised_.allocate(R * padded(d) * 2);
         queries_.allocate(R * d * 4);
         attended_.allocate(R * padded(d) * 2);
         feed_forward_.allocate(R * padded(f) * 2);
-        partial_.allocate(R * H * splits * (D + 2) * 4);
-        const size_t tiles = gemm_column_tiles(shape_.vocabulary_size);
-        candidate_values_.allocate(R * tiles * 4);
-        candidate_indices_.allocate(R * tiles * 4);
+        partial_.allocate(R * H * max_cross_splits() * (D + 2) * 4);
+        const size_t grid = (size_t)kMaxBlocksPerSm * sm_count_;
+        candidate_values_.allocate(R * grid * 4);
+        candidate_indices_.allocate(R * grid * 4);
         row_tokens_.allocate(R * 4);
-        final_rows_hidden_.allocate(R * d * 4);
+        counters_.allocate((R * H + 1) * sizeof(unsigned));
     }
 
     void ensure_staging(DeviceBuffer& buffer, size_t bytes) {
         if (buffer.bytes() < bytes) buffer.allocate(bytes);
     }
 
-    void drop_graph() {
-        if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
-        if (graph_) cudaGraphDestroy(graph_);
-        graph_exec_ = nullptr;
-        graph_ = nullptr;
-    }
-
-    void launch_single_step_graph() {
-        if (!graph_exec_) {
-            CUDA_CHECK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
-            try {
-                StepPlan plan = sampling_plan(1, masks_.get<float>() + shape_.vocabulary_size);
-                record_step(plan, nullptr);
-            } catch (...) {
-                cudaGraph_t broken = nullptr;
-                cudaStreamEndCapture(stream_, &broken);
-                if (broken) cudaGraphDestroy(broken);
-                throw;
-            }
-            CUDA_CHECK(cudaStreamEndCapture(stream_, &graph_));
-            CUDA_CHECK(cudaGraphInstantiate(&graph_exec_, graph_, 0));
-        }
-        CUDA_CHECK(cudaGraphLaunch(graph_exec_, stream_));
-    }
-
-    bool all_windows_ended(const uint32_t* ring) const {
-        const int p = (int)prompt_.size();
-        for (int b = 0; b < windows_; ++b) {
-            bool ended = false;
-            for (int k = 0; k < sampled_steps_ && !ended; ++k)
-                ended = ring[(size_t)b * ring_stride() + p + k] == end_of_text_;
-            if (!ended) return false;
-        }
-        return true;
-    }
-
     void check_device_errors() {
-        int flags[2] = {0, 0};
-        CUDA_CHECK(cudaMemcpy(flags, state_.get(), sizeof flags, cudaMemcpyDeviceToHost));
-        if (flags[1] & 1) {
-            CUDA_CHECK(cudaMemset(state_.get<int>() + 1, 0, sizeof(int)));
+        int state[kStateWords];
+        CUDA_CHECK(cudaMemcpy(state, state_.get(), sizeof state, cudaMemcpyDeviceToHost));
+        if (state[kError] != 0) {
+            CUDA_CHECK(cudaMemset(state_.get<int>() + kError, 0, sizeof(int)));
+            if (state[kError] & kErrBarrierTimeout)
+                throw CudaFailure("the decode kernel gave up waiting at a grid barrier", false);
             throw ModelError("a sampled or supplied token id fell outside the vocabulary");
         }
     }
 
-    // The step: recordDecoderStep (Decoder.cpp:151-177) with decoderLayer
-    // (Decoder.cpp:73-115), lowered onto fused kernels.
-    void record_step(const StepPlan& plan, KernelTimer* timer) {
-        const int T = plan.tokens;
-        const int R = windows_ * T;
-        const int d = shape_.width, f = shape_.feed_forward_width, H = shape_.heads, D = d / H;
-        const int kpd = padded(d), kpf = padded(f);
-        const int L = shape_.layers;
-        int* position = state_.get<int>();
-        int* error = state_.get<int>() + 1;
-        auto mark = [&](int cls) { if (timer) timer->begin(cls); };
-        auto done = [&]() { ++launches_; if (timer) timer->end(); };
-
-        EmbedArgs e{};
-        e.ring = ring_.get<uint32_t>();
-        e.ring_stride = ring_stride();
-        e.position = position;
-        e.tokens = T;
-        e.rows = R;
-        e.width = d;
-        e.vocabulary = shape_.vocabulary_size;
-        e.token_table = token_table_.get();
-        e.token_stride = kpd;
-        e.position_table = position_table_.get<float>();
-        e.hidden = hidden_.get<float>();
-        e.error = error;
-        mark(WSP_KERNEL_EMBED);
-        launch_embed(storage_, e, stream_);
-        done();
-
-        auto layer_norm = [&](const DeviceBuffer& w, const DeviceBuffer& b) {
-            LayerNormArgs a{};
-            a.input = hidden_.get<float>();
-            a.rows = R;
-            a.width = d;
-            a.row_step = 1;
-            a.row_offset = 0;
-            a.gamma = w.get<float>();
-            a.beta = b.get<float>();
-            a.output = normalised_.get();
-            a.ld_output = kpd;
-            mark(WSP_KERNEL_LAYER_NORM);
-            launch_layer_norm(storage_, a, stream_);
-            done();
-        };
-        auto product = [&](Epilogue epi, const DeviceBuffer& w, int n, const void* input, int kp,
-                           const float* bias, GemmArgs g) {
-            g.weight = w.get();
-            g.input = input;
-            g.n = n;
-            g.rows = R;
-            g.kp = kp;
-            g.bias = bias;
-            mark(WSP_KERNEL_PROJECTION);
-            launch_gemm(storage_, epi, g, sm_count_, stream_);
-            done();
-        };
-        auto attend = [&](bool cross, int layer) {
-            AttentionArgs a{};
-            a.queries = queries_.get<float>();
-            a.ld_queries = d;
-            a.rows = R;
-            a.tokens = T;
-            a.heads = H;
-            a.head_width = D;
-            a.position = position;
-            a.scale = 1.f / std::sqrt((float)D);
-            a.partial = partial_.get<float>();
-            const size_t bytes = storage_ == Storage::f16 ? 2 : 2;
-            if (cross) {
-                const size_t n = (size_t)2 * d * L;
-                const char* base = cross_kv_.get<char>() + (size_t)layer * 2 * d * bytes;
-                a.keys = base;
-                a.values = base + (size_t)d * bytes;
-                a.key_stride = (long long)n;
-                a.window_stride = (long long)shape_.cross_positions * n;
-                a.causal = 0;
-                a.key_count = active_cross_;
-                a.splits = cross_splits(active_cross_);
-                a.chunk = (active_cross_ + a.splits - 1) / a.splits;
-            } else {
-                const size_t per_layer = (size_t)windows_ * shape_.max_positions * d * bytes;
-                a.keys = self_keys_.get<char>() + layer * per_layer;
-                a.values = self_values_.get<char>() + layer * per_layer;
-                a.key_stride = d;
-                a.window_stride = (long long)shape_.max_positions * d;
-                a.causal = 1;
-                a.splits = self_splits_;
-                a.chunk = kSelfChunk;
-            }
-            mark(cross ? WSP_KERNEL_CROSS_ATTENTION : WSP_KERNEL_SELF_ATTENTION);
-            launch_attention_partial(storage_, a, stream_);
-            done();
-            CombineArgs c{};
-            c.partial = partial_.get<float>();
-            c.rows = R;
-            c.heads = H;
-            c.head_width = D;
-            c.splits = a.splits;
-            c.bias = cross ? layers_[layer].vc_b.get<float>() : nullptr;
-            c.output = attended_.get();
-            c.ld_output = kpd;
-            mark(WSP_KERNEL_ATTENTION_COMBINE);
-            launch_attention_combine(storage_, c, stream_);
-            done();
-        };
-
-        const size_t self_layer_elements = (size_t)windows_ * shape_.max_positions * d;
-        for (int l = 0; l < L; ++l) {
-            LayerBuffers& W = layers_[l];
-            // h += out_proj(self_attention(self_attn_layer_norm(h)))  (Decoder.cpp:80-91)
-            layer_norm(W.ln1_w, W.ln1_b);
-            GemmArgs qkv{};
-            qkv.out = queries_.get<float>();
-            qkv.ld_out = d;
-            qkv.width = d;
-            qkv.self_keys = self_keys_.get<char>() + l * self_layer_elements * 2;
-            qkv.self_values = self_values_.get<char>() + l * self_layer_elements * 2;
-            qkv.max_positions = shape_.max_positions;
-            qkv.tokens = T;
-            qkv.position = position;
-            product(Epilogue::qkv, W.qkv_w, 3 * d, normalised_.get(), kpd, W.qkv_b.get<float>(), qkv);
-            attend(false, l);
-            GemmArgs residual{};
-            residual.out = hidden_.get<float>();
-            residual.ld_out = d;
-            product(Epilogue::residual, W.o_w, d, attended_.get(), kpd, W.o_b.get<float>(), residual);
-
-            // h += out_proj(cross_attention(encoder_attn_layer_norm(h)))  (Decoder.cpp:93-104)
-            layer_norm(W.ln2_w, W.ln2_b);
-            GemmArgs q{};
-            q.out = queries_.get<float>();
-            q.ld_out = d;
-            product(Epilogue::store, W.qc_w, d, normalised_.get(), kpd, W.qc_b.get<float>(), q);
-            attend(true, l);
-            product(Epilogue::residual, W.oc_w, d, attended_.get(), kpd, W.oc_b.get<float>(), residual);
-
-            // h += fc2(gelu(fc1(final_layer_norm(h))))  (Decoder.cpp:106-114)
-            layer_norm(W.ln3_w, W.ln3_b);
-            GemmArgs up{};
-            up.out16 = feed_forward_.get();
-            up.ld_out16 = kpf;
-            product(Epilogue::gelu, W.fc1_w, f, normalised_.get(), kpd, W.fc1_b.get<float>(), up);
-            product(Epilogue::residual, W.fc2_w, d, feed_forward_.get(), kpf, W.fc2_b.get<float>(), residual);
+    static int op_class(int kind) {
+        switch (kind) {
+        case kOpEmbed: return WSP_KERNEL_EMBED;
+        case kOpProduct: return WSP_KERNEL_PROJECTION;
+        case kOpSelfAttention: return WSP_KERNEL_SELF_ATTENTION;
+        case kOpCrossAttention: return WSP_KERNEL_CROSS_ATTENTION;
+        case kOpLogits: return WSP_KERNEL_LOGITS_ARGMAX;
         }
+        return WSP_KERNEL_OTHER;
+    }
 
-        // Final layer norm and the tied logits (Decoder.cpp:170-176); when
-        // sampling, only each window's last row is normalised and projected
-        // (Whisper::encodeSampling reads the last row, Whisper.cpp:1169-1184).
-        const int out_rows = plan.sample_last_only ? windows_ : R;
-        LayerNormArgs fl{};
-        fl.input = hidden_.get<float>();
-        fl.rows = out_rows;
-        fl.width = d;
-        fl.row_step = plan.sample_last_only ? T : 1;
-        fl.row_offset = plan.sample_last_only ? T - 1 : 0;
-        fl.gamma = final_w_.get<float>();
-        fl.beta = final_b_.get<float>();
-        fl.output = normalised_.get();
-        fl.ld_output = kpd;
-        fl.hidden_copy = plan.hidden;
-        mark(WSP_KERNEL_LAYER_NORM);
-        launch_layer_norm(storage_, fl, stream_);
-        done();
+    static constexpr int kMaxCrossChunk = 2048;
+    static constexpr int kMaxBlocksPerSm = 2;
 
-        GemmArgs lg{};
-        lg.weight = token_table_.get();
-        lg.input = normalised_.get();
-        lg.n = shape_.vocabulary_size;
-        lg.rows = out_rows;
-        lg.kp = kpd;
-        lg.logits = plan.logits;
-        lg.ld_logits = shape_.vocabulary_size;
-        lg.mask = plan.mask;
-        lg.candidate_values = candidate_values_.get<float>();
-        lg.candidate_indices = candidate_indices_.get<uint32_t>();
-        mark(WSP_KERNEL_LOGITS_ARGMAX);
-        launch_gemm(storage_, Epilogue::logits, lg, sm_count_, stream_);
-        done();
+    // The step: recordDecoderStep (Decoder.cpp:151-177) with decoderLayer
+    // (Decoder.cpp:73-115), lowered onto the fused ops of step.cuh.
+    std::vector<StepOp> build_ops(int R, int grid, int* max_chunk) const {
+        const int d = shape_.width, f = shape_.feed_forward_width, H = shape_.heads;
+        const int kpd = padded(d), kpf = padded(f);
+        const size_t elem = 2;
+        const size_t self_layer = (size_t)windows_ * shape_.max_positions * d * elem;
+        const size_t n_cross = (size_t)2 * d * shape_.layers;
+        std::vector<StepOp> ops;
+        StepOp e{};
+        e.kind = kOpEmbed;
+        ops.push_back(e);
+        int splits = (grid + R * H - 1) / (R * H);
+        splits = std::max(splits, (active_cross_ + kMaxCrossChunk - 1) / kMaxCrossChunk);
+        splits = std::min(splits, std::max(1, (active_cross_ + 31) / 32));
+        splits = std::max(1, splits);
+        const int chunk = (active_cross_ + splits - 1) / splits;
+        *max_chunk = chunk;
+        for (int l = 0; l < shape_.layers; ++l) {
+            const LayerBuffers& W = layers_[l];
+            auto product = [&](int epilogue, const DeviceBuffer& w, int n, int kp, const DeviceBuffer& bias) {
+                StepOp o{};
+                o.kind = kOpProduct;
+                o.epilogue = epilogue;
+                o.weight = w.get();
+                o.n = n;
+                o.kp = kp;
+                o.bias = bias.get<float>();
+                return o;
+            };
+            // h += out_proj(self_attention(self_attn_layer_norm(h)))  (Decoder.cpp:80-91)
+            StepOp qkv = product(kEpQkv, W.qkv_w, 3 * d, kpd, W.qkv_b);
+            qkv.gamma = W.ln1_w.get<float>();
+            qkv.beta = W.ln1_b.get<float>();
+            qkv.out = queries_.get();
+            qkv.ld_out = d;
+            qkv.self_keys = self_keys_.get<char>() + l * self_layer;
+            qkv.self_values = self_values_.get<char>() + l * self_layer;
+            ops.push_back(qkv);
+            StepOp self{};
+            self.kind = kOpSelfAttention;
+            self.keys = qkv.self_keys;
+            self.values = qkv.self_values;
+            self.key_stride = d;
+            self.window_stride = (long long)shape_.max_positions * d;
+            ops.push_back(self);
+            StepOp out = product(kEpResidual, W.o_w, d, kpd, W.o_b);
+            out.input16 = attended_.get();
+            out.ld_input = kpd;
+            out.out = hidden_.get();
+            out.ld_out = d;
+            ops.push_back(out);
+            // h += out_proj(cross_attention(encoder_attn_layer_norm(h)))  (Decoder.cpp:93-104)
+            StepOp cq = product(kEpStore, W.qc_w, d, kpd, W.qc_b);
+            cq.gamma = W.ln2_w.get<float>();
+            cq.beta = W.ln2_b.get<float>();
+            cq.out = queries_.get();
+            cq.ld_out = d;
+            ops.push_back(cq);
+            StepOp cross{};
+            cross.kind = kOpCrossAttention;
+            cross.keys = cross_kv_.get<char>() + (size_t)l * 2 * d * elem;
+            cross.values = cross_kv_.get<char>() + ((size_t)l * 2 * d + d) * elem;
+            cross.key_stride = (long long)n_cross;
+            cross.window_stride = (long long)shape_.cross_positions * n_cross;
+            cross.key_count = active_cross_;
+            cross.splits = splits;
+            cross.chunk = chunk;
+            cross.value_bias = W.vc_b.get<float>();
+            ops.push_back(cross);
+            StepOp cout = product(kEpResidual, W.oc_w, d, kpd, W.oc_b);
+            cout.input16 = attended_.get();
+            cout.ld_input = kpd;
+            cout.out = hidden_.get();
+            cout.ld_out = d;
+            ops.push_back(cout);
+            // h += fc2(gelu(fc1(final_layer_norm(h))))  (Decoder.cpp:106-114)
+            StepOp up = product(kEpGelu, W.fc1_w, f, kpd, W.fc1_b);
+            up.gamma = W.ln3_w.get<float>();
+            up.beta = W.ln3_b.get<float>();
+            up.out = feed_forward_.get();
+            up.ld_out = kpf;
+            ops.push_back(up);
+            StepOp down = product(kEpResidual, W.fc2_w, d, kpf, W.fc2_b);
+            down.input16 = feed_forward_.get();
+            down.ld_input = kpf;
+            down.out = hidden_.get();
+            down.ld_out = d;
+            ops.push_back(down);
+        }
+        // Final layer norm and the tied logits with the masked argmax
+        // (Decoder.cpp:170-176, Whisper::encodeSampling Whisper.cpp:1169-1184).
+        StepOp logits{};
+        logits.kind = kOpLogits;
+        ops.push_back(logits);
+        return ops;
+    }
 
-        ArgmaxFinalArgs af{};
-        af.candidate_values = candidate_values_.get<float>();
-        af.candidate_indices = candidate_indices_.get<uint32_t>();
-        af.candidates = gemm_column_tiles(shape_.vocabulary_size);
-        af.rows = out_rows;
-        af.rows_per_window = plan.sample_last_only ? 1 : T;
-        af.step_tokens = T;
-        af.row_tokens = plan.row_tokens;
-        af.ring = plan.write_ring ? ring_.get<uint32_t>() : nullptr;
-        af.ring_stride = ring_stride();
-        af.position = position;
-        mark(WSP_KERNEL_ARGMAX_FINAL);
-        launch_argmax_final(af, stream_);
-        done();
+    // One launch of the decode kernel: `steps` steps of T tokens per window.
+    // sample: only each window's last row is normalised, projected and
+    // sampled into the ring; otherwise every row's logits/hidden/argmax.
+    const std::vector<StepOp>& launch_steps(int T, bool sample, const float* mask, float* logits, float* hidden,
+                                            uint32_t* row_tokens, int steps, bool stop,
+                                            unsigned long long* profile) {
+        const int R = windows_ * T;
+        StepParams p{};
+        p.windows = windows_;
+        p.tokens = T;
+        p.rows = R;
+        p.width = shape_.width;
+        p.heads = shape_.heads;
+        p.head_width = shape_.width / shape_.heads;
+        p.ffn = shape_.feed_forward_width;
+        p.vocabulary = shape_.vocabulary_size;
+        p.kpd = padded(shape_.width);
+        p.max_positions = shape_.max_positions;
+        p.ring_stride = ring_stride();
+        p.scale = 1.f / std::sqrt((float)p.head_width);
+        p.out_rows = sample ? windows_ : R;
+        p.row_step = sample ? T : 1;
+        p.row_offset = sample ? T - 1 : 0;
+        p.ring = ring_.get<uint32_t>();
+        p.state = state_.get<int>();
+        p.token_table = token_table_.get();
+        p.position_table = position_table_.get<float>();
+        p.final_gamma = final_w_.get<float>();
+        p.final_beta = final_b_.get<float>();
+        p.h = hidden_.get<float>();
+        p.q = queries_.get<float>();
+        p.attn16 = attended_.get();
+        p.ffn16 = feed_forward_.get();
+        p.partial = partial_.get<float>();
+        p.combine_counters = counters_.get<unsigned>();
+        p.logits_counter = counters_.get<unsigned>() + (size_t)windows_ * token_capacity_ * shape_.heads;
+        p.candidate_values = candidate_values_.get<float>();
+        p.candidate_indices = candidate_indices_.get<uint32_t>();
+        p.barrier = barrier_.get<unsigned>();
+        p.profile = profile;
+        p.mask = mask;
+        p.logits_out = logits;
+        p.hidden_out = hidden;
+        p.row_tokens = row_tokens;
+        p.ended = ended_.get<uint8_t>();
+        p.write_ring = sample ? 1 : 0;
+        p.steps = steps;
+        p.stop_token = end_of_text_;
+        p.stop_enabled = stop ? 1 : 0;
 
-        mark(WSP_KERNEL_OTHER);
-        launch_advance_position(position, T, stream_);
-        done();
+        const bool half = storage_ == Storage::f16;
+        const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk);
+        if (blocks <= 0) throw CudaFailure("the decode kernel does not fit on an SM", false);
+        const int grid = sm_count_ * std::min(blocks, kMaxBlocksPerSm);
+        int max_chunk = 0;
+        std::vector<StepOp>& ops = sample ? (T == 1 ? ops_step_ : ops_prompt_) : ops_teacher_;
+        DeviceBuffer& ops_dev = sample ? (T == 1 ? ops_step_dev_ : ops_prompt_dev_) : ops_teacher_dev_;
+        ops = build_ops(R, grid, &max_chunk);
+        if (ops_dev.bytes() < ops.size() * sizeof(StepOp)) ops_dev.allocate(ops.size() * sizeof(StepOp));
+        CUDA_CHECK(cudaMemcpyAsync(ops_dev.get(), ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice,
+                                   stream_));
+        p.ops = ops_dev.get<StepOp>();
+        p.n_ops = (int)ops.size();
+        // The abort and steps-done words; the all-ended flag survives from
+        // the prompt step to the steps after it.
+        CUDA_CHECK(cudaMemsetAsync(state_.get<int>() + kAbort, 0, 2 * sizeof(int), stream_));
+        CUDA_CHECK(cudaMemsetAsync(barrier_.get(), 0, barrier_.bytes(), stream_));
+        try {
+            launch_decode(half, p, kMaxCrossChunk, grid, stream_);
+        } catch (const std::runtime_error& e) {
+            throw CudaFailure(e.what(), false);
+        }
+        ++launches_;
+        return ops;
     }
 
     // ------------------------------------------------------ upload helpers
@@ -926,6 +830,25 @@ private:
         CUDA_CHECK(cudaMemcpy(dst.get<uint16_t>() + row_offset * ld, v.data(), v.size() * 2, cudaMemcpyHostToDevice));
     }
 
+    // rows x cols of a row-major [rows, cols] tensor into rows
+    // [row_offset, row_offset+rows) of a fragment-packed [*, kp] matrix
+    // (packed_offset, step.cuh), narrowed to the storage type.  The tiles
+    // touched are read back first, since a tile may hold rows of two tensors.
+    void upload_packed(DeviceBuffer& dst, int row_offset, int rows, int cols, int kp, wsp_dtype dtype,
+                       const void* data) {
+        const int chunks = kp / 32;
+        const int t0 = row_offset / 16, t1 = (row_offset + rows - 1) / 16;
+        const size_t tile_elements = (size_t)16 * kp;
+        std::vector<uint16_t> v((size_t)(t1 - t0 + 1) * tile_elements);
+        uint16_t* base = dst.get<uint16_t>() + (size_t)t0 * tile_elements;
+        CUDA_CHECK(cudaMemcpy(v.data(), base, v.size() * 2, cudaMemcpyDeviceToHost));
+        for (int r = 0; r < rows; ++r)
+            for (int c = 0; c < cols; ++c)
+                v[packed_offset(row_offset + r, c, chunks) - (size_t)t0 * tile_elements] =
+                    narrow(widen(data, dtype, (size_t)r * cols + c), storage_);
+        CUDA_CHECK(cudaMemcpy(base, v.data(), v.size() * 2, cudaMemcpyHostToDevice));
+    }
+
     static void copy_floats(float* out, const float* in, size_t n) {
         if (is_device_pointer(in)) CUDA_CHECK(cudaMemcpy(out, in, n * 4, cudaMemcpyDeviceToHost));
         else std::memcpy(out, in, n * 4);
@@ -945,13 +868,14 @@ private:
 
     DeviceBuffer self_keys_, self_values_, cross_kv_, encoder_staging_, encoder16_;
     DeviceBuffer ring_, ring_prompt_, state_, masks_;
-    DeviceBuffer hidden_, normalised_, queries_, attended_, feed_forward_, partial_;
-    DeviceBuffer candidate_values_, candidate_indices_, row_tokens_, final_rows_hidden_;
+    DeviceBuffer hidden_, queries_, attended_, feed_forward_, partial_;
+    DeviceBuffer candidate_values_, candidate_indices_, row_tokens_, counters_;
+    DeviceBuffer barrier_, ended_, profile_;
     DeviceBuffer logits_staging_, hidden_staging_;
-    uint32_t* pinned_ring_ = nullptr;
+    DeviceBuffer ops_prompt_dev_, ops_step_dev_, ops_teacher_dev_;
+    std::vector<StepOp> ops_prompt_, ops_step_, ops_teacher_;
 
     int token_capacity_ = 0;
-    int self_splits_ = 1;
     int active_cross_ = 0;
     int position_ = 0;
     bool started_ = false;
@@ -963,9 +887,7 @@ private:
     bool stop_at_end_of_text_ = true;
     bool generation_set_ = false;
     int sampled_steps_ = 0;
-
-    cudaGraph_t graph_ = nullptr;
-    cudaGraphExec_t graph_exec_ = nullptr;
+    int queued_steps_ = 0;
 };
 
 template <typename F>

@@ -1,0 +1,113 @@
+// The decoder step as a list of fused ops, run by one persistent kernel.
+//
+// A step of T tokens for each of B windows works on R = B*T rows; row
+// r = b*T + t stands at absolute position position+t of window b.  The host
+// lowers recordDecoderStep (Lib/WhisperEACP/Decoder/Decoder.cpp:151-177) and
+// decoderLayer (:73-115) into StepOps:
+//
+//   embed                       h = token_table[id] + position_table[p]
+//   per layer
+//     product  LN1 -> q,k,v     (k, v appended to the self cache)
+//     self attention            causal over keys 0..position+t
+//     product  out_proj + h     (residual)
+//     product  LN2 -> cross q
+//     cross attention           split over the encoder rows, the splits of a
+//                               (row, head) joined by the last to finish
+//     product  out_proj + h
+//     product  LN3 -> fc1, GELU
+//     product  fc2 + h
+//   logits                      LN, h . token_table^T, masked argmax candidates;
+//                               the last CTA to finish folds them, writes the
+//                               sampled ids and advances the position
+//
+// with a grid-wide barrier after each op.  The decode kernel runs the list
+// once per step for as many steps as it is given, so a whole greedy decode is
+// one launch.
+#pragma once
+
+#include "common.cuh"
+
+namespace wsp {
+
+enum OpKind : int { kOpEmbed = 0, kOpProduct = 1, kOpSelfAttention = 2, kOpCrossAttention = 3, kOpLogits = 4 };
+enum EpilogueKind : int { kEpQkv = 0, kEpStore = 1, kEpResidual = 2, kEpGelu = 3 };
+
+// state words (int): position, error bits, abort, steps done, all windows ended
+enum StateWord : int { kPosition = 0, kError = 1, kAbort = 2, kStepsDone = 3, kAllEnded = 4, kStateWords = 8 };
+enum ErrorBit : int { kErrToken = 1, kErrBarrierTimeout = 2 };
+
+// Weight matrices are stored fragment-packed: the 16-row tiles of an [n, kp]
+// matrix one after another, each as kp/32 chunks of 1 KB, and inside a chunk
+// lane l = 4*(row%8) + (k%32)/8 of an m16n8k16 A fragment owns 32 bytes --
+// rows row%8 then row%8 + 8, eight k each.  A tile is one contiguous block a
+// bulk copy moves whole, and a warp reads a chunk as 32 consecutive 32-byte
+// pieces, conflict-free.
+__host__ __device__ inline size_t packed_offset(int n, int k, int chunks) {
+    const int tile = n >> 4, row = n & 15, chunk = k >> 5, kk = k & 31;
+    const int lane = (row & 7) * 4 + (kk >> 3);
+    return (((size_t)tile * chunks + chunk) * 32 + lane) * 16 + (row >> 3) * 8 + (kk & 7);
+}
+
+struct StepOp {
+    int kind;
+    int epilogue;
+    // products
+    const void* weight;     // 16-bit fragment-packed [n, kp]
+    int n, kp;
+    const float* bias;      // [n] or null
+    const float* gamma;     // non-null: the input is LayerNorm(h) with this gain ...
+    const float* beta;      // ... and offset
+    const void* input16;    // gamma == null: 16-bit input rows [R, ld_input]
+    int ld_input;
+    void* out;              // fp32 [R, ld_out] (q, residual) or 16-bit (gelu)
+    int ld_out;
+    void* self_keys;        // qkv: this layer's caches [B][max_positions][d]
+    void* self_values;
+    // attention
+    const void* keys;       // 16-bit: key j of window b, head h at
+    const void* values;     //   base + b*window_stride + j*key_stride + h*D
+    long long key_stride;
+    long long window_stride;
+    int key_count;          // cross: encoder rows attended
+    int chunk, splits;      // cross: keys per item, items per (row, head)
+    const float* value_bias;  // cross: v_proj bias, added after normalising
+};
+
+struct StepParams {
+    int windows, tokens, rows;          // B, T, R
+    int width, heads, head_width, ffn, vocabulary, kpd;
+    int max_positions, ring_stride;
+    float scale;                        // 1/sqrt(D), on the scores (DecoderShape.cpp:19-26)
+    int out_rows, row_step, row_offset; // logits rows: row i reads h row i*row_step + row_offset
+
+    uint32_t* ring;                     // [B][ring_stride] token slots
+    int* state;                         // StateWord
+    const void* token_table;            // 16-bit fragment-packed [V, kpd]
+    const float* position_table;        // fp32 [max_positions, d]
+    const float* final_gamma;
+    const float* final_beta;
+    float* h;                           // fp32 [R, d]
+    float* q;                           // fp32 [R, d]
+    void* attn16;                       // 16-bit [R, kpd]
+    void* ffn16;                        // 16-bit [R, kpf]
+    float* partial;                     // cross partials [R][H][S][D+2]
+    unsigned* combine_counters;         // [R*H]
+    unsigned* logits_counter;           // [1]
+    float* candidate_values;            // [out_rows][gridDim]
+    uint32_t* candidate_indices;
+    unsigned* barrier;                  // [0] arrivals since the launch began
+    unsigned long long* profile;        // optional [n_ops+1] globaltimer stamps of step 0
+    const float* mask;                  // logits mask (nonzero = suppressed) or null
+    float* logits_out;                  // optional fp32 [out_rows, V]
+    float* hidden_out;                  // optional fp32 [out_rows, d]
+    uint32_t* row_tokens;               // optional [out_rows] greedy ids
+    uint8_t* ended;                     // [B] window produced the stop token
+    int write_ring;
+    int steps;
+    uint32_t stop_token;
+    int stop_enabled;
+    const StepOp* ops;
+    int n_ops;
+};
+
+}  // namespace wsp

@@ -1,0 +1,15 @@
+// Host entry points of the persistent decode kernel (step.cu).
+#pragma once
+
+#include "step.cuh"
+
+namespace wsp {
+
+// CTAs of the decode kernel one SM holds for these parameters (0: none fit).
+int decode_blocks_per_sm(bool half, const StepParams& p, int max_chunk);
+
+// One cooperative launch running p.steps steps of p.ops; max_chunk bounds the
+// keys a cross-attention item holds in shared memory.
+void launch_decode(bool half, const StepParams& p, int max_chunk, int grid, cudaStream_t stream);
+
+}  // namespace wsp
