@@ -192,7 +192,13 @@ enum {
 };
 int wsp_decoder_time_kernels(wsp_decoder* decoder, int steps, float* ms, int* launches);
 
-/* Launches of this library's kernels per single-token step (graph nodes). */
+/*
+ * Mean cost of one grid-wide barrier of the persistent decode kernel, in
+ * microseconds: one launch running `count` empty ops.
+ */
+int wsp_decoder_time_barriers(wsp_decoder* decoder, int count, float* microseconds);
+
+/* Kernel launches of this library per transcription (wsp_decoder_transcribe). */
 int wsp_decoder_step_launches(const wsp_decoder* decoder, int* launches);
 
 /*

@@ -23,33 +23,20 @@ namespace {
 
 // ------------------------------------------------------------ memory access
 
-__device__ __forceinline__ uint4 ld_cg4(const void* p) {
-    uint4 v;
-    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-__device__ __forceinline__ float ld_cg(const float* p) {
-    float v;
-    asm volatile("ld.global.cg.f32 %0, [%1];\n" : "=f"(v) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint32_t ld_cg(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.global.cg.u32 %0, [%1];\n" : "=r"(v) : "l"(p));
-    return v;
-}
+// Data another CTA wrote inside the launch is read through L2 (ld.global.cg:
+// never a stale L1 line); the grid barrier orders it.  Weights, biases and
+// the cross caches are read-only for the whole launch (ld.global.nc).  The
+// compiler's own load builtins keep the loads free to be batched.
+__device__ __forceinline__ uint4 ld_cg4(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ uint32_t ld_cg(const uint32_t* p) { return __ldcg(reinterpret_cast<const unsigned int*>(p)); }
 __device__ __forceinline__ unsigned short ld_cg_u16(const void* p) {
-    unsigned short v;
-    asm volatile("ld.global.cg.u16 %0, [%1];\n" : "=h"(v) : "l"(p));
-    return v;
+    return __ldcg(reinterpret_cast<const unsigned short*>(p));
 }
 __device__ __forceinline__ unsigned short ld_nc_u16(const void* p) {
-    unsigned short v;
-    asm volatile("ld.global.nc.u16 %0, [%1];\n" : "=h"(v) : "l"(p));
-    return v;
+    return __ldg(reinterpret_cast<const unsigned short*>(p));
 }
+__device__ __forceinline__ uint4 ld_nc4(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
@@ -101,77 +88,163 @@ __device__ bool grid_barrier(unsigned* count, unsigned& epoch, int* state) {
 
 // Weight tiles stream through a ring of shared-memory stages, each filled by
 // one cp.async.bulk copy that completes an mbarrier.  The CTA's sequence of
-// weight units -- (op, tile, k-block) over the products and the logits of
-// every step, in the order the ops consume them -- is fixed, so thread 0
+// weight units -- over the ops of every step, the items the CTA owns, their
+// weight regions, and the units of each region -- is fixed, so thread 0
 // issues ahead as far as the ring allows: the next op's first tiles are in
 // flight while this op (an attention, say) and the grid barrier run.
-constexpr int kUnitChunks = 32;                  // 1024 k of a 16-row tile
-constexpr int kUnitBytes = kUnitChunks * 1024;   // 32 KB
 
 __device__ __forceinline__ uint32_t smem_address(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
 struct Cursor {
-    int step, op, item, block;
+    int step, op, item, region, unit;
 };
 
 struct Stream {
-    unsigned char* ring;        // stages x kUnitBytes
-    uint64_t* full;             // one mbarrier per stage
+    unsigned char* ring;          // stages x stage_bytes
+    uint64_t* full;               // one mbarrier per stage
     int stages;
+    int stage_bytes;
     unsigned long long consumed;  // units every thread has finished with
     unsigned long long issued;    // thread 0 only
     Cursor cursor;                // thread 0 only: the next unit to issue
 };
 
-// The weight, extent and inner size a product-like op streams.
-__device__ __forceinline__ bool op_streams(const StepParams& p, const StepOp& op, const void** weight, int* n,
-                                           int* kp, int* rows) {
-    if (op.kind == kOpProduct) {
-        *weight = op.weight; *n = op.n; *kp = op.kp; *rows = p.rows;
+// A run of `tiles` contiguous 16-row tiles of `chunks` 1 KB chunks.  A stream
+// unit is `group` whole tiles, or -- for a tile larger than a stage -- a
+// k-block of one tile.
+struct Region {
+    const unsigned char* base;
+    int tiles, chunks, group;
+};
+
+__device__ __forceinline__ int row_tiles(int rows, int rt) { return (rows + rt - 1) / rt; }
+__device__ __forceinline__ int round16(int n) { return (n + 15) / 16 * 16; }
+
+// Items of an op (each CTA takes items blockIdx.x, + gridDim.x, ...).
+template <int RT>
+__device__ int op_items(const StepParams& p, const StepOp& op) {
+    switch (op.kind) {
+    case kOpProduct: return ((op.n + 15) / 16) * row_tiles(p.rows, RT);
+    case kOpLogits: return ((p.vocabulary + 15) / 16) * row_tiles(p.out_rows, RT);
+    case kOpSelfBlock: return p.heads * row_tiles(p.rows, 8);
+    case kOpCrossBlock: return p.heads * row_tiles(p.rows, 8) * op.splits;
+    case kOpFeedForwardBlock: return (p.ffn / op.slice) * row_tiles(p.rows, 8);
+    }
+    return 0;
+}
+
+// Weight region `region` of item `item` of an op; false when there is none.
+template <int RT>
+__device__ bool item_region(const StepParams& p, const StepOp& op, int item, int region, Region& out) {
+    const int chunks_d = p.kpd / 32;
+    switch (op.kind) {
+    case kOpProduct:
+    case kOpLogits: {
+        if (region != 0) return false;
+        const int n = op.kind == kOpProduct ? op.n : p.vocabulary;
+        const int kp = op.kind == kOpProduct ? op.kp : p.kpd;
+        const void* w = op.kind == kOpProduct ? op.weight : p.token_table;
+        const int tile = item % ((n + 15) / 16);
+        out = Region{static_cast<const unsigned char*>(w) + (size_t)tile * (kp / 32) * 1024, 1, kp / 32, 1};
         return true;
     }
-    if (op.kind == kOpLogits) {
-        *weight = p.token_table; *n = p.vocabulary; *kp = p.kpd; *rows = p.out_rows;
+    case kOpSelfBlock: {
+        const int head = item % p.heads;
+        if (region == 0) {
+            const int tiles = round16(3 * p.head_width) / 16;
+            out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)head * tiles * chunks_d * 1024, tiles,
+                         chunks_d, 1};
+            return true;
+        }
+        if (region == 1) {
+            out = Region{static_cast<const unsigned char*>(op.weight2) + (size_t)head * op.item_stride2,
+                         round16(p.width) / 16, op.kp2 / 32, op.group2};
+            return true;
+        }
+        return false;
+    }
+    case kOpCrossBlock: {
+        if (region != 0) return false;
+        const int head = (item / op.splits) % p.heads;
+        const int tiles = round16(p.head_width) / 16;
+        out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)head * tiles * chunks_d * 1024, tiles,
+                     chunks_d, 1};
         return true;
+    }
+    case kOpFeedForwardBlock: {
+        const int chunk = item % (p.ffn / op.slice);
+        if (region == 0) {
+            const int tiles = op.slice / 16;
+            out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)chunk * tiles * chunks_d * 1024, tiles,
+                         chunks_d, 1};
+            return true;
+        }
+        if (region == 1) {
+            out = Region{static_cast<const unsigned char*>(op.weight2) + (size_t)chunk * op.item_stride2,
+                         round16(p.width) / 16, op.kp2 / 32, op.group2};
+            return true;
+        }
+        return false;
+    }
     }
     return false;
 }
 
+// Units of a region, and the bytes and source of unit u.
+__device__ __forceinline__ int region_units(const Region& r, int stage_chunks) {
+    if (r.chunks > stage_chunks) return r.tiles * ((r.chunks + stage_chunks - 1) / stage_chunks);
+    return (r.tiles + r.group - 1) / r.group;
+}
+__device__ __forceinline__ const unsigned char* region_unit(const Region& r, int u, int stage_chunks, unsigned* bytes) {
+    if (r.chunks > stage_chunks) {
+        const int blocks = (r.chunks + stage_chunks - 1) / stage_chunks;
+        const int tile = u / blocks, block = u % blocks;
+        *bytes = (unsigned)min(stage_chunks, r.chunks - block * stage_chunks) * 1024u;
+        return r.base + ((size_t)tile * r.chunks + (size_t)block * stage_chunks) * 1024;
+    }
+    const int t0 = u * r.group;
+    *bytes = (unsigned)(min(r.group, r.tiles - t0) * r.chunks) * 1024u;
+    return r.base + (size_t)t0 * r.chunks * 1024;
+}
+
 // Thread 0: the next unit of this CTA's sequence, or false past the last step.
 template <int RT>
-__device__ bool next_unit(const StepParams& p, Cursor& c, const unsigned char** src, unsigned* bytes) {
+__device__ bool next_unit(const StepParams& p, const Stream& s, Cursor& c, const unsigned char** src,
+                          unsigned* bytes) {
+    const int stage_chunks = s.stage_bytes / 1024;
     while (c.step < p.steps) {
         if (c.op >= p.n_ops) {
             c.op = 0;
             c.item = blockIdx.x;
-            c.block = 0;
+            c.region = 0;
+            c.unit = 0;
             ++c.step;
             continue;
         }
-        const void* weight;
-        int n, kp, rows;
-        if (op_streams(p, p.ops[c.op], &weight, &n, &kp, &rows)) {
-            const int n_tiles = (n + 15) / 16;
-            const int items = n_tiles * ((rows + RT - 1) / RT);
-            if (c.item < items) {
-                const int chunks = kp / 32;
-                const int blocks = (chunks + kUnitChunks - 1) / kUnitChunks;
-                const int n_tile = c.item % n_tiles;
-                const int chunk0 = c.block * kUnitChunks;
-                *src = static_cast<const unsigned char*>(weight) + ((size_t)n_tile * chunks + chunk0) * 1024;
-                *bytes = (unsigned)min(kUnitChunks, chunks - chunk0) * 1024u;
-                if (++c.block == blocks) {
-                    c.block = 0;
-                    c.item += gridDim.x;
+        const StepOp& op = p.ops[c.op];
+        if (c.item < op_items<RT>(p, op)) {
+            Region r;
+            if (item_region<RT>(p, op, c.item, c.region, r)) {
+                if (c.unit < region_units(r, stage_chunks)) {
+                    *src = region_unit(r, c.unit, stage_chunks, bytes);
+                    ++c.unit;
+                    return true;
                 }
-                return true;
+                ++c.region;
+                c.unit = 0;
+                continue;
             }
+            c.item += gridDim.x;
+            c.region = 0;
+            c.unit = 0;
+            continue;
         }
         ++c.op;
         c.item = blockIdx.x;
-        c.block = 0;
+        c.region = 0;
+        c.unit = 0;
     }
     return false;
 }
@@ -182,10 +255,10 @@ __device__ void issue_ahead(const StepParams& p, Stream& s) {
     while (s.issued < s.consumed + (unsigned long long)s.stages) {
         const unsigned char* src;
         unsigned bytes;
-        if (!next_unit<RT>(p, s.cursor, &src, &bytes)) return;
+        if (!next_unit<RT>(p, s, s.cursor, &src, &bytes)) return;
         const int stage = (int)(s.issued % s.stages);
         const uint32_t bar = smem_address(s.full + stage);
-        const uint32_t dst = smem_address(s.ring + (size_t)stage * kUnitBytes);
+        const uint32_t dst = smem_address(s.ring + (size_t)stage * s.stage_bytes);
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
                      "l"(src), "r"(bytes), "r"(bar)
@@ -215,6 +288,17 @@ __device__ bool wait_unit(const StepParams& p, const Stream& s, unsigned long lo
             return false;
         }
     }
+}
+
+// The next unit, landed: thread 0 waits (bounded) and tells the CTA; then
+// every thread observes the completed phase.  nullptr if the wait gave up.
+__device__ const unsigned char* acquire_unit(const StepParams& p, const Stream& s) {
+    __shared__ int gave_up;
+    if (threadIdx.x == 0) gave_up = wait_unit(p, s, s.consumed) ? 0 : 1;
+    __syncthreads();
+    if (gave_up) return nullptr;
+    wait_unit(p, s, s.consumed);
+    return s.ring + (size_t)(s.consumed % s.stages) * s.stage_bytes;
 }
 
 // After a unit: every thread is done reading its stage, which thread 0 may
@@ -256,21 +340,22 @@ constexpr int kNormMaxPerLane = 48;  // widths up to 1536
 // the row in registers: the mean, then the centred variance, as
 // LayerNorm.h:19-98 does.  hidden_out, when given, receives the fp32 rows.
 template <typename WT>
-__device__ void layer_norm_tile(const StepParams& p, const float* gamma, const float* beta, int r0,
-                                int rows_in_tile, int row_step, int row_offset, WT* xs, int ldx,
+__device__ void layer_norm_tile(const StepParams& p, const float* input, const float* gamma, const float* beta,
+                                int r0, int rows_in_tile, int row_step, int row_offset, WT* xs, int ldx,
                                 float* hidden_out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = p.width;
     for (int rl = warp; rl < rows_in_tile; rl += kWarps) {
-        const float* x = p.h + ((size_t)(r0 + rl) * row_step + row_offset) * d;
+        const float* x = input + ((size_t)(r0 + rl) * row_step + row_offset) * d;
         float v[kNormMaxPerLane];
-        float total = 0.f;
 #pragma unroll
         for (int i = 0; i < kNormMaxPerLane; ++i) {
             const int c = lane + 32 * i;
             v[i] = c < d ? ld_cg(x + c) : 0.f;
-            total += v[i];
         }
+        float total = 0.f;
+#pragma unroll
+        for (int i = 0; i < kNormMaxPerLane; ++i) total += v[i];
         const float mean = warp_sum(total) / (float)d;
         float centred = 0.f;
 #pragma unroll
@@ -285,7 +370,7 @@ __device__ void layer_norm_tile(const StepParams& p, const float* gamma, const f
         for (int i = 0; i < kNormMaxPerLane; ++i) {
             const int c = lane + 32 * i;
             if (c < d) {
-                const float y = (v[i] - mean) * scale * gamma[c] + beta[c];
+                const float y = (v[i] - mean) * scale * __ldg(gamma + c) + __ldg(beta + c);
                 out[c] = Half16<WT>::from_float(y);
                 if (hidden_out) hidden_out[(size_t)(r0 + rl) * d + c] = y;
             } else if (c < ldx) {
@@ -341,7 +426,6 @@ template <typename WT, int NT, bool X_SHARED>
 __device__ bool product_tile(const StepParams& p, Stream& s, int kp, const WT* X, int ldx, int rows_valid,
                              float (&acc)[NT][4]) {
     constexpr int RT = 8 * NT;
-    __shared__ int gave_up;
     const int warp = threadIdx.x >> 5, gq = (threadIdx.x & 31) >> 2;
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -349,13 +433,11 @@ __device__ bool product_tile(const StepParams& p, Stream& s, int kp, const WT* X
 #pragma unroll
     for (int j = 0; j < NT; ++j) x_ok[j] = 8 * j + gq < rows_valid;
     const int chunks = kp / 32;
-    for (int c0 = 0; c0 < chunks; c0 += kUnitChunks) {
-        const int n = min(kUnitChunks, chunks - c0);
-        if (threadIdx.x == 0) gave_up = wait_unit(p, s, s.consumed) ? 0 : 1;
-        __syncthreads();
-        if (gave_up) return false;
-        wait_unit(p, s, s.consumed);  // every thread observes the completed phase
-        const unsigned char* unit = s.ring + (size_t)(s.consumed % s.stages) * kUnitBytes;
+    const int stage_chunks = s.stage_bytes / 1024;
+    for (int c0 = 0; c0 < chunks; c0 += stage_chunks) {
+        const int n = min(stage_chunks, chunks - c0);
+        const unsigned char* unit = acquire_unit(p, s);
+        if (!unit) return false;
         for (int c = warp; c < n; c += kWarps)
             product_chunk<WT, NT, X_SHARED>(unit, c, X, ldx, (c0 + c) * 32, x_ok, acc);
         release_unit<RT>(p, s);
@@ -409,7 +491,7 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
         if (normalise) {
             if (cached_tile != r_tile) {
                 __syncthreads();
-                layer_norm_tile<WT>(p, op.gamma, op.beta, r0, rows_valid, 1, 0, xs, pitch, nullptr);
+                layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, xs, pitch, nullptr);
                 __syncthreads();
                 cached_tile = r_tile;
             }
@@ -427,9 +509,17 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
             float v = product_sum(red, RT, nl, rl);
             if (op.bias) v += op.bias[n];
             switch (op.epilogue) {
-            case kEpStore:
-                static_cast<float*>(op.out)[(size_t)r * op.ld_out + n] = v;
+            case kEpStore: {
+                // Rows grouped by head, each head's rows padded to a whole tile.
+                int col = n;
+                if (op.slice > 0) {
+                    const int within = n % round16(op.slice);
+                    if (within >= op.slice) break;
+                    col = (n / round16(op.slice)) * op.slice + within;
+                }
+                static_cast<float*>(op.out)[(size_t)r * op.ld_out + col] = v;
                 break;
+            }
             case kEpResidual: {
                 float* at = static_cast<float*>(op.out) + (size_t)r * op.ld_out + n;
                 *at = ld_cg(at) + v;
@@ -438,17 +528,22 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
             case kEpGelu:
                 static_cast<WT*>(op.out)[(size_t)r * op.ld_out + n] = Half16<WT>::from_float(gelu_exact(v));
                 break;
-            case kEpQkv:
-                if (n < p.width) {
-                    static_cast<float*>(op.out)[(size_t)r * op.ld_out + n] = v;
+            case kEpQkv: {
+                // Head h's rows: its q, k and v rows, padded to a whole tile.
+                const int D = p.head_width, group = round16(3 * D);
+                const int within = n % group;
+                if (within >= 3 * D) break;
+                const int col = (n / group) * D + within % D;
+                const int which = within / D;
+                if (which == 0) {
+                    static_cast<float*>(op.out)[(size_t)r * op.ld_out + col] = v;
                 } else {
-                    const int which = (n - p.width) / p.width;
-                    const int c = n - p.width - which * p.width;
                     const int b = r / p.tokens, t = r % p.tokens;
-                    WT* cache = static_cast<WT*>(which == 0 ? op.self_keys : op.self_values);
-                    cache[((size_t)b * p.max_positions + position + t) * p.width + c] = Half16<WT>::from_float(v);
+                    WT* cache = static_cast<WT*>(which == 1 ? op.self_keys : op.self_values);
+                    cache[((size_t)b * p.max_positions + position + t) * p.width + col] = Half16<WT>::from_float(v);
                 }
                 break;
+            }
             }
         }
         __syncthreads();
@@ -488,7 +583,7 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
         const int rows_valid = min(RT, p.out_rows - r0);
         if (cached_tile != r_tile) {
             __syncthreads();
-            layer_norm_tile<WT>(p, p.final_gamma, p.final_beta, r0, rows_valid, p.row_step, p.row_offset, xs, pitch,
+            layer_norm_tile<WT>(p, p.h, p.final_gamma, p.final_beta, r0, rows_valid, p.row_step, p.row_offset, xs, pitch,
                                 p.hidden_out);
             __syncthreads();
             cached_tile = r_tile;
@@ -574,27 +669,60 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
 
 // ----------------------------------------------------------------- attention
 
-// Scores of keys [k0, k1) against q (in shared, pre-scaled), into scores[];
-// returns this thread's maximum.
+template <typename WT, bool READ_ONLY>
+__device__ __forceinline__ uint4 load_kv4(const WT* at) {
+    return READ_ONLY ? ld_nc4(at) : ld_cg4(at);
+}
+template <typename WT, bool READ_ONLY>
+__device__ __forceinline__ float load_kv1(const WT* at) {
+    return bits_to_float<WT>(READ_ONLY ? ld_nc_u16(at) : ld_cg_u16(at));
+}
+
+// q . K[key] over a 64-wide head: the key row's eight 16-byte pieces are all
+// loaded before any is used, so a score costs one memory latency.
+template <typename WT, bool READ_ONLY>
+__device__ __forceinline__ float score64(const float* q, const WT* krow) {
+    uint4 u[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) u[i] = load_kv4<WT, READ_ONLY>(krow + 8 * i);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float2 f0 = Half16<WT>::pair_to_float2(u[i].x), f1 = Half16<WT>::pair_to_float2(u[i].y);
+        const float2 f2 = Half16<WT>::pair_to_float2(u[i].z), f3 = Half16<WT>::pair_to_float2(u[i].w);
+        const float* qq = q + 8 * i;
+        s += qq[0] * f0.x + qq[1] * f0.y + qq[2] * f1.x + qq[3] * f1.y + qq[4] * f2.x + qq[5] * f2.y + qq[6] * f3.x +
+             qq[7] * f3.y;
+    }
+    return s;
+}
+
+template <typename WT, bool READ_ONLY>
+__device__ __forceinline__ float score_any(const float* q, const WT* krow, int D) {
+    if (D == 64) return score64<WT, READ_ONLY>(q, krow);
+    float s = 0.f;
+    if (D % 8 == 0) {
+        for (int c = 0; c < D; c += 8) {
+            const uint4 u = load_kv4<WT, READ_ONLY>(krow + c);
+            const float2 f0 = Half16<WT>::pair_to_float2(u.x), f1 = Half16<WT>::pair_to_float2(u.y);
+            const float2 f2 = Half16<WT>::pair_to_float2(u.z), f3 = Half16<WT>::pair_to_float2(u.w);
+            s += q[c] * f0.x + q[c + 1] * f0.y + q[c + 2] * f1.x + q[c + 3] * f1.y + q[c + 4] * f2.x +
+                 q[c + 5] * f2.y + q[c + 6] * f3.x + q[c + 7] * f3.y;
+        }
+    } else {
+        for (int c = 0; c < D; ++c) s += q[c] * load_kv1<WT, READ_ONLY>(krow + c);
+    }
+    return s;
+}
+
+// Scores of keys [k0, k0+n) against q (in shared, pre-scaled), into scores[],
+// a thread per key; returns this thread's maximum.
 template <typename WT, bool READ_ONLY>
 __device__ __forceinline__ float attention_scores(const float* q, const WT* K, long long key_stride, int D, int k0,
                                                   int n, float* scores) {
     float local_max = -INFINITY;
     for (int j = threadIdx.x; j < n; j += kThreads) {
-        const WT* krow = K + (size_t)(k0 + j) * key_stride;
-        float s = 0.f;
-        if (D % 8 == 0) {
-            for (int c = 0; c < D; c += 8) {
-                const uint4 u = READ_ONLY ? load_stream(krow + c) : ld_cg4(krow + c);
-                const float2 f0 = Half16<WT>::pair_to_float2(u.x), f1 = Half16<WT>::pair_to_float2(u.y);
-                const float2 f2 = Half16<WT>::pair_to_float2(u.z), f3 = Half16<WT>::pair_to_float2(u.w);
-                s += q[c] * f0.x + q[c + 1] * f0.y + q[c + 2] * f1.x + q[c + 3] * f1.y + q[c + 4] * f2.x +
-                     q[c + 5] * f2.y + q[c + 6] * f3.x + q[c + 7] * f3.y;
-            }
-        } else {
-            for (int c = 0; c < D; ++c)
-                s += q[c] * bits_to_float<WT>(READ_ONLY ? ld_nc_u16(krow + c) : ld_cg_u16(krow + c));
-        }
+        const float s = score_any<WT, READ_ONLY>(q, K + (size_t)(k0 + j) * key_stride, D);
         scores[j] = s;
         local_max = fmaxf(local_max, s);
     }
@@ -602,8 +730,9 @@ __device__ __forceinline__ float attention_scores(const float* q, const WT* K, l
 }
 
 // sum_j p_j V[k0 + j] over the keys into result[0..D).  With D a multiple
-// of 8, thread (group, piece) reads 16 bytes of a value row per key and the
-// 256/(D/8) key groups fold in shared memory (fold holds 2048 floats).
+// of 8, thread (group, piece) reads 16 bytes of a value row per key, four
+// keys' loads in flight at a time, and the 256/(D/8) key groups fold in
+// shared memory (fold holds 2048 floats).
 template <typename WT, bool READ_ONLY>
 __device__ __forceinline__ void attention_values(const float* scores, const WT* V, long long key_stride, int D,
                                                  int k0, int n, float* fold, float* result) {
@@ -613,9 +742,9 @@ __device__ __forceinline__ void attention_values(const float* scores, const WT* 
         const int piece = threadIdx.x % pieces, g = threadIdx.x / pieces;
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (g < groups) {
+#pragma unroll 4
             for (int j = g; j < n; j += groups) {
-                const WT* at = V + (size_t)(k0 + j) * key_stride + piece * 8;
-                const uint4 u = READ_ONLY ? load_stream(at) : ld_cg4(at);
+                const uint4 u = load_kv4<WT, READ_ONLY>(V + (size_t)(k0 + j) * key_stride + piece * 8);
                 const float w = scores[j];
                 const float2 f0 = Half16<WT>::pair_to_float2(u.x), f1 = Half16<WT>::pair_to_float2(u.y);
                 const float2 f2 = Half16<WT>::pair_to_float2(u.z), f3 = Half16<WT>::pair_to_float2(u.w);
@@ -635,12 +764,12 @@ __device__ __forceinline__ void attention_values(const float* scores, const WT* 
         const int groups = kThreads / D;
         const int c = threadIdx.x % D, g = threadIdx.x / D;
         float acc = 0.f;
-        if (g < groups)
-            for (int j = g; j < n; j += groups) {
-                const WT* at = V + (size_t)(k0 + j) * key_stride + c;
-                acc += scores[j] * bits_to_float<WT>(READ_ONLY ? ld_nc_u16(at) : ld_cg_u16(at));
-            }
-        if (g < groups) fold[g * D + c] = acc;
+        if (g < groups) {
+#pragma unroll 4
+            for (int j = g; j < n; j += groups)
+                acc += scores[j] * load_kv1<WT, READ_ONLY>(V + (size_t)(k0 + j) * key_stride + c);
+            fold[g * D + c] = acc;
+        }
         __syncthreads();
         if (threadIdx.x < D) {
             float o = 0.f;
@@ -649,6 +778,58 @@ __device__ __forceinline__ void attention_values(const float* scores, const WT* 
         }
     }
     __syncthreads();
+}
+
+// One warp's attention of one query over keys [k0, k0+n), n <= kWarpKeys:
+// lanes score keys, the warp folds the maximum and the sum, then lane c and
+// c+32 accumulate channels c and c+32 over the keys, eight loads in flight.
+// Leaves the unnormalised row in out[0..D) and returns (max, sum).
+constexpr int kWarpKeys = 512;
+
+template <typename WT, bool READ_ONLY>
+__device__ float2 warp_attention(const float* q, const WT* K, const WT* V, long long key_stride, int D, int k0,
+                                 int n, float* scores, float* out) {
+    const int lane = threadIdx.x & 31;
+    float mx = -INFINITY;
+    for (int j = lane; j < n; j += 32) {
+        const float sc = score_any<WT, READ_ONLY>(q, K + (size_t)(k0 + j) * key_stride, D);
+        scores[j] = sc;
+        mx = fmaxf(mx, sc);
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int j = lane; j < n; j += 32) {
+        const float e = __expf(scores[j] - mx);
+        scores[j] = e;
+        sum += e;
+    }
+    sum = warp_sum(sum);
+    __syncwarp();
+    float a0 = 0.f, a1 = 0.f;
+    const bool c0 = lane < D, c1 = lane + 32 < D;
+    const WT* v = V + (size_t)k0 * key_stride;
+    int j = 0;
+    for (; j + 8 <= n; j += 8) {
+        float x0[8], x1[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            x0[u] = c0 ? load_kv1<WT, READ_ONLY>(v + (size_t)(j + u) * key_stride + lane) : 0.f;
+            x1[u] = c1 ? load_kv1<WT, READ_ONLY>(v + (size_t)(j + u) * key_stride + lane + 32) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            a0 += scores[j + u] * x0[u];
+            a1 += scores[j + u] * x1[u];
+        }
+    }
+    for (; j < n; ++j) {
+        if (c0) a0 += scores[j] * load_kv1<WT, READ_ONLY>(v + (size_t)j * key_stride + lane);
+        if (c1) a1 += scores[j] * load_kv1<WT, READ_ONLY>(v + (size_t)j * key_stride + lane + 32);
+    }
+    if (c0) out[lane] = a0;
+    if (c1) out[lane + 32] = a1;
+    __syncwarp();
+    return make_float2(mx, sum);
 }
 
 // Shared memory of attention: [q: 64][scratch: 8][fold: 2048][result: 64][scores: ...]
@@ -763,9 +944,399 @@ __device__ void op_cross_attention(const StepParams& p, const StepOp& op, unsign
     }
 }
 
-// -------------------------------------------------------------- the kernel
+// ---------------------------------------------------- fused blocks (T = 1)
 
-template <int NT> struct StreamStages { static constexpr int value = NT <= 2 ? 4 : 3; };
+constexpr int kBlockRows = 8;        // rows of a fused-block item
+constexpr int kMaxSplitTiles = 12;   // 16-row tiles of a K-split product: 3 x 64 q/k/v rows
+constexpr int kSmallPitch = 96;      // shared pitch of a <= 64-wide product input
+
+__host__ __device__ __forceinline__ size_t align128(size_t n) { return (n + 127) / 128 * 128; }
+
+template <typename WT>
+struct BlockArea {
+    WT* xs;       // [8][pitch]       normalised rows
+    float* red;   // [8 warps][12 tiles][16][8]
+    float* res;   // [12*16][8]       reduced K-split products, [n][row]
+    float* q;     // [8][64]          scaled queries
+    WT* o16;      // [8][96]          attention or GELU rows, a product input
+    float* att;   // attention scratch
+    int pitch;
+};
+
+__host__ __device__ inline size_t block_area_bytes(int kpd, int wt_bytes, int max_positions) {
+    const size_t att = sizeof(float) * (size_t)max(8 + 2048 + 64 + max(max_positions, 512), kWarps * kWarpKeys);
+    return align128((size_t)kBlockRows * tile_pitch(kpd) * wt_bytes) + sizeof(float) * kWarps * kMaxSplitTiles * 16 * 8 +
+           sizeof(float) * kMaxSplitTiles * 16 * 8 + sizeof(float) * 8 * 64 +
+           align128((size_t)kBlockRows * kSmallPitch * wt_bytes) + att;
+}
+
+template <typename WT>
+__device__ BlockArea<WT> block_area(const StepParams& p, unsigned char* work) {
+    BlockArea<WT> a;
+    a.pitch = tile_pitch(p.kpd);
+    unsigned char* at = work;
+    a.xs = reinterpret_cast<WT*>(at);
+    at += align128((size_t)kBlockRows * a.pitch * sizeof(WT));
+    a.red = reinterpret_cast<float*>(at);
+    at += sizeof(float) * kWarps * kMaxSplitTiles * 16 * 8;
+    a.res = reinterpret_cast<float*>(at);
+    at += sizeof(float) * kMaxSplitTiles * 16 * 8;
+    a.q = reinterpret_cast<float*>(at);
+    at += sizeof(float) * 8 * 64;
+    a.o16 = reinterpret_cast<WT*>(at);
+    at += align128((size_t)kBlockRows * kSmallPitch * sizeof(WT));
+    a.att = reinterpret_cast<float*>(at);
+    return a;
+}
+
+// `tiles` units off the stream, each one 16-row tile over all of kpd; the 8
+// warps take alternate chunks of every tile into per-tile accumulators, and
+// one fold at the end leaves res[(t*16 + row)*8 + input row].
+template <typename WT, int NT>
+__device__ bool split_product(const StepParams& p, Stream& s, int tiles, const BlockArea<WT>& A, int rows_valid) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;
+    const bool x_ok[1] = {gq < rows_valid};
+    const int chunks = p.kpd / 32;
+    float acc[kMaxSplitTiles][1][4];
+#pragma unroll
+    for (int t = 0; t < kMaxSplitTiles; ++t) acc[t][0][0] = acc[t][0][1] = acc[t][0][2] = acc[t][0][3] = 0.f;
+#pragma unroll
+    for (int t = 0; t < kMaxSplitTiles; ++t) {
+        if (t < tiles) {
+            const unsigned char* unit = acquire_unit(p, s);
+            if (!unit) return false;
+            for (int c = warp; c < chunks; c += kWarps)
+                product_chunk<WT, 1, true>(unit, c, A.xs, A.pitch, c * 32, x_ok, acc[t]);
+            release_unit<8 * NT>(p, s);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kMaxSplitTiles; ++t) {
+        if (t < tiles) {
+            float* r = A.red + (size_t)(warp * kMaxSplitTiles + t) * 128;
+            r[gq * 8 + 2 * tq] = acc[t][0][0];
+            r[gq * 8 + 2 * tq + 1] = acc[t][0][1];
+            r[(gq + 8) * 8 + 2 * tq] = acc[t][0][2];
+            r[(gq + 8) * 8 + 2 * tq + 1] = acc[t][0][3];
+        }
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < tiles * 128; o += kThreads) {
+        const int t = o / 128, within = o % 128;
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) v += A.red[(size_t)(w * kMaxSplitTiles + t) * 128 + within];
+        A.res[o] = v;
+    }
+    __syncthreads();
+    return true;
+}
+
+// A product whose tiles each fit a warp whole (K <= 64): warp w takes tiles
+// w, w+8, ... over all K and hands every output to emit(n, row, value).
+// Streamed: `group` tiles to a unit.
+template <typename WT, int NT, typename Emit>
+__device__ bool tiled_product(const StepParams& p, Stream& s, int tiles, int chunks, int group, const WT* X,
+                              int ldx, int rows_valid, Emit&& emit) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;
+    const bool x_ok[1] = {gq < rows_valid};
+    for (int t0 = 0; t0 < tiles; t0 += group) {
+        const int nt = min(group, tiles - t0);
+        const unsigned char* unit = acquire_unit(p, s);
+        if (!unit) return false;
+        for (int tl = warp; tl < nt; tl += kWarps) {
+            float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+            const unsigned char* tile = unit + (size_t)tl * chunks * 1024;
+            for (int c = 0; c < chunks; ++c) product_chunk<WT, 1, true>(tile, c, X, ldx, c * 32, x_ok, acc);
+            const int n = (t0 + tl) * 16 + gq, rl = 2 * tq;
+            emit(n, rl, acc[0][0]);
+            emit(n, rl + 1, acc[0][1]);
+            emit(n + 8, rl, acc[0][2]);
+            emit(n + 8, rl + 1, acc[0][3]);
+        }
+        release_unit<8 * NT>(p, s);
+    }
+    return true;
+}
+
+// The same over weights read straight from global memory (not streamed).
+template <typename WT, typename Emit>
+__device__ void direct_tiled_product(const unsigned char* weights, int tiles, int chunks, const WT* X, int ldx,
+                                     int rows_valid, Emit&& emit) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;
+    const bool x_ok[1] = {gq < rows_valid};
+    for (int t = warp; t < tiles; t += kWarps) {
+        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+        const unsigned char* tile = weights + (size_t)t * chunks * 1024;
+        for (int c = 0; c < chunks; ++c) product_chunk<WT, 1, true>(tile, c, X, ldx, c * 32, x_ok, acc);
+        const int n = t * 16 + gq, rl = 2 * tq;
+        emit(n, rl, acc[0][0]);
+        emit(n, rl + 1, acc[0][1]);
+        emit(n + 8, rl, acc[0][2]);
+        emit(n + 8, rl + 1, acc[0][3]);
+    }
+}
+
+// One query of one row over keys [k0, k0+n) by the whole CTA: the
+// unnormalised row lands in att[8 + 2048 .. + D); returns (max, sum).
+template <typename WT, bool READ_ONLY>
+__device__ float2 cta_attention(const float* q, const WT* K, const WT* V, long long key_stride, int D, int k0, int n,
+                                float* att) {
+    float* scratch = att;
+    float* fold = att + 8;
+    float* result = fold + kFold;
+    float* scores = result + 64;
+    if (n <= 0) return make_float2(-INFINITY, 0.f);
+    const float m = block_max(attention_scores<WT, READ_ONLY>(q, K, key_stride, D, k0, n, scores), scratch);
+    float local = 0.f;
+    for (int j = threadIdx.x; j < n; j += kThreads) {
+        const float e = __expf(scores[j] - m);
+        scores[j] = e;
+        local += e;
+    }
+    const float l = block_sum(local, scratch);
+    attention_values<WT, READ_ONLY>(scores, V, key_stride, D, k0, n, fold, result);
+    return make_float2(m, l);
+}
+
+__device__ __forceinline__ void zero_rows(float* x, int r0, int rows, int width) {
+    for (int o = threadIdx.x; o < rows * width; o += kThreads) x[(size_t)r0 * width + o] = 0.f;
+}
+
+// Self block: item (head, 8 rows).  Reads X0, adds into X1, zeroes X2.
+template <typename WT, int NT>
+__device__ void op_self_block(const StepParams& p, const StepOp& op, int position, Stream& s, unsigned char* work) {
+    const BlockArea<WT> A = block_area<WT>(p, work);
+    const int D = p.head_width, H = p.heads, d = p.width;
+    const int r_tiles = row_tiles(p.rows, kBlockRows);
+    const int group = round16(3 * D);
+    const int ps = tile_pitch(op.kp2);
+    int cached = -1;
+    for (int item = blockIdx.x; item < H * r_tiles; item += gridDim.x) {
+        const int head = item % H, r_tile = item / H;
+        const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
+        if (cached != r_tile) {
+            __syncthreads();
+            layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
+            __syncthreads();
+            cached = r_tile;
+        }
+        if (!split_product<WT, NT>(p, s, group / 16, A, rows_valid)) return;
+        // The head's query (scaled) to shared; its key and value rows of this
+        // position into the cache (Decoder.cpp:29-48; row r is window r).
+        const float* bias = op.bias + (size_t)head * group;
+        for (int o = threadIdx.x; o < 3 * D * rows_valid; o += kThreads) {
+            const int n = o / rows_valid, rl = o % rows_valid;
+            const float v = A.res[n * 8 + rl] + __ldg(bias + n);
+            const int which = n / D, c = n % D;
+            if (which == 0) {
+                A.q[rl * 64 + c] = v * p.scale;
+            } else {
+                WT* cache = static_cast<WT*>(which == 1 ? op.self_keys : op.self_values);
+                cache[((size_t)(r0 + rl) * p.max_positions + position) * d + head * D + c] = Half16<WT>::from_float(v);
+            }
+        }
+        __syncthreads();
+        const int keys = position + 1;
+        if (rows_valid <= 2) {
+            for (int rl = 0; rl < rows_valid; ++rl) {
+                const size_t base = (size_t)(r0 + rl) * p.max_positions * d + (size_t)head * D;
+                const float2 ml = cta_attention<WT, false>(A.q + rl * 64, static_cast<const WT*>(op.self_keys) + base,
+                                                           static_cast<const WT*>(op.self_values) + base, d, D, 0,
+                                                           keys, A.att);
+                const float* row = A.att + 8 + kFold;
+                for (int c = threadIdx.x; c < op.kp2; c += kThreads)
+                    A.o16[rl * ps + c] = Half16<WT>::from_float(c < D ? row[c] / ml.y : 0.f);
+                __syncthreads();
+            }
+        } else {
+            const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+            if (warp < rows_valid) {
+                const int rl = warp;
+                const size_t base = (size_t)(r0 + rl) * p.max_positions * d + (size_t)head * D;
+                float* row = A.res + warp * 64;
+                const float2 ml = warp_attention<WT, false>(A.q + rl * 64, static_cast<const WT*>(op.self_keys) + base,
+                                                            static_cast<const WT*>(op.self_values) + base, d, D, 0,
+                                                            keys, A.att + warp * kWarpKeys, row);
+                for (int c = lane; c < op.kp2; c += 32)
+                    A.o16[rl * ps + c] = Half16<WT>::from_float(c < D ? row[c] / ml.y : 0.f);
+            }
+            __syncthreads();
+        }
+        // X1 += the head's slice of out_proj; head 0 adds the bias and X0.
+        const bool first = head == 0;
+        if (!tiled_product<WT, NT>(p, s, round16(d) / 16, op.kp2 / 32, op.group2, A.o16, ps, rows_valid,
+                                   [&](int n, int rl, float v) {
+                                       if (n >= d || rl >= rows_valid) return;
+                                       const size_t at = (size_t)(r0 + rl) * d + n;
+                                       if (first) v += __ldg(op.bias2 + n) + ld_cg(p.h + at);
+                                       atomicAdd(p.x1 + at, v);
+                                   }))
+            return;
+        if (first) zero_rows(p.x2, r0, rows_valid, d);
+        __syncthreads();
+    }
+}
+
+// Cross block: item (head, 8 rows, key split).  Reads X1, adds into X2,
+// zeroes X0.
+template <typename WT, int NT>
+__device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
+    const BlockArea<WT> A = block_area<WT>(p, work);
+    const int D = p.head_width, H = p.heads, d = p.width, S = op.splits;
+    const int r_tiles = row_tiles(p.rows, kBlockRows);
+    const int group = round16(D);
+    const int ps = tile_pitch(op.kp2);
+    __shared__ int is_last;
+    int cached = -1;
+    for (int item = blockIdx.x; item < H * r_tiles * S; item += gridDim.x) {
+        const int split = item % S, head = (item / S) % H, r_tile = item / (S * H);
+        const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
+        if (cached != r_tile) {
+            __syncthreads();
+            layer_norm_tile<WT>(p, p.x1, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
+            __syncthreads();
+            cached = r_tile;
+        }
+        if (!split_product<WT, NT>(p, s, group / 16, A, rows_valid)) return;
+        const float* bias = op.bias + (size_t)head * group;
+        for (int o = threadIdx.x; o < D * rows_valid; o += kThreads) {
+            const int n = o / rows_valid, rl = o % rows_valid;
+            A.q[rl * 64 + n] = (A.res[n * 8 + rl] + __ldg(bias + n)) * p.scale;
+        }
+        __syncthreads();
+        // This split's partial (max, sum, unnormalised row) of every row.
+        const int k0 = split * op.chunk;
+        const int n_keys = min(op.key_count, k0 + op.chunk) - k0;
+        auto partial_of = [&](int rl) {
+            return p.partial + (((size_t)(r0 + rl) * H + head) * S + split) * (D + 2);
+        };
+        if (rows_valid <= 2) {
+            for (int rl = 0; rl < rows_valid; ++rl) {
+                const size_t base = (size_t)(r0 + rl) * op.window_stride + (size_t)head * D;
+                const float2 ml = cta_attention<WT, true>(A.q + rl * 64, static_cast<const WT*>(op.keys) + base,
+                                                          static_cast<const WT*>(op.values) + base, op.key_stride, D,
+                                                          k0, n_keys, A.att);
+                const float* row = A.att + 8 + kFold;
+                float* out = partial_of(rl);
+                for (int c = threadIdx.x; c < D; c += kThreads) out[2 + c] = n_keys > 0 ? row[c] : 0.f;
+                if (threadIdx.x == 0) {
+                    out[0] = ml.x;
+                    out[1] = ml.y;
+                }
+                __syncthreads();
+            }
+        } else {
+            const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+            if (warp < rows_valid) {
+                const int rl = warp;
+                const size_t base = (size_t)(r0 + rl) * op.window_stride + (size_t)head * D;
+                float* out = partial_of(rl);
+                if (n_keys > 0) {
+                    const float2 ml = warp_attention<WT, true>(A.q + rl * 64, static_cast<const WT*>(op.keys) + base,
+                                                               static_cast<const WT*>(op.values) + base,
+                                                               op.key_stride, D, k0, n_keys, A.att + warp * kWarpKeys,
+                                                               out + 2);
+                    if (lane == 0) {
+                        out[0] = ml.x;
+                        out[1] = ml.y;
+                    }
+                } else {
+                    for (int c = lane; c < D + 2; c += 32) out[c] = c == 0 ? -INFINITY : 0.f;
+                }
+            }
+        }
+        if (head == 0 && split == 0) zero_rows(p.h, r0, rows_valid, d);
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned* counter = p.combine_counters + (size_t)r_tile * H + head;
+            is_last = atomicAdd(counter, 1u) == (unsigned)(S - 1);
+            if (is_last) atomicExch(counter, 0u);
+        }
+        __syncthreads();
+        if (!is_last) continue;
+        __threadfence();
+        // The last split joins the splits of every row (SingleQueryAttention.h:11-37)
+        // and adds the v_proj bias (the weights sum to one).
+        for (int o = threadIdx.x; o < rows_valid * op.kp2; o += kThreads) {
+            const int rl = o / op.kp2, c = o % op.kp2;
+            float y = 0.f;
+            if (c < D) {
+                const float* part = p.partial + ((size_t)(r0 + rl) * H + head) * S * (D + 2);
+                float mx = -INFINITY;
+                for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, ld_cg(part + (size_t)sp * (D + 2)));
+                float l = 0.f, acc = 0.f;
+                for (int sp = 0; sp < S; ++sp) {
+                    const float ms = ld_cg(part + (size_t)sp * (D + 2));
+                    if (ms == -INFINITY) continue;
+                    const float f = __expf(ms - mx);
+                    l += ld_cg(part + (size_t)sp * (D + 2) + 1) * f;
+                    acc += ld_cg(part + (size_t)sp * (D + 2) + 2 + c) * f;
+                }
+                y = acc / l + __ldg(op.value_bias + head * D + c);
+            }
+            A.o16[rl * ps + c] = Half16<WT>::from_float(y);
+        }
+        __syncthreads();
+        // X2 += the head's slice of out_proj; head 0 adds the bias and X1.
+        const bool first = head == 0;
+        direct_tiled_product<WT>(static_cast<const unsigned char*>(op.weight2) + (size_t)head * op.item_stride2,
+                                 round16(d) / 16, op.kp2 / 32, A.o16, ps, rows_valid, [&](int n, int rl, float v) {
+                                     if (n >= d || rl >= rows_valid) return;
+                                     const size_t at = (size_t)(r0 + rl) * d + n;
+                                     if (first) v += __ldg(op.bias2 + n) + ld_cg(p.x1 + at);
+                                     atomicAdd(p.x2 + at, v);
+                                 });
+        __syncthreads();
+    }
+}
+
+// Feed-forward block: item (fc1 chunk, 8 rows).  Reads X2, adds into X0,
+// zeroes X1.
+template <typename WT, int NT>
+__device__ void op_ffn_block(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
+    const BlockArea<WT> A = block_area<WT>(p, work);
+    const int d = p.width, FC = op.slice, chunks_n = p.ffn / FC;
+    const int r_tiles = row_tiles(p.rows, kBlockRows);
+    const int ps = tile_pitch(op.kp2);
+    int cached = -1;
+    for (int item = blockIdx.x; item < chunks_n * r_tiles; item += gridDim.x) {
+        const int j = item % chunks_n, r_tile = item / chunks_n;
+        const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
+        if (cached != r_tile) {
+            __syncthreads();
+            layer_norm_tile<WT>(p, p.x2, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
+            __syncthreads();
+            cached = r_tile;
+        }
+        if (!split_product<WT, NT>(p, s, FC / 16, A, rows_valid)) return;
+        const float* bias = op.bias + (size_t)j * FC;
+        for (int o = threadIdx.x; o < rows_valid * op.kp2; o += kThreads) {
+            const int rl = o / op.kp2, c = o % op.kp2;
+            const float v = c < FC ? gelu_exact(A.res[c * 8 + rl] + __ldg(bias + c)) : 0.f;
+            A.o16[rl * ps + c] = Half16<WT>::from_float(v);
+        }
+        __syncthreads();
+        // X0 += the fc2 slice of this chunk; chunk 0 adds the bias and X2.
+        const bool first = j == 0;
+        if (!tiled_product<WT, NT>(p, s, round16(d) / 16, op.kp2 / 32, op.group2, A.o16, ps, rows_valid,
+                                   [&](int n, int rl, float v) {
+                                       if (n >= d || rl >= rows_valid) return;
+                                       const size_t at = (size_t)(r0 + rl) * d + n;
+                                       if (first) v += __ldg(op.bias2 + n) + ld_cg(p.x2 + at);
+                                       atomicAdd(p.h + at, v);
+                                   }))
+            return;
+        if (first) zero_rows(p.x1, r0, rows_valid, d);
+        __syncthreads();
+    }
+}
+
+// -------------------------------------------------------------- the kernel
 
 // Thread 0, on the way out: no bulk copy may still be landing in shared
 // memory once the CTA exits, so wait (bounded) for every unit issued.
@@ -776,18 +1347,21 @@ __device__ void drain_stream(const StepParams& p, Stream& s) {
     __syncthreads();
 }
 
+constexpr int kMaxStages = 8;
+
 template <typename WT, int NT>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(StepParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int RT = 8 * NT;
     Stream s;
-    s.stages = StreamStages<NT>::value;
+    s.stages = p.stages;
+    s.stage_bytes = p.stage_bytes;
     s.ring = smem;
-    s.full = reinterpret_cast<uint64_t*>(smem + (size_t)s.stages * kUnitBytes);
-    unsigned char* work = smem + (size_t)s.stages * kUnitBytes + 128;
+    s.full = reinterpret_cast<uint64_t*>(smem + (size_t)s.stages * s.stage_bytes);
+    unsigned char* work = smem + (size_t)s.stages * s.stage_bytes + 8 * kMaxStages;
     s.consumed = 0;
     s.issued = 0;
-    s.cursor = Cursor{0, 0, (int)blockIdx.x, 0};
+    s.cursor = Cursor{0, 0, (int)blockIdx.x, 0, 0};
     if (threadIdx.x == 0) {
         for (int i = 0; i < s.stages; ++i)
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(s.full + i)) : "memory");
@@ -809,6 +1383,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(StepParams p) {
             case kOpSelfAttention: op_self_attention<WT>(p, op, position, work); break;
             case kOpCrossAttention: op_cross_attention<WT>(p, op, work); break;
             case kOpLogits: op_logits<WT, NT>(p, position, s, work); break;
+            case kOpSelfBlock: op_self_block<WT, NT>(p, op, position, s, work); break;
+            case kOpCrossBlock: op_cross_block<WT, NT>(p, op, s, work); break;
+            case kOpFeedForwardBlock: op_ffn_block<WT, NT>(p, op, s, work); break;
             }
             if (!grid_barrier(p.barrier, epoch, p.state)) {
                 drain_stream(p, s);
@@ -821,19 +1398,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(StepParams p) {
     drain_stream(p, s);
 }
 
+// Shared memory past the ring: the largest work area any op of the launch uses.
 template <typename WT, int NT>
-size_t shared_bytes(const StepParams& p, int max_chunk) {
+size_t work_bytes(const StepParams& p, int max_chunk, bool fused) {
     constexpr int RT = 8 * NT;
     const size_t product = (size_t)RT * tile_pitch(p.kpd) * sizeof(WT) +
                            sizeof(float) * (kWarps * 16 * RT + 16 * RT) + (size_t)p.out_rows * 8;
     const size_t attention = sizeof(float) * (kAttentionFixed + std::max(max_chunk, p.max_positions));
-    const size_t work = (std::max(product, attention) + 127) / 128 * 128;
-    return (size_t)StreamStages<NT>::value * kUnitBytes + 128 + work;
+    size_t work = std::max(product, attention);
+    if (fused) work = std::max(work, block_area_bytes(p.kpd, (int)sizeof(WT), p.max_positions));
+    return (work + 127) / 128 * 128;
 }
 
 template <typename WT, int NT>
-void launch_typed(const StepParams& p, int max_chunk, int grid, cudaStream_t stream) {
-    const size_t smem = shared_bytes<WT, NT>(p, max_chunk);
+size_t shared_bytes(const StepParams& p, int max_chunk, bool fused) {
+    return (size_t)p.stages * p.stage_bytes + 8 * kMaxStages + work_bytes<WT, NT>(p, max_chunk, fused);
+}
+
+template <typename WT, int NT>
+void launch_typed(const StepParams& p, int max_chunk, bool fused, int grid, cudaStream_t stream) {
+    const size_t smem = shared_bytes<WT, NT>(p, max_chunk, fused);
     auto kernel = decode_kernel<WT, NT>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) throw std::runtime_error(std::string("decode kernel shared memory: ") + cudaGetErrorString(e));
@@ -844,8 +1428,8 @@ void launch_typed(const StepParams& p, int max_chunk, int grid, cudaStream_t str
 }
 
 template <typename WT, int NT>
-int occupancy_typed(const StepParams& p, int max_chunk) {
-    const size_t smem = shared_bytes<WT, NT>(p, max_chunk);
+int occupancy_typed(const StepParams& p, int max_chunk, bool fused) {
+    const size_t smem = shared_bytes<WT, NT>(p, max_chunk, fused);
     auto kernel = decode_kernel<WT, NT>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
         cudaGetLastError();
@@ -866,34 +1450,50 @@ inline int tile_columns(const StepParams& p) {
 }
 
 template <typename WT>
-void launch_rows(const StepParams& p, int max_chunk, int grid, cudaStream_t stream) {
+void launch_rows(const StepParams& p, int max_chunk, bool fused, int grid, cudaStream_t stream) {
     switch (tile_columns(p)) {
-    case 1: launch_typed<WT, 1>(p, max_chunk, grid, stream); break;
-    case 2: launch_typed<WT, 2>(p, max_chunk, grid, stream); break;
-    default: launch_typed<WT, 4>(p, max_chunk, grid, stream); break;
+    case 1: launch_typed<WT, 1>(p, max_chunk, fused, grid, stream); break;
+    case 2: launch_typed<WT, 2>(p, max_chunk, fused, grid, stream); break;
+    default: launch_typed<WT, 4>(p, max_chunk, fused, grid, stream); break;
     }
 }
 
 template <typename WT>
-int occupancy_rows(const StepParams& p, int max_chunk) {
+int occupancy_rows(const StepParams& p, int max_chunk, bool fused) {
     switch (tile_columns(p)) {
-    case 1: return occupancy_typed<WT, 1>(p, max_chunk);
-    case 2: return occupancy_typed<WT, 2>(p, max_chunk);
-    default: return occupancy_typed<WT, 4>(p, max_chunk);
+    case 1: return occupancy_typed<WT, 1>(p, max_chunk, fused);
+    case 2: return occupancy_typed<WT, 2>(p, max_chunk, fused);
+    default: return occupancy_typed<WT, 4>(p, max_chunk, fused);
+    }
+}
+
+template <typename WT>
+size_t work_rows(const StepParams& p, int max_chunk, bool fused) {
+    switch (tile_columns(p)) {
+    case 1: return work_bytes<WT, 1>(p, max_chunk, fused);
+    case 2: return work_bytes<WT, 2>(p, max_chunk, fused);
+    default: return work_bytes<WT, 4>(p, max_chunk, fused);
     }
 }
 
 }  // namespace
 
-int decode_blocks_per_sm(bool half, const StepParams& p, int max_chunk) {
-    return half ? occupancy_rows<__half>(p, max_chunk) : occupancy_rows<__nv_bfloat16>(p, max_chunk);
+size_t decode_work_bytes(bool half, const StepParams& p, int max_chunk, bool fused) {
+    return (half ? work_rows<__half>(p, max_chunk, fused) : work_rows<__nv_bfloat16>(p, max_chunk, fused)) +
+           8 * kMaxStages;
 }
 
-void launch_decode(bool half, const StepParams& p, int max_chunk, int grid, cudaStream_t stream) {
+int decode_blocks_per_sm(bool half, const StepParams& p, int max_chunk, bool fused) {
+    return half ? occupancy_rows<__half>(p, max_chunk, fused) : occupancy_rows<__nv_bfloat16>(p, max_chunk, fused);
+}
+
+void launch_decode(bool half, const StepParams& p, int max_chunk, bool fused, int grid, cudaStream_t stream) {
     if (p.width > 32 * kNormMaxPerLane) throw std::invalid_argument("widths above 1536 are not supported");
     if (p.head_width > 64) throw std::invalid_argument("heads wider than 64 are not supported");
-    if (half) launch_rows<__half>(p, max_chunk, grid, stream);
-    else launch_rows<__nv_bfloat16>(p, max_chunk, grid, stream);
+    if (p.stages < 1 || p.stages > kMaxStages || p.stage_bytes % 1024 != 0)
+        throw std::invalid_argument("weight stream stages out of range");
+    if (half) launch_rows<__half>(p, max_chunk, fused, grid, stream);
+    else launch_rows<__nv_bfloat16>(p, max_chunk, fused, grid, stream);
 }
 
 }  // namespace wsp

@@ -228,6 +228,12 @@ class Decoder:
         check(self._lib.wsp_decoder_step_launches(self._handle, ctypes.byref(value)))
         return value.value
 
+    def time_barriers(self, count: int = 40) -> float:
+        """Mean microseconds of one grid barrier of the decode kernel."""
+        value = ctypes.c_float()
+        check(self._lib.wsp_decoder_time_barriers(self._handle, count, ctypes.byref(value)))
+        return value.value
+
     def time_kernels(self, steps: int) -> dict[str, tuple[float, int]]:
         """Mean ms per launch and launches per step of each kernel class."""
         ms = (ctypes.c_float * len(KERNEL_CLASSES))()
