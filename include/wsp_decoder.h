@@ -198,6 +198,14 @@ int wsp_decoder_time_kernels(wsp_decoder* decoder, int steps, float* ms, int* la
  */
 int wsp_decoder_time_barriers(wsp_decoder* decoder, int count, float* microseconds);
 
+/*
+ * Clock cycles per step that CTA 0 of the decode kernel spent in each section
+ * (waiting for weights, products, stage releases, epilogues, layer norms,
+ * attention, issuing copies), averaged over the last wsp_decoder_time_kernels
+ * run; `count` entries (7 are defined).
+ */
+int wsp_decoder_trace_cycles(const wsp_decoder* decoder, double* cycles, int count);
+
 /* Kernel launches of this library per transcription (wsp_decoder_transcribe). */
 int wsp_decoder_step_launches(const wsp_decoder* decoder, int* launches);
 

@@ -22,6 +22,8 @@ WSP_FLOAT32 = 0
 WSP_FLOAT16 = 1
 WSP_BFLOAT16 = 2
 
+TRACE_SECTIONS = ("wait", "compute", "release", "epilogue", "norm", "attention", "issue")
+
 KERNEL_CLASSES = ("embed", "layer_norm", "projection", "self_attention", "cross_attention",
                   "attention_combine", "logits_argmax", "argmax_final", "other")
 
@@ -77,6 +79,7 @@ SIGNATURES = {
     "wsp_decoder_synchronize": ([_P], _I),
     "wsp_decoder_time_kernels": ([_P, _I, _P, _P], _I),
     "wsp_decoder_time_barriers": ([_P, _I, ctypes.POINTER(ctypes.c_float)], _I),
+    "wsp_decoder_trace_cycles": ([_P, ctypes.POINTER(ctypes.c_double), _I], _I),
     "wsp_decoder_step_launches": ([_P, ctypes.POINTER(_I)], _I),
     "wsp_argmax": ([_P, _P, _P, _I, _I, _P], _I),
 }

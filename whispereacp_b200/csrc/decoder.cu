@@ -7,6 +7,7 @@
 //   greedy search                                      Lib/WhisperEACP/Whisper/Whisper.cpp:148-254,1158-1449
 #include "../../include/wsp_decoder.h"
 #include "kernels.cuh"
+#include "schedule.h"
 #include "step_launch.h"
 
 #include <cublas_v2.h>
@@ -502,14 +503,21 @@ public:
         std::vector<double> total(WSP_KERNEL_CLASSES, 0.0);
         std::vector<int> count(WSP_KERNEL_CLASSES, 0);
         std::vector<unsigned long long> stamps;
+        std::vector<unsigned long long> sections(kTraceSections, 0);
+        trace_cycles_.assign(kTraceSections, 0.0);
         for (int i = 0; i < steps; ++i) {
+            CUDA_CHECK(cudaMemsetAsync(profile_.get<unsigned long long>() + kTraceOffset, 0,
+                                       kTraceSections * sizeof(unsigned long long), stream_));
             const std::vector<StepOp>& ops = launch_steps(1, true, masks_.get<float>() + shape_.vocabulary_size,
                                                           nullptr, nullptr, nullptr, 1, false,
                                                           profile_.get<unsigned long long>());
             stamps.resize(ops.size() + 1);
             CUDA_CHECK(cudaMemcpyAsync(stamps.data(), profile_.get(), stamps.size() * 8, cudaMemcpyDeviceToHost,
                                        stream_));
+            CUDA_CHECK(cudaMemcpyAsync(sections.data(), profile_.get<unsigned long long>() + kTraceOffset,
+                                       kTraceSections * sizeof(unsigned long long), cudaMemcpyDeviceToHost, stream_));
             CUDA_CHECK(cudaStreamSynchronize(stream_));
+            for (int t = 0; t < kTraceSections; ++t) trace_cycles_[t] += (double)sections[t] / steps;
             for (size_t o = 0; o < ops.size(); ++o) {
                 const int cls = op_class(ops[o].kind);
                 total[cls] += (stamps[o + 1] - stamps[o]) * 1e-6;
@@ -542,6 +550,7 @@ public:
         configure_stream(half, p, false);
         const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk, false);
         if (blocks <= 0) throw CudaFailure("the decode kernel does not fit on an SM", false);
+        upload_schedule(p, ops, sm_count_ * std::min(blocks, kMaxBlocksPerSm));
         CUDA_CHECK(cudaMemsetAsync(state_.get<int>() + kAbort, 0, 2 * sizeof(int), stream_));
         CUDA_CHECK(cudaMemsetAsync(barrier_.get(), 0, barrier_.bytes(), stream_));
         launch_decode(half, p, kMaxCrossChunk, false, sm_count_ * std::min(blocks, kMaxBlocksPerSm), stream_);
@@ -551,6 +560,11 @@ public:
         check_device_errors();
         // The first barrier also absorbs the launch's start-up skew.
         return count > 1 ? (float)((stamps[count] - stamps[1]) * 1e-3 / (count - 1)) : 0.f;
+    }
+
+    // Section cycles of CTA 0 per step, from the last time_kernels run.
+    void trace_cycles(double* out, int count) const {
+        for (int i = 0; i < count; ++i) out[i] = i < (int)trace_cycles_.size() ? trace_cycles_[i] : 0.0;
     }
 
     // Kernel launches of this library per transcription: the encoder-row
@@ -636,7 +650,7 @@ private:
         state_.allocate(kStateWords * sizeof(int));
         barrier_.allocate(64);
         ended_.allocate((size_t)windows_);
-        profile_.allocate((size_t)(8 * shape_.layers + 8) * sizeof(unsigned long long));
+        profile_.allocate(1024 * sizeof(unsigned long long));
         masks_.allocate(2 * (size_t)shape_.vocabulary_size * 4);
     }
 
@@ -811,7 +825,7 @@ private:
         const int r_tiles = (windows_ + 7) / 8;
         const int stage_chunks = stage_bytes / 1024;
         // Enough (head, rows, split) items for the grid; chunks of 32..512 keys.
-        int splits = (grid + H * r_tiles - 1) / (H * r_tiles);
+        int splits = grid / (H * r_tiles);
         splits = std::min(splits, std::max(1, (active_cross_ + 31) / 32));
         splits = std::max({1, splits, (active_cross_ + kWarpKeyLimit - 1) / kWarpKeyLimit});
         const int chunk = (active_cross_ + splits - 1) / splits;
@@ -875,6 +889,20 @@ private:
         logits.kind = kOpLogits;
         ops.push_back(logits);
         return ops;
+    }
+
+    // The weight-stream schedule of every CTA (schedule.h), into device memory.
+    void upload_schedule(StepParams& p, const std::vector<StepOp>& ops, int grid) {
+        build_schedule(p, ops, grid, decode_tile_rows(p), schedule_host_, offsets_host_);
+        if (schedule_host_.empty()) schedule_host_.push_back(0);
+        if (schedule_dev_.bytes() < schedule_host_.size() * 8) schedule_dev_.allocate(schedule_host_.size() * 8 * 2);
+        if (offsets_dev_.bytes() < offsets_host_.size() * 4) offsets_dev_.allocate(offsets_host_.size() * 4 * 2);
+        CUDA_CHECK(cudaMemcpyAsync(schedule_dev_.get(), schedule_host_.data(), schedule_host_.size() * 8,
+                                   cudaMemcpyHostToDevice, stream_));
+        CUDA_CHECK(cudaMemcpyAsync(offsets_dev_.get(), offsets_host_.data(), offsets_host_.size() * 4,
+                                   cudaMemcpyHostToDevice, stream_));
+        p.schedule = schedule_dev_.get<unsigned long long>();
+        p.schedule_offsets = offsets_dev_.get<unsigned>();
     }
 
     // Stage size: one 16-row tile over kpd (at least 16 KB); as many stages
@@ -963,6 +991,7 @@ private:
                                    stream_));
         p.ops = ops_dev.get<StepOp>();
         p.n_ops = (int)ops.size();
+        upload_schedule(p, ops, grid);
         // The abort and steps-done words; the all-ended flag survives from
         // the prompt step to the steps after it.
         CUDA_CHECK(cudaMemsetAsync(state_.get<int>() + kAbort, 0, 2 * sizeof(int), stream_));
@@ -1107,6 +1136,9 @@ private:
     DeviceBuffer barrier_, ended_, profile_;
     DeviceBuffer logits_staging_, hidden_staging_;
     DeviceBuffer ops_prompt_dev_, ops_step_dev_, ops_teacher_dev_, ops_probe_dev_;
+    DeviceBuffer schedule_dev_, offsets_dev_;
+    std::vector<unsigned long long> schedule_host_;
+    std::vector<unsigned> offsets_host_;
     std::vector<StepOp> ops_prompt_, ops_step_, ops_teacher_;
 
     int token_capacity_ = 0;
@@ -1121,6 +1153,9 @@ private:
     bool stop_at_end_of_text_ = true;
     bool generation_set_ = false;
     int sampled_steps_ = 0;
+    std::vector<double> trace_cycles_;
+    static constexpr int kTraceOffset = 512;   // kTraceBase of step.cu
+    static constexpr int kTraceSections = 7;
     int queued_steps_ = 0;
 };
 
@@ -1292,6 +1327,14 @@ int wsp_decoder_time_barriers(wsp_decoder* decoder, int count, float* microsecon
         WSP_NEED(decoder);
         if (!microseconds) throw wsp::InvalidArgument("microseconds is NULL");
         *microseconds = decoder->impl->time_barriers(count);
+    });
+}
+
+int wsp_decoder_trace_cycles(const wsp_decoder* decoder, double* cycles, int count) {
+    return guarded([&] {
+        WSP_NEED(decoder);
+        if (!cycles || count < 0) throw wsp::InvalidArgument("cycles is NULL");
+        decoder->impl->trace_cycles(cycles, count);
     });
 }
 

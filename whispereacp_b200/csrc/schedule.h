@@ -1,0 +1,130 @@
+// The weight-stream schedule of a decode-kernel launch: for every CTA, the
+// units of weights it streams through its shared-memory ring in one step, in
+// the order its ops consume them.  Built on the host once per op list; the
+// kernel's thread 0 only walks it.
+#pragma once
+
+#include "step.cuh"
+
+#include <algorithm>
+#include <vector>
+
+namespace wsp {
+
+// A run of `tiles` contiguous 16-row tiles of `chunks` 1 KB chunks.  A stream
+// unit is `group` whole tiles, or -- for a tile larger than a stage -- a
+// k-block of one tile.
+struct Region {
+    const unsigned char* base;
+    int tiles, chunks, group;
+};
+
+inline int schedule_row_tiles(int rows, int rt) { return (rows + rt - 1) / rt; }
+inline int schedule_round16(int n) { return (n + 15) / 16 * 16; }
+
+// Items of an op; CTA c takes items c, c + grid, ...  rt: input rows of a
+// general product's tile (8 * NT of the launch); fused blocks take 8.
+inline int op_items(const StepParams& p, const StepOp& op, int rt) {
+    switch (op.kind) {
+    case kOpProduct: return ((op.n + 15) / 16) * schedule_row_tiles(p.rows, rt);
+    case kOpLogits: return ((p.vocabulary + 15) / 16) * schedule_row_tiles(p.out_rows, rt);
+    case kOpSelfBlock: return p.heads * schedule_row_tiles(p.rows, 8);
+    case kOpCrossBlock: return p.heads * schedule_row_tiles(p.rows, 8) * op.splits;
+    case kOpFeedForwardBlock: return (p.ffn / op.slice) * schedule_row_tiles(p.rows, 8);
+    }
+    return 0;
+}
+
+// Weight region `region` of item `item` of an op; false when there is none.
+inline bool item_region(const StepParams& p, const StepOp& op, int item, int region, Region& out) {
+    const int chunks_d = p.kpd / 32;
+    switch (op.kind) {
+    case kOpProduct:
+    case kOpLogits: {
+        if (region != 0) return false;
+        const int n = op.kind == kOpProduct ? op.n : p.vocabulary;
+        const int kp = op.kind == kOpProduct ? op.kp : p.kpd;
+        const void* w = op.kind == kOpProduct ? op.weight : p.token_table;
+        const int tile = item % ((n + 15) / 16);
+        out = Region{static_cast<const unsigned char*>(w) + (size_t)tile * (kp / 32) * 1024, 1, kp / 32, 1};
+        return true;
+    }
+    case kOpSelfBlock: {
+        const int head = item % p.heads;
+        if (region == 0) {
+            const int tiles = schedule_round16(3 * p.head_width) / 16;
+            out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)head * tiles * chunks_d * 1024, tiles,
+                         chunks_d, 1};
+            return true;
+        }
+        if (region == 1) {
+            out = Region{static_cast<const unsigned char*>(op.weight2) + (size_t)head * op.item_stride2,
+                         schedule_round16(p.width) / 16, op.kp2 / 32, op.group2};
+            return true;
+        }
+        return false;
+    }
+    case kOpCrossBlock: {
+        if (region != 0) return false;
+        const int head = (item / op.splits) % p.heads;
+        const int tiles = schedule_round16(p.head_width) / 16;
+        out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)head * tiles * chunks_d * 1024, tiles,
+                     chunks_d, 1};
+        return true;
+    }
+    case kOpFeedForwardBlock: {
+        const int chunk = item % (p.ffn / op.slice);
+        if (region == 0) {
+            const int tiles = op.slice / 16;
+            out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)chunk * tiles * chunks_d * 1024, tiles,
+                         chunks_d, 1};
+            return true;
+        }
+        if (region == 1) {
+            out = Region{static_cast<const unsigned char*>(op.weight2) + (size_t)chunk * op.item_stride2,
+                         schedule_round16(p.width) / 16, op.kp2 / 32, op.group2};
+            return true;
+        }
+        return false;
+    }
+    }
+    return false;
+}
+
+// Appends the units of a region: whole-tile groups, or k-blocks of a tile
+// larger than a stage.
+inline void append_region(const Region& r, int stage_chunks, std::vector<unsigned long long>& out) {
+    if (r.chunks > stage_chunks) {
+        const int blocks = (r.chunks + stage_chunks - 1) / stage_chunks;
+        for (int t = 0; t < r.tiles; ++t)
+            for (int b = 0; b < blocks; ++b) {
+                const unsigned bytes = (unsigned)std::min(stage_chunks, r.chunks - b * stage_chunks) * 1024u;
+                out.push_back(schedule_entry(r.base + ((size_t)t * r.chunks + (size_t)b * stage_chunks) * 1024, bytes));
+            }
+        return;
+    }
+    for (int t0 = 0; t0 < r.tiles; t0 += r.group) {
+        const unsigned bytes = (unsigned)(std::min(r.group, r.tiles - t0) * r.chunks) * 1024u;
+        out.push_back(schedule_entry(r.base + (size_t)t0 * r.chunks * 1024, bytes));
+    }
+}
+
+// The per-CTA schedules of a launch, concatenated, and their offsets.
+inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, int grid, int rt,
+                           std::vector<unsigned long long>& units, std::vector<unsigned>& offsets) {
+    const int stage_chunks = p.stage_bytes / 1024;
+    units.clear();
+    offsets.assign(1, 0u);
+    for (int cta = 0; cta < grid; ++cta) {
+        for (const StepOp& op : ops) {
+            const int items = op_items(p, op, rt);
+            for (int item = cta; item < items; item += grid) {
+                Region r;
+                for (int region = 0; item_region(p, op, item, region, r); ++region) append_region(r, stage_chunks, units);
+            }
+        }
+        offsets.push_back((unsigned)units.size());
+    }
+}
+
+}  // namespace wsp

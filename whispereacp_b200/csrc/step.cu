@@ -49,6 +49,30 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
+// Section timers for measurement: CTA 0, thread 0 accumulates clock64
+// cycles per section of a launch into profile[kTraceBase + section] when a
+// profile buffer is given.
+enum TraceSection : int { kTrWait = 0, kTrCompute, kTrRelease, kTrEpilogue, kTrNorm, kTrAttention, kTrIssue,
+                          kTrSections };
+constexpr int kTraceBase = 512;
+__device__ unsigned long long g_trace_dummy;
+
+struct Trace {
+    unsigned long long* out;
+    long long start;
+    __device__ __forceinline__ void begin() { if (out) start = clock64(); }
+    __device__ __forceinline__ void end(int section) {
+        if (out) out[kTraceBase + section] += (unsigned long long)(clock64() - start);
+    }
+};
+__device__ __forceinline__ Trace trace_of(const unsigned long long* profile) {
+    Trace t;
+    t.out = (profile != nullptr && blockIdx.x == 0 && threadIdx.x == 0) ? const_cast<unsigned long long*>(profile)
+                                                                           : nullptr;
+    t.start = 0;
+    return t;
+}
+
 template <typename WT>
 __device__ __forceinline__ float bits_to_float(unsigned short b) {
     return Half16<WT>::to_float(*reinterpret_cast<const WT*>(&b));
@@ -98,7 +122,8 @@ __device__ __forceinline__ uint32_t smem_address(const void* p) {
 }
 
 struct Cursor {
-    int step, op, item, region, unit;
+    int step;      // step of the next unit
+    unsigned at;   // index of the next unit within the CTA's schedule
 };
 
 struct Stream {
@@ -111,142 +136,26 @@ struct Stream {
     Cursor cursor;                // thread 0 only: the next unit to issue
 };
 
-// A run of `tiles` contiguous 16-row tiles of `chunks` 1 KB chunks.  A stream
-// unit is `group` whole tiles, or -- for a tile larger than a stage -- a
-// k-block of one tile.
-struct Region {
-    const unsigned char* base;
-    int tiles, chunks, group;
-};
-
 __device__ __forceinline__ int row_tiles(int rows, int rt) { return (rows + rt - 1) / rt; }
 __device__ __forceinline__ int round16(int n) { return (n + 15) / 16 * 16; }
 
-// Items of an op (each CTA takes items blockIdx.x, + gridDim.x, ...).
+// Thread 0: the next unit of this CTA's schedule, or false past the last step.
 template <int RT>
-__device__ int op_items(const StepParams& p, const StepOp& op) {
-    switch (op.kind) {
-    case kOpProduct: return ((op.n + 15) / 16) * row_tiles(p.rows, RT);
-    case kOpLogits: return ((p.vocabulary + 15) / 16) * row_tiles(p.out_rows, RT);
-    case kOpSelfBlock: return p.heads * row_tiles(p.rows, 8);
-    case kOpCrossBlock: return p.heads * row_tiles(p.rows, 8) * op.splits;
-    case kOpFeedForwardBlock: return (p.ffn / op.slice) * row_tiles(p.rows, 8);
+__device__ __forceinline__ bool next_unit(const StepParams& p, const Stream& s, Cursor& c, const unsigned char** src,
+                                          unsigned* bytes) {
+    const unsigned first = __ldg(p.schedule_offsets + blockIdx.x);
+    const unsigned count = __ldg(p.schedule_offsets + blockIdx.x + 1) - first;
+    if (count == 0) return false;
+    if (c.at == count) {
+        c.at = 0;
+        ++c.step;
     }
-    return 0;
-}
-
-// Weight region `region` of item `item` of an op; false when there is none.
-template <int RT>
-__device__ bool item_region(const StepParams& p, const StepOp& op, int item, int region, Region& out) {
-    const int chunks_d = p.kpd / 32;
-    switch (op.kind) {
-    case kOpProduct:
-    case kOpLogits: {
-        if (region != 0) return false;
-        const int n = op.kind == kOpProduct ? op.n : p.vocabulary;
-        const int kp = op.kind == kOpProduct ? op.kp : p.kpd;
-        const void* w = op.kind == kOpProduct ? op.weight : p.token_table;
-        const int tile = item % ((n + 15) / 16);
-        out = Region{static_cast<const unsigned char*>(w) + (size_t)tile * (kp / 32) * 1024, 1, kp / 32, 1};
-        return true;
-    }
-    case kOpSelfBlock: {
-        const int head = item % p.heads;
-        if (region == 0) {
-            const int tiles = round16(3 * p.head_width) / 16;
-            out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)head * tiles * chunks_d * 1024, tiles,
-                         chunks_d, 1};
-            return true;
-        }
-        if (region == 1) {
-            out = Region{static_cast<const unsigned char*>(op.weight2) + (size_t)head * op.item_stride2,
-                         round16(p.width) / 16, op.kp2 / 32, op.group2};
-            return true;
-        }
-        return false;
-    }
-    case kOpCrossBlock: {
-        if (region != 0) return false;
-        const int head = (item / op.splits) % p.heads;
-        const int tiles = round16(p.head_width) / 16;
-        out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)head * tiles * chunks_d * 1024, tiles,
-                     chunks_d, 1};
-        return true;
-    }
-    case kOpFeedForwardBlock: {
-        const int chunk = item % (p.ffn / op.slice);
-        if (region == 0) {
-            const int tiles = op.slice / 16;
-            out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)chunk * tiles * chunks_d * 1024, tiles,
-                         chunks_d, 1};
-            return true;
-        }
-        if (region == 1) {
-            out = Region{static_cast<const unsigned char*>(op.weight2) + (size_t)chunk * op.item_stride2,
-                         round16(p.width) / 16, op.kp2 / 32, op.group2};
-            return true;
-        }
-        return false;
-    }
-    }
-    return false;
-}
-
-// Units of a region, and the bytes and source of unit u.
-__device__ __forceinline__ int region_units(const Region& r, int stage_chunks) {
-    if (r.chunks > stage_chunks) return r.tiles * ((r.chunks + stage_chunks - 1) / stage_chunks);
-    return (r.tiles + r.group - 1) / r.group;
-}
-__device__ __forceinline__ const unsigned char* region_unit(const Region& r, int u, int stage_chunks, unsigned* bytes) {
-    if (r.chunks > stage_chunks) {
-        const int blocks = (r.chunks + stage_chunks - 1) / stage_chunks;
-        const int tile = u / blocks, block = u % blocks;
-        *bytes = (unsigned)min(stage_chunks, r.chunks - block * stage_chunks) * 1024u;
-        return r.base + ((size_t)tile * r.chunks + (size_t)block * stage_chunks) * 1024;
-    }
-    const int t0 = u * r.group;
-    *bytes = (unsigned)(min(r.group, r.tiles - t0) * r.chunks) * 1024u;
-    return r.base + (size_t)t0 * r.chunks * 1024;
-}
-
-// Thread 0: the next unit of this CTA's sequence, or false past the last step.
-template <int RT>
-__device__ bool next_unit(const StepParams& p, const Stream& s, Cursor& c, const unsigned char** src,
-                          unsigned* bytes) {
-    const int stage_chunks = s.stage_bytes / 1024;
-    while (c.step < p.steps) {
-        if (c.op >= p.n_ops) {
-            c.op = 0;
-            c.item = blockIdx.x;
-            c.region = 0;
-            c.unit = 0;
-            ++c.step;
-            continue;
-        }
-        const StepOp& op = p.ops[c.op];
-        if (c.item < op_items<RT>(p, op)) {
-            Region r;
-            if (item_region<RT>(p, op, c.item, c.region, r)) {
-                if (c.unit < region_units(r, stage_chunks)) {
-                    *src = region_unit(r, c.unit, stage_chunks, bytes);
-                    ++c.unit;
-                    return true;
-                }
-                ++c.region;
-                c.unit = 0;
-                continue;
-            }
-            c.item += gridDim.x;
-            c.region = 0;
-            c.unit = 0;
-            continue;
-        }
-        ++c.op;
-        c.item = blockIdx.x;
-        c.region = 0;
-        c.unit = 0;
-    }
-    return false;
+    if (c.step >= p.steps) return false;
+    const unsigned long long e = __ldg(p.schedule + first + c.at);
+    ++c.at;
+    *src = reinterpret_cast<const unsigned char*>((size_t)(e & ~1023ull));
+    *bytes = ((unsigned)(e & 1023u) + 1u) * 1024u;
+    return true;
 }
 
 // Thread 0: fills every free stage.
@@ -271,8 +180,8 @@ __device__ void issue_ahead(const StepParams& p, Stream& s) {
 __device__ bool wait_unit(const StepParams& p, const Stream& s, unsigned long long index) {
     const uint32_t bar = smem_address(s.full + (int)(index % s.stages));
     const uint32_t parity = (uint32_t)((index / s.stages) & 1);
-    const unsigned long long start = global_ns();
-    while (true) {
+    unsigned long long start = 0;
+    for (int attempt = 0;; ++attempt) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred P;\n\t"
@@ -282,7 +191,8 @@ __device__ bool wait_unit(const StepParams& p, const Stream& s, unsigned long lo
             : "r"(bar), "r"(parity)
             : "memory");
         if (done) return true;
-        if (global_ns() - start > kWaitTimeoutNs) {
+        if (attempt == 0) start = global_ns();
+        else if (global_ns() - start > kWaitTimeoutNs) {
             atomicOr(p.state + kError, kErrBarrierTimeout);
             atomicExch(p.state + kAbort, 1);
             return false;
@@ -294,10 +204,25 @@ __device__ bool wait_unit(const StepParams& p, const Stream& s, unsigned long lo
 // every thread observes the completed phase.  nullptr if the wait gave up.
 __device__ const unsigned char* acquire_unit(const StepParams& p, const Stream& s) {
     __shared__ int gave_up;
+    Trace tr = trace_of(p.profile);
+    tr.begin();
     if (threadIdx.x == 0) gave_up = wait_unit(p, s, s.consumed) ? 0 : 1;
     __syncthreads();
+    tr.end(kTrWait);
     if (gave_up) return nullptr;
-    wait_unit(p, s, s.consumed);
+    if (threadIdx.x != 0) {
+        const uint32_t bar = smem_address(s.full + (int)(s.consumed % s.stages));
+        const uint32_t parity = (uint32_t)((s.consumed / s.stages) & 1);
+        uint32_t done = 0;
+        while (!done)
+            asm volatile(
+                "{\n\t.reg .pred P;\n\t"
+                "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+                "selp.u32 %0, 1, 0, P;\n\t}\n"
+                : "=r"(done)
+                : "r"(bar), "r"(parity)
+                : "memory");
+    }
     return s.ring + (size_t)(s.consumed % s.stages) * s.stage_bytes;
 }
 
@@ -305,9 +230,14 @@ __device__ const unsigned char* acquire_unit(const StepParams& p, const Stream& 
 // now refill.
 template <int RT>
 __device__ __forceinline__ void release_unit(const StepParams& p, Stream& s) {
+    Trace tr = trace_of(p.profile);
+    tr.begin();
     __syncthreads();
+    tr.end(kTrRelease);
     ++s.consumed;
+    tr.begin();
     if (threadIdx.x == 0) issue_ahead<RT>(p, s);
+    tr.end(kTrIssue);
 }
 
 // -------------------------------------------------------------------- embed
@@ -343,8 +273,50 @@ template <typename WT>
 __device__ void layer_norm_tile(const StepParams& p, const float* input, const float* gamma, const float* beta,
                                 int r0, int rows_in_tile, int row_step, int row_offset, WT* xs, int ldx,
                                 float* hidden_out) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int d = p.width;
+    if (rows_in_tile <= 2) {
+        // A row or two: the whole CTA on each row, every load of the row,
+        // the gains and the offsets in flight at once.
+        __shared__ float scratch[kWarps];
+        constexpr int kPer = 6;  // 1536 / 256
+        for (int rl = 0; rl < rows_in_tile; ++rl) {
+            const float* x = input + ((size_t)(r0 + rl) * row_step + row_offset) * d;
+            float v[kPer], g[kPer], b[kPer];
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int c = threadIdx.x + i * kThreads;
+                v[i] = c < d ? ld_cg(x + c) : 0.f;
+                g[i] = c < d ? __ldg(gamma + c) : 0.f;
+                b[i] = c < d ? __ldg(beta + c) : 0.f;
+            }
+            float total = 0.f;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) total += v[i];
+            const float mean = block_sum(total, scratch) / (float)d;
+            float centred = 0.f;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int c = threadIdx.x + i * kThreads;
+                const float dv = c < d ? v[i] - mean : 0.f;
+                centred += dv * dv;
+            }
+            const float scale = rsqrtf(block_sum(centred, scratch) / (float)d + 1e-5f);
+            WT* out = xs + (size_t)rl * ldx;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int c = threadIdx.x + i * kThreads;
+                if (c < d) {
+                    const float y = (v[i] - mean) * scale * g[i] + b[i];
+                    out[c] = Half16<WT>::from_float(y);
+                    if (hidden_out) hidden_out[(size_t)(r0 + rl) * d + c] = y;
+                }
+            }
+            for (int c = d + threadIdx.x; c < ldx; c += kThreads) out[c] = Half16<WT>::from_float(0.f);
+        }
+        return;
+    }
+    // More rows: one warp a row, the row in registers.
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int rl = warp; rl < rows_in_tile; rl += kWarps) {
         const float* x = input + ((size_t)(r0 + rl) * row_step + row_offset) * d;
         float v[kNormMaxPerLane];
@@ -365,14 +337,20 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
             centred += dv * dv;
         }
         const float scale = rsqrtf(warp_sum(centred) / (float)d + 1e-5f);
+        // The gains and offsets are loaded in a loop with no stores, so they
+        // can all be in flight together; the stores follow.
+#pragma unroll
+        for (int i = 0; i < kNormMaxPerLane; ++i) {
+            const int c = lane + 32 * i;
+            if (c < d) v[i] = (v[i] - mean) * scale * __ldg(gamma + c) + __ldg(beta + c);
+        }
         WT* out = xs + (size_t)rl * ldx;
 #pragma unroll
         for (int i = 0; i < kNormMaxPerLane; ++i) {
             const int c = lane + 32 * i;
             if (c < d) {
-                const float y = (v[i] - mean) * scale * __ldg(gamma + c) + __ldg(beta + c);
-                out[c] = Half16<WT>::from_float(y);
-                if (hidden_out) hidden_out[(size_t)(r0 + rl) * d + c] = y;
+                out[c] = Half16<WT>::from_float(v[i]);
+                if (hidden_out) hidden_out[(size_t)(r0 + rl) * d + c] = v[i];
             } else if (c < ldx) {
                 out[c] = Half16<WT>::from_float(0.f);
             }
@@ -438,8 +416,11 @@ __device__ bool product_tile(const StepParams& p, Stream& s, int kp, const WT* X
         const int n = min(stage_chunks, chunks - c0);
         const unsigned char* unit = acquire_unit(p, s);
         if (!unit) return false;
+        Trace tr = trace_of(p.profile);
+        tr.begin();
         for (int c = warp; c < n; c += kWarps)
             product_chunk<WT, NT, X_SHARED>(unit, c, X, ldx, (c0 + c) * 32, x_ok, acc);
+        tr.end(kTrCompute);
         release_unit<RT>(p, s);
     }
     return true;
@@ -491,8 +472,11 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
         if (normalise) {
             if (cached_tile != r_tile) {
                 __syncthreads();
+                Trace trn = trace_of(p.profile);
+                trn.begin();
                 layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, xs, pitch, nullptr);
                 __syncthreads();
+                trn.end(kTrNorm);
                 cached_tile = r_tile;
             }
             ok = product_tile<WT, NT, true>(p, s, op.kp, xs, pitch, rows_valid, acc);
@@ -563,8 +547,8 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
     const int pitch = tile_pitch(p.kpd);
     WT* xs = reinterpret_cast<WT*>(work);
     float* red = reinterpret_cast<float*>(work + (size_t)RT * pitch * sizeof(WT));
-    float* tile = red + kWarps * 16 * RT;
-    float* best_v = tile + 16 * RT;
+    float* tile = red + kWarps * 16 * RT;  // [16][RT] values, then [16][RT] indices
+    float* best_v = tile + 2 * 16 * RT;
     uint32_t* best_i = reinterpret_cast<uint32_t*>(best_v + p.out_rows);
     __shared__ int is_last;
 
@@ -575,6 +559,36 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
     const int n_tiles = (p.vocabulary + 15) / 16;
     const int r_tiles = (p.out_rows + RT - 1) / RT;
     int cached_tile = -1;
+    // Thread o < 16*RT keeps, for input row o % RT of the current row tile,
+    // the first maximum over column o / RT of every tile it has seen.
+    const bool owner = threadIdx.x < 16 * RT;
+    const int my_nl = threadIdx.x / RT, my_rl = threadIdx.x % RT;
+    float cand_v = -INFINITY;
+    uint32_t cand_i = kUnchosen;
+    int cand_r0 = 0, cand_rows = 0;
+    // Folds the owners' candidates of a row tile into best_v/best_i.
+    auto flush = [&]() {
+        __syncthreads();
+        if (owner) {
+            tile[my_nl * RT + my_rl] = cand_v;
+            reinterpret_cast<uint32_t*>(tile + 16 * RT)[my_nl * RT + my_rl] = cand_i;
+        }
+        __syncthreads();
+        for (int rl = threadIdx.x; rl < cand_rows; rl += kThreads) {
+            float bv = best_v[cand_r0 + rl];
+            uint32_t bi = best_i[cand_r0 + rl];
+            for (int nl = 0; nl < 16; ++nl) {
+                const float v = tile[nl * RT + rl];
+                const uint32_t i = reinterpret_cast<const uint32_t*>(tile + 16 * RT)[nl * RT + rl];
+                if (candidate_better(v, i, bv, bi)) { bv = v; bi = i; }
+            }
+            best_v[cand_r0 + rl] = bv;
+            best_i[cand_r0 + rl] = bi;
+        }
+        __syncthreads();
+        cand_v = -INFINITY;
+        cand_i = kUnchosen;
+    };
     __syncthreads();
 
     for (int item = blockIdx.x; item < n_tiles * r_tiles; item += gridDim.x) {
@@ -582,39 +596,39 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
         const int r0 = r_tile * RT, n0 = n_tile * 16;
         const int rows_valid = min(RT, p.out_rows - r0);
         if (cached_tile != r_tile) {
+            if (cached_tile >= 0) flush();
             __syncthreads();
+            Trace trn = trace_of(p.profile);
+            trn.begin();
             layer_norm_tile<WT>(p, p.h, p.final_gamma, p.final_beta, r0, rows_valid, p.row_step, p.row_offset, xs, pitch,
                                 p.hidden_out);
             __syncthreads();
+            trn.end(kTrNorm);
             cached_tile = r_tile;
+            cand_r0 = r0;
+            cand_rows = rows_valid;
         }
         float acc[NT][4];
         if (!product_tile<WT, NT, true>(p, s, p.kpd, xs, pitch, rows_valid, acc)) return;
+        Trace tre = trace_of(p.profile);
+        tre.begin();
         product_reduce<NT>(red, acc);
-        for (int o = threadIdx.x; o < 16 * RT; o += kThreads) {
-            const int nl = o / RT, rl = o % RT;
-            const float v = product_sum(red, RT, nl, rl);
-            tile[nl * RT + rl] = v;
-            const int n = n0 + nl;
-            if (p.logits_out && n < p.vocabulary && rl < rows_valid)
-                p.logits_out[(size_t)(r0 + rl) * p.vocabulary + n] = v;
-        }
-        __syncthreads();
-        for (int rl = threadIdx.x; rl < rows_valid; rl += kThreads) {
-            float bv = best_v[r0 + rl];
-            uint32_t bi = best_i[r0 + rl];
-            for (int nl = 0; nl < 16; ++nl) {
-                const int n = n0 + nl;
-                if (n >= p.vocabulary) break;
-                if (p.mask && p.mask[n] != 0.f) continue;
-                const float v = tile[nl * RT + rl];
-                if (candidate_better(v, (uint32_t)n, bv, bi)) { bv = v; bi = (uint32_t)n; }
+        if (owner) {
+            const int n = n0 + my_nl;
+            const float v = product_sum(red, RT, my_nl, my_rl);
+            if (n < p.vocabulary && my_rl < rows_valid) {
+                if (p.logits_out) p.logits_out[(size_t)(r0 + my_rl) * p.vocabulary + n] = v;
+                const bool allowed = p.mask == nullptr || __ldg(p.mask + n) == 0.f;
+                if (allowed && candidate_better(v, (uint32_t)n, cand_v, cand_i)) {
+                    cand_v = v;
+                    cand_i = (uint32_t)n;
+                }
             }
-            best_v[r0 + rl] = bv;
-            best_i[r0 + rl] = bi;
         }
         __syncthreads();
+        tre.end(kTrEpilogue);
     }
+    if (cached_tile >= 0) flush();
 
     // This CTA's candidates, then the fold by whichever CTA finishes last.
     for (int r = threadIdx.x; r < p.out_rows; r += kThreads) {
@@ -742,7 +756,7 @@ __device__ __forceinline__ void attention_values(const float* scores, const WT* 
         const int piece = threadIdx.x % pieces, g = threadIdx.x / pieces;
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         if (g < groups) {
-#pragma unroll 4
+#pragma unroll 8
             for (int j = g; j < n; j += groups) {
                 const uint4 u = load_kv4<WT, READ_ONLY>(V + (size_t)(k0 + j) * key_stride + piece * 8);
                 const float w = scores[j];
@@ -1006,11 +1020,16 @@ __device__ bool split_product(const StepParams& p, Stream& s, int tiles, const B
         if (t < tiles) {
             const unsigned char* unit = acquire_unit(p, s);
             if (!unit) return false;
+            Trace tr = trace_of(p.profile);
+            tr.begin();
             for (int c = warp; c < chunks; c += kWarps)
                 product_chunk<WT, 1, true>(unit, c, A.xs, A.pitch, c * 32, x_ok, acc[t]);
+            tr.end(kTrCompute);
             release_unit<8 * NT>(p, s);
         }
     }
+    Trace tr = trace_of(p.profile);
+    tr.begin();
 #pragma unroll
     for (int t = 0; t < kMaxSplitTiles; ++t) {
         if (t < tiles) {
@@ -1030,6 +1049,7 @@ __device__ bool split_product(const StepParams& p, Stream& s, int tiles, const B
         A.res[o] = v;
     }
     __syncthreads();
+    tr.end(kTrEpilogue);
     return true;
 }
 
@@ -1046,6 +1066,8 @@ __device__ bool tiled_product(const StepParams& p, Stream& s, int tiles, int chu
         const int nt = min(group, tiles - t0);
         const unsigned char* unit = acquire_unit(p, s);
         if (!unit) return false;
+        Trace tr = trace_of(p.profile);
+        tr.begin();
         for (int tl = warp; tl < nt; tl += kWarps) {
             float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
             const unsigned char* tile = unit + (size_t)tl * chunks * 1024;
@@ -1056,6 +1078,7 @@ __device__ bool tiled_product(const StepParams& p, Stream& s, int tiles, int chu
             emit(n + 8, rl, acc[0][2]);
             emit(n + 8, rl + 1, acc[0][3]);
         }
+        tr.end(kTrCompute);
         release_unit<8 * NT>(p, s);
     }
     return true;
@@ -1120,8 +1143,11 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
         const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
         if (cached != r_tile) {
             __syncthreads();
+            Trace trn = trace_of(p.profile);
+            trn.begin();
             layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
             __syncthreads();
+            trn.end(kTrNorm);
             cached = r_tile;
         }
         if (!split_product<WT, NT>(p, s, group / 16, A, rows_valid)) return;
@@ -1141,6 +1167,8 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
         }
         __syncthreads();
         const int keys = position + 1;
+        Trace tra = trace_of(p.profile);
+        tra.begin();
         if (rows_valid <= 2) {
             for (int rl = 0; rl < rows_valid; ++rl) {
                 const size_t base = (size_t)(r0 + rl) * p.max_positions * d + (size_t)head * D;
@@ -1166,6 +1194,7 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
             }
             __syncthreads();
         }
+        tra.end(kTrAttention);
         // X1 += the head's slice of out_proj; head 0 adds the bias and X0.
         const bool first = head == 0;
         if (!tiled_product<WT, NT>(p, s, round16(d) / 16, op.kp2 / 32, op.group2, A.o16, ps, rows_valid,
@@ -1197,8 +1226,11 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
         const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
         if (cached != r_tile) {
             __syncthreads();
+            Trace trn = trace_of(p.profile);
+            trn.begin();
             layer_norm_tile<WT>(p, p.x1, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
             __syncthreads();
+            trn.end(kTrNorm);
             cached = r_tile;
         }
         if (!split_product<WT, NT>(p, s, group / 16, A, rows_valid)) return;
@@ -1209,6 +1241,8 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
         }
         __syncthreads();
         // This split's partial (max, sum, unnormalised row) of every row.
+        Trace tra = trace_of(p.profile);
+        tra.begin();
         const int k0 = split * op.chunk;
         const int n_keys = min(op.key_count, k0 + op.chunk) - k0;
         auto partial_of = [&](int rl) {
@@ -1252,6 +1286,7 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
         if (head == 0 && split == 0) zero_rows(p.h, r0, rows_valid, d);
         __threadfence();
         __syncthreads();
+        tra.end(kTrAttention);
         if (threadIdx.x == 0) {
             unsigned* counter = p.combine_counters + (size_t)r_tile * H + head;
             is_last = atomicAdd(counter, 1u) == (unsigned)(S - 1);
@@ -1284,6 +1319,8 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
         __syncthreads();
         // X2 += the head's slice of out_proj; head 0 adds the bias and X1.
         const bool first = head == 0;
+        Trace trd = trace_of(p.profile);
+        trd.begin();
         direct_tiled_product<WT>(static_cast<const unsigned char*>(op.weight2) + (size_t)head * op.item_stride2,
                                  round16(d) / 16, op.kp2 / 32, A.o16, ps, rows_valid, [&](int n, int rl, float v) {
                                      if (n >= d || rl >= rows_valid) return;
@@ -1292,6 +1329,7 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
                                      atomicAdd(p.x2 + at, v);
                                  });
         __syncthreads();
+        trd.end(kTrEpilogue);
     }
 }
 
@@ -1309,8 +1347,11 @@ __device__ void op_ffn_block(const StepParams& p, const StepOp& op, Stream& s, u
         const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
         if (cached != r_tile) {
             __syncthreads();
+            Trace trn = trace_of(p.profile);
+            trn.begin();
             layer_norm_tile<WT>(p, p.x2, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
             __syncthreads();
+            trn.end(kTrNorm);
             cached = r_tile;
         }
         if (!split_product<WT, NT>(p, s, FC / 16, A, rows_valid)) return;
@@ -1361,7 +1402,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(StepParams p) {
     unsigned char* work = smem + (size_t)s.stages * s.stage_bytes + 8 * kMaxStages;
     s.consumed = 0;
     s.issued = 0;
-    s.cursor = Cursor{0, 0, (int)blockIdx.x, 0, 0};
+    s.cursor = Cursor{0, 0u};
     if (threadIdx.x == 0) {
         for (int i = 0; i < s.stages; ++i)
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(s.full + i)) : "memory");
@@ -1403,7 +1444,7 @@ template <typename WT, int NT>
 size_t work_bytes(const StepParams& p, int max_chunk, bool fused) {
     constexpr int RT = 8 * NT;
     const size_t product = (size_t)RT * tile_pitch(p.kpd) * sizeof(WT) +
-                           sizeof(float) * (kWarps * 16 * RT + 16 * RT) + (size_t)p.out_rows * 8;
+                           sizeof(float) * (kWarps * 16 * RT + 2 * 16 * RT) + (size_t)p.out_rows * 8;
     const size_t attention = sizeof(float) * (kAttentionFixed + std::max(max_chunk, p.max_positions));
     size_t work = std::max(product, attention);
     if (fused) work = std::max(work, block_area_bytes(p.kpd, (int)sizeof(WT), p.max_positions));
@@ -1477,6 +1518,8 @@ size_t work_rows(const StepParams& p, int max_chunk, bool fused) {
 }
 
 }  // namespace
+
+int decode_tile_rows(const StepParams& p) { return 8 * tile_columns(p); }
 
 size_t decode_work_bytes(bool half, const StepParams& p, int max_chunk, bool fused) {
     return (half ? work_rows<__half>(p, max_chunk, fused) : work_rows<__nv_bfloat16>(p, max_chunk, fused)) +

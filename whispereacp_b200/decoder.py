@@ -23,8 +23,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._native import (CGeneration, CShape, KERNEL_CLASSES, LogicError, ModelError, WSP_BFLOAT16,
-                      WSP_FLOAT16, WSP_FLOAT32, check, library)
+from ._native import (CGeneration, CShape, KERNEL_CLASSES, TRACE_SECTIONS, LogicError, ModelError,
+                      WSP_BFLOAT16, WSP_FLOAT16, WSP_FLOAT32, check, library)
 
 __all__ = ["DecoderShape", "Decoder", "StepResult", "ModelError", "LogicError", "argmax",
            "STORAGE"]
@@ -233,6 +233,12 @@ class Decoder:
         value = ctypes.c_float()
         check(self._lib.wsp_decoder_time_barriers(self._handle, count, ctypes.byref(value)))
         return value.value
+
+    def trace_cycles(self) -> dict[str, float]:
+        """CTA 0's clock cycles per step in each section, from the last time_kernels."""
+        values = (ctypes.c_double * len(TRACE_SECTIONS))()
+        check(self._lib.wsp_decoder_trace_cycles(self._handle, values, len(TRACE_SECTIONS)))
+        return {name: values[i] for i, name in enumerate(TRACE_SECTIONS)}
 
     def time_kernels(self, steps: int) -> dict[str, tuple[float, int]]:
         """Mean ms per launch and launches per step of each kernel class."""
