@@ -894,15 +894,44 @@ private:
     // The weight-stream schedule of every CTA (schedule.h), into device memory.
     void upload_schedule(StepParams& p, const std::vector<StepOp>& ops, int grid) {
         build_schedule(p, ops, grid, decode_tile_rows(p), schedule_host_, offsets_host_);
-        if (schedule_host_.empty()) schedule_host_.push_back(0);
-        if (schedule_dev_.bytes() < schedule_host_.size() * 8) schedule_dev_.allocate(schedule_host_.size() * 8 * 2);
+        if (schedule_host_.empty()) schedule_host_.push_back(ScheduleEntry{0, 0});
+        const size_t entry = sizeof(ScheduleEntry);
+        if (schedule_dev_.bytes() < schedule_host_.size() * entry)
+            schedule_dev_.allocate(schedule_host_.size() * entry * 2);
         if (offsets_dev_.bytes() < offsets_host_.size() * 4) offsets_dev_.allocate(offsets_host_.size() * 4 * 2);
-        CUDA_CHECK(cudaMemcpyAsync(schedule_dev_.get(), schedule_host_.data(), schedule_host_.size() * 8,
+        check_schedule(p.stage_bytes);
+        CUDA_CHECK(cudaMemcpyAsync(schedule_dev_.get(), schedule_host_.data(), schedule_host_.size() * entry,
                                    cudaMemcpyHostToDevice, stream_));
         CUDA_CHECK(cudaMemcpyAsync(offsets_dev_.get(), offsets_host_.data(), offsets_host_.size() * 4,
                                    cudaMemcpyHostToDevice, stream_));
-        p.schedule = schedule_dev_.get<unsigned long long>();
+        p.schedule = schedule_dev_.get<ScheduleEntry>();
         p.schedule_offsets = offsets_dev_.get<unsigned>();
+    }
+
+    // Every unit must lie inside one weight allocation, start 16-byte aligned
+    // and fit a stage: checked on the host before any launch, so a bad
+    // schedule is an error here rather than a fault on the device.
+    void check_schedule(int stage_bytes) const {
+        std::vector<std::pair<size_t, size_t>> ranges;
+        auto add = [&](const DeviceBuffer& b) {
+            if (b.get()) ranges.push_back({(size_t)b.get(), (size_t)b.get() + b.bytes()});
+        };
+        add(token_table_);
+        for (int l = 0; l < shape_.layers; ++l) {
+            const LayerBuffers& W = layers_[l];
+            add(W.qkv_w); add(W.o_w); add(W.qc_w); add(W.oc_w); add(W.fc1_w); add(W.fc2_w);
+            add(W.wo_heads); add(W.woc_heads); add(W.w2_chunks);
+        }
+        std::sort(ranges.begin(), ranges.end());
+        for (size_t i = 0; i < schedule_host_.size(); ++i) {
+            const ScheduleEntry& e = schedule_host_[i];
+            if (e.source == 0 && e.bytes == 0) continue;  // the placeholder of an empty schedule
+            const size_t lo = (size_t)e.source, hi = lo + (size_t)e.bytes;
+            auto it = std::upper_bound(ranges.begin(), ranges.end(), std::make_pair(lo, (size_t)-1));
+            const bool inside = it != ranges.begin() && lo >= std::prev(it)->first && hi <= std::prev(it)->second;
+            if (!inside || lo % 16 != 0 || e.bytes % 16 != 0 || e.bytes == 0 || e.bytes > (size_t)stage_bytes)
+                throw LogicError("weight-stream unit " + std::to_string(i) + " lies outside the weights");
+        }
     }
 
     // Stage size: one 16-row tile over kpd (at least 16 KB); as many stages
@@ -1137,7 +1166,7 @@ private:
     DeviceBuffer logits_staging_, hidden_staging_;
     DeviceBuffer ops_prompt_dev_, ops_step_dev_, ops_teacher_dev_, ops_probe_dev_;
     DeviceBuffer schedule_dev_, offsets_dev_;
-    std::vector<unsigned long long> schedule_host_;
+    std::vector<ScheduleEntry> schedule_host_;
     std::vector<unsigned> offsets_host_;
     std::vector<StepOp> ops_prompt_, ops_step_, ops_teacher_;
 

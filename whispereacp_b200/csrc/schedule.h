@@ -93,7 +93,7 @@ inline bool item_region(const StepParams& p, const StepOp& op, int item, int reg
 
 // Appends the units of a region: whole-tile groups, or k-blocks of a tile
 // larger than a stage.
-inline void append_region(const Region& r, int stage_chunks, std::vector<unsigned long long>& out) {
+inline void append_region(const Region& r, int stage_chunks, std::vector<ScheduleEntry>& out) {
     if (r.chunks > stage_chunks) {
         const int blocks = (r.chunks + stage_chunks - 1) / stage_chunks;
         for (int t = 0; t < r.tiles; ++t)
@@ -111,7 +111,7 @@ inline void append_region(const Region& r, int stage_chunks, std::vector<unsigne
 
 // The per-CTA schedules of a launch, concatenated, and their offsets.
 inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, int grid, int rt,
-                           std::vector<unsigned long long>& units, std::vector<unsigned>& offsets) {
+                           std::vector<ScheduleEntry>& units, std::vector<unsigned>& offsets) {
     const int stage_chunks = p.stage_bytes / 1024;
     units.clear();
     offsets.assign(1, 0u);

@@ -37,6 +37,38 @@ __device__ __forceinline__ unsigned short ld_nc_u16(const void* p) {
     return __ldg(reinterpret_cast<const unsigned short*>(p));
 }
 __device__ __forceinline__ uint4 ld_nc4(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// The CTA is 8 consumer warps, which run the ops, and one producer warp,
+// which only streams weights into the shared-memory ring.  The consumers
+// synchronise among themselves on named barrier 1.
+constexpr int kConsumers = kThreads;
+constexpr int kBlockThreads = kThreads + 32;
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kConsumers) : "memory"); }
+
+__device__ __forceinline__ float consumer_sum(float v, float* scratch) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    consumer_sync();
+    if (lane == 0) scratch[warp] = v;
+    consumer_sync();
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) total += scratch[w];
+    return total;
+}
+
+__device__ __forceinline__ float consumer_max(float v, float* scratch) {
+    v = warp_max(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    consumer_sync();
+    if (lane == 0) scratch[warp] = v;
+    consumer_sync();
+    float best = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) best = fmaxf(best, scratch[w]);
+    return best;
+}
+
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
@@ -88,7 +120,7 @@ constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
 // records kErrBarrierTimeout, raises the abort word and the kernel returns.
 __device__ bool grid_barrier(unsigned* count, unsigned& epoch, int* state) {
     __shared__ int aborted;
-    __syncthreads();
+    consumer_sync();
     ++epoch;
     if (threadIdx.x == 0) {
         asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(count), "r"(1u) : "memory");
@@ -104,140 +136,124 @@ __device__ bool grid_barrier(unsigned* count, unsigned& epoch, int* state) {
         }
         aborted = ld_volatile(state + kAbort);
     }
-    __syncthreads();
+    consumer_sync();
     return aborted == 0;
 }
 
 // ------------------------------------------------------------ weight stream
 
-// Weight tiles stream through a ring of shared-memory stages, each filled by
-// one cp.async.bulk copy that completes an mbarrier.  The CTA's sequence of
-// weight units -- over the ops of every step, the items the CTA owns, their
-// weight regions, and the units of each region -- is fixed, so thread 0
-// issues ahead as far as the ring allows: the next op's first tiles are in
-// flight while this op (an attention, say) and the grid barrier run.
+// Weight tiles stream through a ring of shared-memory stages.  The producer
+// warp walks the CTA's schedule (built on the host, schedule.h) -- every
+// unit of weights the CTA's ops consume in a step, in order, step after step
+// -- and fills stage u % S with unit u by one cp.async.bulk copy that
+// completes full[u % S], once the consumers have released unit u - S
+// through empty[u % S].  The consumers wait on full[], read, and release
+// warp by warp, so no CTA-wide sync is spent per unit, and the next op's
+// first units land while this op and the grid barrier run.
 
 __device__ __forceinline__ uint32_t smem_address(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-struct Cursor {
-    int step;      // step of the next unit
-    unsigned at;   // index of the next unit within the CTA's schedule
-};
-
 struct Stream {
     unsigned char* ring;          // stages x stage_bytes
-    uint64_t* full;               // one mbarrier per stage
+    uint64_t* full;               // per stage: the unit landed (tx bytes)
+    uint64_t* empty;              // per stage: the 8 consumer warps released it
     int stages;
     int stage_bytes;
-    unsigned long long consumed;  // units every thread has finished with
-    unsigned long long issued;    // thread 0 only
-    Cursor cursor;                // thread 0 only: the next unit to issue
+    unsigned long long next;      // the next unit this CTA's consumers reach
 };
 
-__device__ __forceinline__ int row_tiles(int rows, int rt) { return (rows + rt - 1) / rt; }
-__device__ __forceinline__ int round16(int n) { return (n + 15) / 16 * 16; }
-
-// Thread 0: the next unit of this CTA's schedule, or false past the last step.
-template <int RT>
-__device__ __forceinline__ bool next_unit(const StepParams& p, const Stream& s, Cursor& c, const unsigned char** src,
-                                          unsigned* bytes) {
-    const unsigned first = __ldg(p.schedule_offsets + blockIdx.x);
-    const unsigned count = __ldg(p.schedule_offsets + blockIdx.x + 1) - first;
-    if (count == 0) return false;
-    if (c.at == count) {
-        c.at = 0;
-        ++c.step;
-    }
-    if (c.step >= p.steps) return false;
-    const unsigned long long e = __ldg(p.schedule + first + c.at);
-    ++c.at;
-    *src = reinterpret_cast<const unsigned char*>((size_t)(e & ~1023ull));
-    *bytes = ((unsigned)(e & 1023u) + 1u) * 1024u;
-    return true;
+__device__ __forceinline__ bool try_parity(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, P;\n\t}\n"
+        : "=r"(done)
+        : "r"(smem_address(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
 }
 
-// Thread 0: fills every free stage.
-template <int RT>
-__device__ void issue_ahead(const StepParams& p, Stream& s) {
-    while (s.issued < s.consumed + (unsigned long long)s.stages) {
-        const unsigned char* src;
-        unsigned bytes;
-        if (!next_unit<RT>(p, s, s.cursor, &src, &bytes)) return;
-        const int stage = (int)(s.issued % s.stages);
-        const uint32_t bar = smem_address(s.full + stage);
-        const uint32_t dst = smem_address(s.ring + (size_t)stage * s.stage_bytes);
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
-        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
-                     "l"(src), "r"(bytes), "r"(bar)
-                     : "memory");
-        ++s.issued;
-    }
-}
-
-// Waits (bounded) for unit `index` to land; false if the wait gave up.
-__device__ bool wait_unit(const StepParams& p, const Stream& s, unsigned long long index) {
-    const uint32_t bar = smem_address(s.full + (int)(index % s.stages));
-    const uint32_t parity = (uint32_t)((index / s.stages) & 1);
-    unsigned long long start = 0;
-    for (int attempt = 0;; ++attempt) {
-        uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred P;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, P;\n\t}\n"
-            : "=r"(done)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (done) return true;
-        if (attempt == 0) start = global_ns();
-        else if (global_ns() - start > kWaitTimeoutNs) {
+// Waits for the phase of `parity` to complete, for at most kWaitTimeoutNs;
+// gives up early when *stop is raised.  On a timeout it records
+// kErrBarrierTimeout and raises the abort word.
+__device__ bool wait_parity(const StepParams& p, uint64_t* bar, uint32_t parity, const volatile int* stop) {
+    if (try_parity(bar, parity)) return true;
+    const unsigned long long start = global_ns();
+    while (!try_parity(bar, parity)) {
+        if (stop && *stop) return false;
+        if (global_ns() - start > kWaitTimeoutNs) {
             atomicOr(p.state + kError, kErrBarrierTimeout);
             atomicExch(p.state + kAbort, 1);
             return false;
         }
     }
+    return true;
 }
 
-// The next unit, landed: thread 0 waits (bounded) and tells the CTA; then
-// every thread observes the completed phase.  nullptr if the wait gave up.
-__device__ const unsigned char* acquire_unit(const StepParams& p, const Stream& s) {
-    __shared__ int gave_up;
+// Consumers: unit `index` landed.  A wait that gave up (the abort word is
+// then raised) returns the stage all the same, so every warp keeps the same
+// path to the next grid barrier, where the kernel leaves.
+__device__ __forceinline__ const unsigned char* unit_at(const StepParams& p, const Stream& s, unsigned long long index) {
     Trace tr = trace_of(p.profile);
     tr.begin();
-    if (threadIdx.x == 0) gave_up = wait_unit(p, s, s.consumed) ? 0 : 1;
-    __syncthreads();
+    const int stage = (int)(index % s.stages);
+    wait_parity(p, s.full + stage, (uint32_t)((index / s.stages) & 1), nullptr);
     tr.end(kTrWait);
-    if (gave_up) return nullptr;
-    if (threadIdx.x != 0) {
-        const uint32_t bar = smem_address(s.full + (int)(s.consumed % s.stages));
-        const uint32_t parity = (uint32_t)((s.consumed / s.stages) & 1);
-        uint32_t done = 0;
-        while (!done)
-            asm volatile(
-                "{\n\t.reg .pred P;\n\t"
-                "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
-                "selp.u32 %0, 1, 0, P;\n\t}\n"
-                : "=r"(done)
-                : "r"(bar), "r"(parity)
-                : "memory");
-    }
-    return s.ring + (size_t)(s.consumed % s.stages) * s.stage_bytes;
+    return s.ring + (size_t)stage * s.stage_bytes;
 }
 
-// After a unit: every thread is done reading its stage, which thread 0 may
-// now refill.
-template <int RT>
-__device__ __forceinline__ void release_unit(const StepParams& p, Stream& s) {
-    Trace tr = trace_of(p.profile);
-    tr.begin();
-    __syncthreads();
-    tr.end(kTrRelease);
-    ++s.consumed;
-    tr.begin();
-    if (threadIdx.x == 0) issue_ahead<RT>(p, s);
-    tr.end(kTrIssue);
+// Consumers: this warp is done with unit `index` (its share of it, or the
+// whole of it when the warp owns the unit: count 8).
+__device__ __forceinline__ void release_at(const Stream& s, unsigned long long index, unsigned count = 1) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_address(s.empty + index % s.stages)),
+                     "r"(count)
+                     : "memory");
+}
+
+// The shared-unit pattern: every warp reads the next unit, then releases it.
+__device__ __forceinline__ const unsigned char* acquire_unit(const StepParams& p, const Stream& s) {
+    return unit_at(p, s, s.next);
+}
+__device__ __forceinline__ void release_unit(Stream& s) {
+    release_at(s, s.next);
+    ++s.next;
+}
+
+// The producer warp's lane 0: the CTA's schedule for every step, then a
+// wait for every copy still landing, so none outlives the CTA.
+__device__ void produce(const StepParams& p, Stream& s, const volatile int* stop) {
+    const unsigned first = __ldg(p.schedule_offsets + blockIdx.x);
+    const unsigned count = __ldg(p.schedule_offsets + blockIdx.x + 1) - first;
+    const ulonglong2* schedule = reinterpret_cast<const ulonglong2*>(p.schedule) + first;
+    unsigned long long u = 0;
+    bool go = count > 0;
+    for (int step = 0; go && step < p.steps; ++step) {
+        for (unsigned i = 0; i < count; ++i, ++u) {
+            const int stage = (int)(u % s.stages);
+            if (u >= (unsigned long long)s.stages &&
+                !wait_parity(p, s.empty + stage, (uint32_t)((u / s.stages - 1) & 1), stop)) {
+                go = false;
+                break;
+            }
+            const ulonglong2 e = __ldg(schedule + i);
+            const uint32_t bar = smem_address(s.full + stage);
+            const uint32_t dst = smem_address(s.ring + (size_t)stage * s.stage_bytes);
+            const unsigned bytes = (unsigned)e.y;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+            asm volatile(
+                "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                "l"(e.x), "r"(bytes), "r"(bar)
+                : "memory");
+        }
+    }
+    const unsigned long long stages = (unsigned long long)s.stages;
+    for (unsigned long long v = u > stages ? u - stages : 0; v < u; ++v)
+        if (!wait_parity(p, s.full + v % stages, (uint32_t)((v / stages) & 1), nullptr)) break;
 }
 
 // -------------------------------------------------------------------- embed
@@ -292,7 +308,7 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
             float total = 0.f;
 #pragma unroll
             for (int i = 0; i < kPer; ++i) total += v[i];
-            const float mean = block_sum(total, scratch) / (float)d;
+            const float mean = consumer_sum(total, scratch) / (float)d;
             float centred = 0.f;
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
@@ -300,7 +316,7 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
                 const float dv = c < d ? v[i] - mean : 0.f;
                 centred += dv * dv;
             }
-            const float scale = rsqrtf(block_sum(centred, scratch) / (float)d + 1e-5f);
+            const float scale = rsqrtf(consumer_sum(centred, scratch) / (float)d + 1e-5f);
             WT* out = xs + (size_t)rl * ldx;
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
@@ -357,6 +373,9 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
         }
     }
 }
+
+__device__ __forceinline__ int row_tiles(int rows, int rt) { return (rows + rt - 1) / rt; }
+__device__ __forceinline__ int round16(int n) { return (n + 15) / 16 * 16; }
 
 // ------------------------------------------------------------------ products
 
@@ -421,7 +440,7 @@ __device__ bool product_tile(const StepParams& p, Stream& s, int kp, const WT* X
         for (int c = warp; c < n; c += kWarps)
             product_chunk<WT, NT, X_SHARED>(unit, c, X, ldx, (c0 + c) * 32, x_ok, acc);
         tr.end(kTrCompute);
-        release_unit<RT>(p, s);
+        release_unit(s);
     }
     return true;
 }
@@ -440,7 +459,7 @@ __device__ __forceinline__ void product_reduce(float* red, const float (&acc)[NT
         red[(warp * 16 + gq + 8) * RT + col] = acc[j][2];
         red[(warp * 16 + gq + 8) * RT + col + 1] = acc[j][3];
     }
-    __syncthreads();
+    consumer_sync();
 }
 
 __device__ __forceinline__ float product_sum(const float* red, int RT, int nl, int rl) {
@@ -471,11 +490,11 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
         bool ok;
         if (normalise) {
             if (cached_tile != r_tile) {
-                __syncthreads();
+                consumer_sync();
                 Trace trn = trace_of(p.profile);
                 trn.begin();
                 layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, xs, pitch, nullptr);
-                __syncthreads();
+                consumer_sync();
                 trn.end(kTrNorm);
                 cached_tile = r_tile;
             }
@@ -530,7 +549,7 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
             }
             }
         }
-        __syncthreads();
+        consumer_sync();
     }
 }
 
@@ -546,11 +565,13 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
     constexpr int RT = 8 * NT;
     const int pitch = tile_pitch(p.kpd);
     WT* xs = reinterpret_cast<WT*>(work);
-    float* red = reinterpret_cast<float*>(work + (size_t)RT * pitch * sizeof(WT));
-    float* tile = red + kWarps * 16 * RT;  // [16][RT] values, then [16][RT] indices
-    float* best_v = tile + 2 * 16 * RT;
+    float* fold_v = reinterpret_cast<float*>(work + (size_t)RT * pitch * sizeof(WT));  // [8 warps][RT]
+    uint32_t* fold_i = reinterpret_cast<uint32_t*>(fold_v + kWarps * RT);
+    float* best_v = reinterpret_cast<float*>(fold_i + kWarps * RT);
     uint32_t* best_i = reinterpret_cast<uint32_t*>(best_v + p.out_rows);
     __shared__ int is_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;
 
     for (int r = threadIdx.x; r < p.out_rows; r += kThreads) {
         best_v[r] = -INFINITY;
@@ -558,77 +579,117 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
     }
     const int n_tiles = (p.vocabulary + 15) / 16;
     const int r_tiles = (p.out_rows + RT - 1) / RT;
-    int cached_tile = -1;
-    // Thread o < 16*RT keeps, for input row o % RT of the current row tile,
-    // the first maximum over column o / RT of every tile it has seen.
-    const bool owner = threadIdx.x < 16 * RT;
-    const int my_nl = threadIdx.x / RT, my_rl = threadIdx.x % RT;
-    float cand_v = -INFINITY;
-    uint32_t cand_i = kUnchosen;
-    int cand_r0 = 0, cand_rows = 0;
-    // Folds the owners' candidates of a row tile into best_v/best_i.
-    auto flush = [&]() {
-        __syncthreads();
-        if (owner) {
-            tile[my_nl * RT + my_rl] = cand_v;
-            reinterpret_cast<uint32_t*>(tile + 16 * RT)[my_nl * RT + my_rl] = cand_i;
-        }
-        __syncthreads();
-        for (int rl = threadIdx.x; rl < cand_rows; rl += kThreads) {
-            float bv = best_v[cand_r0 + rl];
-            uint32_t bi = best_i[cand_r0 + rl];
-            for (int nl = 0; nl < 16; ++nl) {
-                const float v = tile[nl * RT + rl];
-                const uint32_t i = reinterpret_cast<const uint32_t*>(tile + 16 * RT)[nl * RT + rl];
-                if (candidate_better(v, i, bv, bi)) { bv = v; bi = i; }
-            }
-            best_v[cand_r0 + rl] = bv;
-            best_i[cand_r0 + rl] = bi;
-        }
-        __syncthreads();
-        cand_v = -INFINITY;
-        cand_i = kUnchosen;
-    };
-    __syncthreads();
+    const int chunks = p.kpd / 32;
+    const int stage_chunks = s.stage_bytes / 1024;
+    const int blocks = (chunks + stage_chunks - 1) / stage_chunks;  // units of a tile
+    const unsigned long long base = s.next;
+    int mine = 0;  // this CTA's items so far (unit index = base + mine*blocks + block)
 
-    for (int item = blockIdx.x; item < n_tiles * r_tiles; item += gridDim.x) {
-        const int r_tile = item / n_tiles, n_tile = item % n_tiles;
-        const int r0 = r_tile * RT, n0 = n_tile * 16;
+    // A row tile at a time: the CTA normalises its rows, then every warp
+    // takes whole vocabulary tiles of it -- tile k of the CTA goes to warp
+    // k % 8 -- over all of K, keeping per row the first maximum it meets.
+    for (int r_tile = 0; r_tile < r_tiles; ++r_tile) {
+        const int lo = r_tile * n_tiles, hi = lo + n_tiles;
+        int first = blockIdx.x;
+        if (first < lo) first += ((lo - first + gridDim.x - 1) / gridDim.x) * gridDim.x;
+        if (first >= hi) continue;
+        const int count = (hi - first + gridDim.x - 1) / gridDim.x;
+        const int r0 = r_tile * RT;
         const int rows_valid = min(RT, p.out_rows - r0);
-        if (cached_tile != r_tile) {
-            if (cached_tile >= 0) flush();
-            __syncthreads();
-            Trace trn = trace_of(p.profile);
-            trn.begin();
-            layer_norm_tile<WT>(p, p.h, p.final_gamma, p.final_beta, r0, rows_valid, p.row_step, p.row_offset, xs, pitch,
-                                p.hidden_out);
-            __syncthreads();
-            trn.end(kTrNorm);
-            cached_tile = r_tile;
-            cand_r0 = r0;
-            cand_rows = rows_valid;
+        consumer_sync();
+        Trace trn = trace_of(p.profile);
+        trn.begin();
+        layer_norm_tile<WT>(p, p.h, p.final_gamma, p.final_beta, r0, rows_valid, p.row_step, p.row_offset, xs, pitch,
+                            p.hidden_out);
+        consumer_sync();
+        trn.end(kTrNorm);
+
+        bool x_ok[NT];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) x_ok[j] = 8 * j + gq < rows_valid;
+        float cand_v[NT][2];
+        uint32_t cand_i[NT][2];
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+            cand_v[j][0] = cand_v[j][1] = -INFINITY;
+            cand_i[j][0] = cand_i[j][1] = kUnchosen;
         }
-        float acc[NT][4];
-        if (!product_tile<WT, NT, true>(p, s, p.kpd, xs, pitch, rows_valid, acc)) return;
-        Trace tre = trace_of(p.profile);
-        tre.begin();
-        product_reduce<NT>(red, acc);
-        if (owner) {
-            const int n = n0 + my_nl;
-            const float v = product_sum(red, RT, my_nl, my_rl);
-            if (n < p.vocabulary && my_rl < rows_valid) {
-                if (p.logits_out) p.logits_out[(size_t)(r0 + my_rl) * p.vocabulary + n] = v;
-                const bool allowed = p.mask == nullptr || __ldg(p.mask + n) == 0.f;
-                if (allowed && candidate_better(v, (uint32_t)n, cand_v, cand_i)) {
-                    cand_v = v;
-                    cand_i = (uint32_t)n;
+        for (int k = warp; k < count; k += kWarps) {
+            const int n0 = (first - lo + k * (int)gridDim.x) * 16;
+            float acc[NT][4];
+#pragma unroll
+            for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+            for (int b = 0; b < blocks; ++b) {
+                const unsigned long long index = base + (unsigned long long)(mine + k) * blocks + b;
+                const unsigned char* unit = unit_at(p, s, index);
+                Trace tr = trace_of(p.profile);
+                tr.begin();
+                const int c0 = b * stage_chunks, n = min(stage_chunks, chunks - c0);
+                for (int c = 0; c < n; ++c) product_chunk<WT, NT, true>(unit, c, xs, pitch, (c0 + c) * 32, x_ok, acc);
+                tr.end(kTrCompute);
+                release_at(s, index, kWarps);
+            }
+            // Lane (g, t) holds rows n0+g and n0+g+8 of input rows 8j+2t, 8j+2t+1.
+            const int na = n0 + gq, nb = n0 + gq + 8;
+            const bool a_ok = na < p.vocabulary && (p.mask == nullptr || __ldg(p.mask + na) == 0.f);
+            const bool b_ok = nb < p.vocabulary && (p.mask == nullptr || __ldg(p.mask + nb) == 0.f);
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int rl = 8 * j + 2 * tq + e;
+                    if (rl >= rows_valid) continue;
+                    const float va = acc[j][e], vb = acc[j][2 + e];
+                    if (p.logits_out) {
+                        if (na < p.vocabulary) p.logits_out[(size_t)(r0 + rl) * p.vocabulary + na] = va;
+                        if (nb < p.vocabulary) p.logits_out[(size_t)(r0 + rl) * p.vocabulary + nb] = vb;
+                    }
+                    if (a_ok && candidate_better(va, (uint32_t)na, cand_v[j][e], cand_i[j][e])) {
+                        cand_v[j][e] = va;
+                        cand_i[j][e] = (uint32_t)na;
+                    }
+                    if (b_ok && candidate_better(vb, (uint32_t)nb, cand_v[j][e], cand_i[j][e])) {
+                        cand_v[j][e] = vb;
+                        cand_i[j][e] = (uint32_t)nb;
+                    }
                 }
             }
         }
-        __syncthreads();
-        tre.end(kTrEpilogue);
+        // Fold the warp's lanes of equal t (the 8 values of g), then the warps.
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                float bv = cand_v[j][e];
+                uint32_t bi = cand_i[j][e];
+#pragma unroll
+                for (int o = 4; o < 32; o <<= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (candidate_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+                }
+                if (gq == 0) {
+                    fold_v[warp * RT + 8 * j + 2 * tq + e] = bv;
+                    fold_i[warp * RT + 8 * j + 2 * tq + e] = bi;
+                }
+            }
+        }
+        consumer_sync();
+        for (int rl = threadIdx.x; rl < rows_valid; rl += kThreads) {
+            float bv = best_v[r0 + rl];
+            uint32_t bi = best_i[r0 + rl];
+            for (int w = 0; w < kWarps; ++w)
+                if (candidate_better(fold_v[w * RT + rl], fold_i[w * RT + rl], bv, bi)) {
+                    bv = fold_v[w * RT + rl];
+                    bi = fold_i[w * RT + rl];
+                }
+            best_v[r0 + rl] = bv;
+            best_i[r0 + rl] = bi;
+        }
+        mine += count;
     }
-    if (cached_tile >= 0) flush();
+    s.next = base + (unsigned long long)mine * blocks;
+    consumer_sync();
 
     // This CTA's candidates, then the fold by whichever CTA finishes last.
     for (int r = threadIdx.x; r < p.out_rows; r += kThreads) {
@@ -636,12 +697,11 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
         p.candidate_indices[(size_t)r * gridDim.x + blockIdx.x] = best_i[r];
     }
     __threadfence();
-    __syncthreads();
+    consumer_sync();
     if (threadIdx.x == 0) is_last = atomicAdd(p.logits_counter, 1u) == gridDim.x - 1;
-    __syncthreads();
+    consumer_sync();
     if (!is_last) return;
     __threadfence();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rows_per_window = p.out_rows / p.windows;
     for (int r = warp; r < p.out_rows; r += kWarps) {
         float bv = -INFINITY;
@@ -667,7 +727,7 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
             }
         }
     }
-    __syncthreads();
+    consumer_sync();
     if (threadIdx.x == 0) {
         if (p.stop_enabled) {
             int all = 1;
@@ -768,7 +828,7 @@ __device__ __forceinline__ void attention_values(const float* scores, const WT* 
 #pragma unroll
             for (int e = 0; e < 8; ++e) fold[g * D + piece * 8 + e] = acc[e];
         }
-        __syncthreads();
+        consumer_sync();
         if (threadIdx.x < D) {
             float o = 0.f;
             for (int gg = 0; gg < groups; ++gg) o += fold[gg * D + threadIdx.x];
@@ -784,14 +844,14 @@ __device__ __forceinline__ void attention_values(const float* scores, const WT* 
                 acc += scores[j] * load_kv1<WT, READ_ONLY>(V + (size_t)(k0 + j) * key_stride + c);
             fold[g * D + c] = acc;
         }
-        __syncthreads();
+        consumer_sync();
         if (threadIdx.x < D) {
             float o = 0.f;
             for (int gg = 0; gg < groups; ++gg) o += fold[gg * D + threadIdx.x];
             result[threadIdx.x] = o;
         }
     }
-    __syncthreads();
+    consumer_sync();
 }
 
 // One warp's attention of one query over keys [k0, k0+n), n <= kWarpKeys:
@@ -863,19 +923,19 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
         const int r = item / p.heads, head = item % p.heads;
         const int b = r / p.tokens, t = r % p.tokens;
         const int keys = position + t + 1;
-        __syncthreads();
+        consumer_sync();
         for (int c = threadIdx.x; c < D; c += kThreads) q[c] = ld_cg(p.q + (size_t)r * p.width + head * D + c) * p.scale;
-        __syncthreads();
+        consumer_sync();
         const WT* K = static_cast<const WT*>(op.keys) + (size_t)b * op.window_stride + (size_t)head * D;
         const WT* V = static_cast<const WT*>(op.values) + (size_t)b * op.window_stride + (size_t)head * D;
-        const float m = block_max(attention_scores<WT, false>(q, K, op.key_stride, D, 0, keys, scores), scratch);
+        const float m = consumer_max(attention_scores<WT, false>(q, K, op.key_stride, D, 0, keys, scores), scratch);
         float local = 0.f;
         for (int j = threadIdx.x; j < keys; j += kThreads) {
             const float e = __expf(scores[j] - m);
             scores[j] = e;
             local += e;
         }
-        const float l = block_sum(local, scratch);
+        const float l = consumer_sum(local, scratch);
         attention_values<WT, false>(scores, V, op.key_stride, D, 0, keys, fold, result);
         WT* out = static_cast<WT*>(p.attn16) + (size_t)r * p.kpd + head * D;
         for (int c = threadIdx.x; c < D; c += kThreads) out[c] = Half16<WT>::from_float(result[c] / l);
@@ -904,23 +964,23 @@ __device__ void op_cross_attention(const StepParams& p, const StepOp& op, unsign
         const int k0 = split * op.chunk;
         const int n = min(op.key_count, k0 + op.chunk) - k0;
         float* out = p.partial + (((size_t)r * p.heads + head) * S + split) * (D + 2);
-        __syncthreads();
+        consumer_sync();
         if (n <= 0) {
             for (int c = threadIdx.x; c < D + 2; c += kThreads) out[c] = c == 0 ? -INFINITY : 0.f;
         } else {
             for (int c = threadIdx.x; c < D; c += kThreads)
                 q[c] = ld_cg(p.q + (size_t)r * p.width + head * D + c) * p.scale;
-            __syncthreads();
+            consumer_sync();
             const WT* K = static_cast<const WT*>(op.keys) + (size_t)b * op.window_stride + (size_t)head * D;
             const WT* V = static_cast<const WT*>(op.values) + (size_t)b * op.window_stride + (size_t)head * D;
-            const float m = block_max(attention_scores<WT, true>(q, K, op.key_stride, D, k0, n, scores), scratch);
+            const float m = consumer_max(attention_scores<WT, true>(q, K, op.key_stride, D, k0, n, scores), scratch);
             float local = 0.f;
             for (int j = threadIdx.x; j < n; j += kThreads) {
                 const float e = __expf(scores[j] - m);
                 scores[j] = e;
                 local += e;
             }
-            const float l = block_sum(local, scratch);
+            const float l = consumer_sum(local, scratch);
             attention_values<WT, true>(scores, V, op.key_stride, D, k0, n, fold, result);
             for (int c = threadIdx.x; c < D; c += kThreads) out[2 + c] = result[c];
             if (threadIdx.x == 0) {
@@ -929,13 +989,13 @@ __device__ void op_cross_attention(const StepParams& p, const StepOp& op, unsign
             }
         }
         __threadfence();
-        __syncthreads();
+        consumer_sync();
         if (threadIdx.x == 0) {
             unsigned* counter = p.combine_counters + (size_t)r * p.heads + head;
             is_last = atomicAdd(counter, 1u) == (unsigned)(S - 1);
             if (is_last) atomicExch(counter, 0u);
         }
-        __syncthreads();
+        consumer_sync();
         if (!is_last) continue;
         __threadfence();
         const float* part = p.partial + ((size_t)r * p.heads + head) * S * (D + 2);
@@ -1025,7 +1085,7 @@ __device__ bool split_product(const StepParams& p, Stream& s, int tiles, const B
             for (int c = warp; c < chunks; c += kWarps)
                 product_chunk<WT, 1, true>(unit, c, A.xs, A.pitch, c * 32, x_ok, acc[t]);
             tr.end(kTrCompute);
-            release_unit<8 * NT>(p, s);
+            release_unit(s);
         }
     }
     Trace tr = trace_of(p.profile);
@@ -1040,7 +1100,7 @@ __device__ bool split_product(const StepParams& p, Stream& s, int tiles, const B
             r[(gq + 8) * 8 + 2 * tq + 1] = acc[t][0][3];
         }
     }
-    __syncthreads();
+    consumer_sync();
     for (int o = threadIdx.x; o < tiles * 128; o += kThreads) {
         const int t = o / 128, within = o % 128;
         float v = 0.f;
@@ -1048,7 +1108,7 @@ __device__ bool split_product(const StepParams& p, Stream& s, int tiles, const B
         for (int w = 0; w < kWarps; ++w) v += A.red[(size_t)(w * kMaxSplitTiles + t) * 128 + within];
         A.res[o] = v;
     }
-    __syncthreads();
+    consumer_sync();
     tr.end(kTrEpilogue);
     return true;
 }
@@ -1079,7 +1139,7 @@ __device__ bool tiled_product(const StepParams& p, Stream& s, int tiles, int chu
             emit(n + 8, rl + 1, acc[0][3]);
         }
         tr.end(kTrCompute);
-        release_unit<8 * NT>(p, s);
+        release_unit(s);
     }
     return true;
 }
@@ -1113,14 +1173,14 @@ __device__ float2 cta_attention(const float* q, const WT* K, const WT* V, long l
     float* result = fold + kFold;
     float* scores = result + 64;
     if (n <= 0) return make_float2(-INFINITY, 0.f);
-    const float m = block_max(attention_scores<WT, READ_ONLY>(q, K, key_stride, D, k0, n, scores), scratch);
+    const float m = consumer_max(attention_scores<WT, READ_ONLY>(q, K, key_stride, D, k0, n, scores), scratch);
     float local = 0.f;
     for (int j = threadIdx.x; j < n; j += kThreads) {
         const float e = __expf(scores[j] - m);
         scores[j] = e;
         local += e;
     }
-    const float l = block_sum(local, scratch);
+    const float l = consumer_sum(local, scratch);
     attention_values<WT, READ_ONLY>(scores, V, key_stride, D, k0, n, fold, result);
     return make_float2(m, l);
 }
@@ -1142,11 +1202,11 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
         const int head = item % H, r_tile = item / H;
         const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
         if (cached != r_tile) {
-            __syncthreads();
+            consumer_sync();
             Trace trn = trace_of(p.profile);
             trn.begin();
             layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
-            __syncthreads();
+            consumer_sync();
             trn.end(kTrNorm);
             cached = r_tile;
         }
@@ -1165,7 +1225,7 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
                 cache[((size_t)(r0 + rl) * p.max_positions + position) * d + head * D + c] = Half16<WT>::from_float(v);
             }
         }
-        __syncthreads();
+        consumer_sync();
         const int keys = position + 1;
         Trace tra = trace_of(p.profile);
         tra.begin();
@@ -1178,7 +1238,7 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
                 const float* row = A.att + 8 + kFold;
                 for (int c = threadIdx.x; c < op.kp2; c += kThreads)
                     A.o16[rl * ps + c] = Half16<WT>::from_float(c < D ? row[c] / ml.y : 0.f);
-                __syncthreads();
+                consumer_sync();
             }
         } else {
             const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1192,7 +1252,7 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
                 for (int c = lane; c < op.kp2; c += 32)
                     A.o16[rl * ps + c] = Half16<WT>::from_float(c < D ? row[c] / ml.y : 0.f);
             }
-            __syncthreads();
+            consumer_sync();
         }
         tra.end(kTrAttention);
         // X1 += the head's slice of out_proj; head 0 adds the bias and X0.
@@ -1206,7 +1266,7 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
                                    }))
             return;
         if (first) zero_rows(p.x2, r0, rows_valid, d);
-        __syncthreads();
+        consumer_sync();
     }
 }
 
@@ -1225,11 +1285,11 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
         const int split = item % S, head = (item / S) % H, r_tile = item / (S * H);
         const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
         if (cached != r_tile) {
-            __syncthreads();
+            consumer_sync();
             Trace trn = trace_of(p.profile);
             trn.begin();
             layer_norm_tile<WT>(p, p.x1, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
-            __syncthreads();
+            consumer_sync();
             trn.end(kTrNorm);
             cached = r_tile;
         }
@@ -1239,7 +1299,7 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
             const int n = o / rows_valid, rl = o % rows_valid;
             A.q[rl * 64 + n] = (A.res[n * 8 + rl] + __ldg(bias + n)) * p.scale;
         }
-        __syncthreads();
+        consumer_sync();
         // This split's partial (max, sum, unnormalised row) of every row.
         Trace tra = trace_of(p.profile);
         tra.begin();
@@ -1261,7 +1321,7 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
                     out[0] = ml.x;
                     out[1] = ml.y;
                 }
-                __syncthreads();
+                consumer_sync();
             }
         } else {
             const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1285,14 +1345,14 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
         }
         if (head == 0 && split == 0) zero_rows(p.h, r0, rows_valid, d);
         __threadfence();
-        __syncthreads();
+        consumer_sync();
         tra.end(kTrAttention);
         if (threadIdx.x == 0) {
             unsigned* counter = p.combine_counters + (size_t)r_tile * H + head;
             is_last = atomicAdd(counter, 1u) == (unsigned)(S - 1);
             if (is_last) atomicExch(counter, 0u);
         }
-        __syncthreads();
+        consumer_sync();
         if (!is_last) continue;
         __threadfence();
         // The last split joins the splits of every row (SingleQueryAttention.h:11-37)
@@ -1316,7 +1376,7 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
             }
             A.o16[rl * ps + c] = Half16<WT>::from_float(y);
         }
-        __syncthreads();
+        consumer_sync();
         // X2 += the head's slice of out_proj; head 0 adds the bias and X1.
         const bool first = head == 0;
         Trace trd = trace_of(p.profile);
@@ -1328,7 +1388,7 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
                                      if (first) v += __ldg(op.bias2 + n) + ld_cg(p.x1 + at);
                                      atomicAdd(p.x2 + at, v);
                                  });
-        __syncthreads();
+        consumer_sync();
         trd.end(kTrEpilogue);
     }
 }
@@ -1346,11 +1406,11 @@ __device__ void op_ffn_block(const StepParams& p, const StepOp& op, Stream& s, u
         const int j = item % chunks_n, r_tile = item / chunks_n;
         const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
         if (cached != r_tile) {
-            __syncthreads();
+            consumer_sync();
             Trace trn = trace_of(p.profile);
             trn.begin();
             layer_norm_tile<WT>(p, p.x2, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
-            __syncthreads();
+            consumer_sync();
             trn.end(kTrNorm);
             cached = r_tile;
         }
@@ -1361,7 +1421,7 @@ __device__ void op_ffn_block(const StepParams& p, const StepOp& op, Stream& s, u
             const float v = c < FC ? gelu_exact(A.res[c * 8 + rl] + __ldg(bias + c)) : 0.f;
             A.o16[rl * ps + c] = Half16<WT>::from_float(v);
         }
-        __syncthreads();
+        consumer_sync();
         // X0 += the fc2 slice of this chunk; chunk 0 adds the bias and X2.
         const bool first = j == 0;
         if (!tiled_product<WT, NT>(p, s, round16(d) / 16, op.kp2 / 32, op.group2, A.o16, ps, rows_valid,
@@ -1373,43 +1433,41 @@ __device__ void op_ffn_block(const StepParams& p, const StepOp& op, Stream& s, u
                                    }))
             return;
         if (first) zero_rows(p.x1, r0, rows_valid, d);
-        __syncthreads();
+        consumer_sync();
     }
 }
 
 // -------------------------------------------------------------- the kernel
 
-// Thread 0, on the way out: no bulk copy may still be landing in shared
-// memory once the CTA exits, so wait (bounded) for every unit issued.
-__device__ void drain_stream(const StepParams& p, Stream& s) {
-    if (threadIdx.x == 0)
-        for (unsigned long long i = s.consumed; i < s.issued; ++i)
-            if (!wait_unit(p, s, i)) break;
-    __syncthreads();
-}
-
 constexpr int kMaxStages = 8;
 
 template <typename WT, int NT>
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(StepParams p) {
+__global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
-    constexpr int RT = 8 * NT;
+    __shared__ int stop_flag;
     Stream s;
     s.stages = p.stages;
     s.stage_bytes = p.stage_bytes;
     s.ring = smem;
     s.full = reinterpret_cast<uint64_t*>(smem + (size_t)s.stages * s.stage_bytes);
-    unsigned char* work = smem + (size_t)s.stages * s.stage_bytes + 8 * kMaxStages;
-    s.consumed = 0;
-    s.issued = 0;
-    s.cursor = Cursor{0, 0u};
+    s.empty = s.full + kMaxStages;
+    unsigned char* work = smem + (size_t)s.stages * s.stage_bytes + 16 * kMaxStages;
+    s.next = 0;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < s.stages; ++i)
+        stop_flag = 0;
+        for (int i = 0; i < s.stages; ++i) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(s.full + i)) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_address(s.empty + i)), "r"(kWarps)
+                         : "memory");
+        }
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     __syncthreads();
-    if (threadIdx.x == 0) issue_ahead<RT>(p, s);
+    volatile int* stop = &stop_flag;
+    if (threadIdx.x >= kConsumers) {
+        if (threadIdx.x == kConsumers) produce(p, s, stop);
+        return;
+    }
 
     unsigned epoch = 0;
     const bool stamp = p.profile != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
@@ -1429,14 +1487,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(StepParams p) {
             case kOpFeedForwardBlock: op_ffn_block<WT, NT>(p, op, s, work); break;
             }
             if (!grid_barrier(p.barrier, epoch, p.state)) {
-                drain_stream(p, s);
+                if (threadIdx.x == 0) *stop = 1;
                 return;
             }
             if (stamp && step == 0) p.profile[i + 1] = global_ns();
         }
         if (p.stop_enabled && ld_volatile(p.state + kAllEnded)) break;
     }
-    drain_stream(p, s);
+    if (threadIdx.x == 0) *stop = 1;
 }
 
 // Shared memory past the ring: the largest work area any op of the launch uses.
@@ -1444,7 +1502,8 @@ template <typename WT, int NT>
 size_t work_bytes(const StepParams& p, int max_chunk, bool fused) {
     constexpr int RT = 8 * NT;
     const size_t product = (size_t)RT * tile_pitch(p.kpd) * sizeof(WT) +
-                           sizeof(float) * (kWarps * 16 * RT + 2 * 16 * RT) + (size_t)p.out_rows * 8;
+                           sizeof(float) * (kWarps * 16 * RT + 16 * RT) + (size_t)p.out_rows * 8 +
+                           sizeof(float) * 2 * kWarps * RT;
     const size_t attention = sizeof(float) * (kAttentionFixed + std::max(max_chunk, p.max_positions));
     size_t work = std::max(product, attention);
     if (fused) work = std::max(work, block_area_bytes(p.kpd, (int)sizeof(WT), p.max_positions));
@@ -1453,7 +1512,7 @@ size_t work_bytes(const StepParams& p, int max_chunk, bool fused) {
 
 template <typename WT, int NT>
 size_t shared_bytes(const StepParams& p, int max_chunk, bool fused) {
-    return (size_t)p.stages * p.stage_bytes + 8 * kMaxStages + work_bytes<WT, NT>(p, max_chunk, fused);
+    return (size_t)p.stages * p.stage_bytes + 16 * kMaxStages + work_bytes<WT, NT>(p, max_chunk, fused);
 }
 
 template <typename WT, int NT>
@@ -1464,7 +1523,7 @@ void launch_typed(const StepParams& p, int max_chunk, bool fused, int grid, cuda
     if (e != cudaSuccess) throw std::runtime_error(std::string("decode kernel shared memory: ") + cudaGetErrorString(e));
     StepParams copy = p;
     void* args[] = {&copy};
-    e = cudaLaunchCooperativeKernel((const void*)kernel, grid, kThreads, args, smem, stream);
+    e = cudaLaunchCooperativeKernel((const void*)kernel, grid, kBlockThreads, args, smem, stream);
     if (e != cudaSuccess) throw std::runtime_error(std::string("decode kernel launch: ") + cudaGetErrorString(e));
 }
 
@@ -1477,7 +1536,7 @@ int occupancy_typed(const StepParams& p, int max_chunk, bool fused) {
         return 0;
     }
     int blocks = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, smem) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kBlockThreads, smem) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
@@ -1523,7 +1582,7 @@ int decode_tile_rows(const StepParams& p) { return 8 * tile_columns(p); }
 
 size_t decode_work_bytes(bool half, const StepParams& p, int max_chunk, bool fused) {
     return (half ? work_rows<__half>(p, max_chunk, fused) : work_rows<__nv_bfloat16>(p, max_chunk, fused)) +
-           8 * kMaxStages;
+           16 * kMaxStages;
 }
 
 int decode_blocks_per_sm(bool half, const StepParams& p, int max_chunk, bool fused) {

@@ -149,15 +149,19 @@ struct StepParams {
     int stage_bytes;                    // bytes of a weight-stream stage (multiple of 1 KB)
     int stages;                         // stages in the ring
     // The weight units each CTA streams in one step, in order: CTA c's are
-    // schedule[schedule_offsets[c] .. schedule_offsets[c+1]), each a source
-    // address (1 KB aligned) with (bytes / 1024 - 1) in its low 10 bits.
-    const unsigned long long* schedule;
+    // schedule[schedule_offsets[c] .. schedule_offsets[c+1]).
+    const struct ScheduleEntry* schedule;
     const unsigned* schedule_offsets;
 };
 
-// One weight-stream unit of a schedule.
-__host__ __device__ inline unsigned long long schedule_entry(const void* src, unsigned bytes) {
-    return (unsigned long long)(size_t)src | (unsigned long long)(bytes / 1024 - 1);
+// One weight-stream unit: a 16-byte aligned source and its size in bytes.
+struct __align__(16) ScheduleEntry {
+    unsigned long long source;
+    unsigned long long bytes;
+};
+
+__host__ __device__ inline ScheduleEntry schedule_entry(const void* src, unsigned bytes) {
+    return ScheduleEntry{(unsigned long long)(size_t)src, (unsigned long long)bytes};
 }
 
 }  // namespace wsp
