@@ -21,6 +21,12 @@
 namespace wsp {
 namespace {
 
+// Consumer warps of the decode kernel: 7, so that with the producer warp a
+// CTA is 8 warps -- two per SM sub-partition, each thread keeping the full
+// register budget.
+constexpr int kWarps = 7;
+constexpr int kThreads = 32 * kWarps;
+
 // ------------------------------------------------------------ memory access
 
 // Data another CTA wrote inside the launch is read through L2 (ld.global.cg:
@@ -87,22 +93,27 @@ __device__ __forceinline__ unsigned long long global_ns() {
 enum TraceSection : int { kTrWait = 0, kTrCompute, kTrRelease, kTrEpilogue, kTrNorm, kTrAttention, kTrIssue,
                           kTrSections };
 constexpr int kTraceBase = 512;
-__device__ unsigned long long g_trace_dummy;
+__shared__ unsigned long long trace_cycles[kTrSections];
 
 struct Trace {
-    unsigned long long* out;
+    bool on;
     long long start;
-    __device__ __forceinline__ void begin() { if (out) start = clock64(); }
+    __device__ __forceinline__ void begin() { if (on) start = clock64(); }
     __device__ __forceinline__ void end(int section) {
-        if (out) out[kTraceBase + section] += (unsigned long long)(clock64() - start);
+        if (on) trace_cycles[section] += (unsigned long long)(clock64() - start);
     }
 };
 __device__ __forceinline__ Trace trace_of(const unsigned long long* profile) {
     Trace t;
-    t.out = (profile != nullptr && blockIdx.x == 0 && threadIdx.x == 0) ? const_cast<unsigned long long*>(profile)
-                                                                           : nullptr;
+    t.on = profile != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
     t.start = 0;
     return t;
+}
+
+// CTA 0's thread 0 adds its section cycles into profile[kTraceBase ...].
+__device__ __forceinline__ void trace_flush(const StepParams& p) {
+    if (p.profile != nullptr && blockIdx.x == 0 && threadIdx.x == 0)
+        for (int i = 0; i < kTrSections; ++i) p.profile[kTraceBase + i] += trace_cycles[i];
 }
 
 template <typename WT>
@@ -294,7 +305,7 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
         // A row or two: the whole CTA on each row, every load of the row,
         // the gains and the offsets in flight at once.
         __shared__ float scratch[kWarps];
-        constexpr int kPer = 6;  // 1536 / 256
+        constexpr int kPer = (1536 + kThreads - 1) / kThreads;
         for (int rl = 0; rl < rows_in_tile; ++rl) {
             const float* x = input + ((size_t)(r0 + rl) * row_step + row_offset) * d;
             float v[kPer], g[kPer], b[kPer];
@@ -416,6 +427,67 @@ __device__ __forceinline__ void product_chunk(const unsigned char* unit, int c, 
     }
 }
 
+// Two chunks, c and c2, against the input rows: all fragments of both are
+// loaded before the first MMA, and the products go to two independent sums
+// (the k-halves alternate), so the warp waits on one MMA latency, not four.
+template <typename WT, int NT, bool X_SHARED>
+__device__ __forceinline__ void product_chunk_pair(const unsigned char* unit, int c, int c2, const WT* X, int ldx,
+                                                   int k0, int k02, const bool (&x_ok)[NT], float (&acc)[NT][4],
+                                                   float (&acc2)[NT][4]) {
+    const int lane = threadIdx.x & 31;
+    const int gq = lane >> 2, tq = lane & 3;
+    const uint4* w = reinterpret_cast<const uint4*>(unit + ((size_t)c * 32 + lane) * 32);
+    const uint4* w2 = reinterpret_cast<const uint4*>(unit + ((size_t)c2 * 32 + lane) * 32);
+    const uint4 lo = w[0], hi = w[1], lo2 = w2[0], hi2 = w2[1];
+    uint4 B[NT], B2[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const WT* row = X + (size_t)(x_ok[j] ? 8 * j + gq : 0) * ldx + 8 * tq;
+        if (!x_ok[j]) {
+            B[j] = B2[j] = make_uint4(0, 0, 0, 0);
+        } else if constexpr (X_SHARED) {
+            B[j] = *reinterpret_cast<const uint4*>(row + k0);
+            B2[j] = *reinterpret_cast<const uint4*>(row + k02);
+        } else {
+            B[j] = ld_cg4(row + k0);
+            B2[j] = ld_cg4(row + k02);
+        }
+    }
+    const uint32_t a0[4] = {lo.x, hi.x, lo.y, hi.y}, a1[4] = {lo.z, hi.z, lo.w, hi.w};
+    const uint32_t c0[4] = {lo2.x, hi2.x, lo2.y, hi2.y}, c1[4] = {lo2.z, hi2.z, lo2.w, hi2.w};
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const uint32_t b0[2] = {B[j].x, B[j].y}, b1[2] = {B[j].z, B[j].w};
+        const uint32_t d0[2] = {B2[j].x, B2[j].y}, d1[2] = {B2[j].z, B2[j].w};
+        mma_16816<WT>(acc[j], a0, b0);
+        mma_16816<WT>(acc2[j], a1, b1);
+        mma_16816<WT>(acc[j], c0, d0);
+        mma_16816<WT>(acc2[j], c1, d1);
+    }
+}
+
+// The warp's chunks c_first, c_first + step, ... (< n) of a unit, k offset
+// k_base + 32 c, two at a time.
+template <typename WT, int NT, bool X_SHARED>
+__device__ __forceinline__ void chunks_product(const unsigned char* unit, int c_first, int step, int n, const WT* X,
+                                               int ldx, int k_base, const bool (&x_ok)[NT], float (&acc)[NT][4]) {
+    float acc2[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc2[j][0] = acc2[j][1] = acc2[j][2] = acc2[j][3] = 0.f;
+    int c = c_first;
+    for (; c + step < n; c += 2 * step)
+        product_chunk_pair<WT, NT, X_SHARED>(unit, c, c + step, X, ldx, k_base + c * 32, k_base + (c + step) * 32,
+                                             x_ok, acc, acc2);
+    if (c < n) product_chunk<WT, NT, X_SHARED>(unit, c, X, ldx, k_base + c * 32, x_ok, acc2);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        acc[j][0] += acc2[j][0];
+        acc[j][1] += acc2[j][1];
+        acc[j][2] += acc2[j][2];
+        acc[j][3] += acc2[j][3];
+    }
+}
+
 // One 16-row tile over all of K: its units come off the weight stream in
 // order, the 8 warps taking alternate chunks of each.  False if a wait gave
 // up (the abort word is then raised and the kernel is on its way out).
@@ -437,8 +509,7 @@ __device__ bool product_tile(const StepParams& p, Stream& s, int kp, const WT* X
         if (!unit) return false;
         Trace tr = trace_of(p.profile);
         tr.begin();
-        for (int c = warp; c < n; c += kWarps)
-            product_chunk<WT, NT, X_SHARED>(unit, c, X, ldx, (c0 + c) * 32, x_ok, acc);
+        chunks_product<WT, NT, X_SHARED>(unit, warp, kWarps, n, X, ldx, c0 * 32, x_ok, acc);
         tr.end(kTrCompute);
         release_unit(s);
     }
@@ -625,7 +696,7 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
                 Trace tr = trace_of(p.profile);
                 tr.begin();
                 const int c0 = b * stage_chunks, n = min(stage_chunks, chunks - c0);
-                for (int c = 0; c < n; ++c) product_chunk<WT, NT, true>(unit, c, xs, pitch, (c0 + c) * 32, x_ok, acc);
+                chunks_product<WT, NT, true>(unit, 0, 1, n, xs, pitch, c0 * 32, x_ok, acc);
                 tr.end(kTrCompute);
                 release_at(s, index, kWarps);
             }
@@ -1082,8 +1153,7 @@ __device__ bool split_product(const StepParams& p, Stream& s, int tiles, const B
             if (!unit) return false;
             Trace tr = trace_of(p.profile);
             tr.begin();
-            for (int c = warp; c < chunks; c += kWarps)
-                product_chunk<WT, 1, true>(unit, c, A.xs, A.pitch, c * 32, x_ok, acc[t]);
+            chunks_product<WT, 1, true>(unit, warp, kWarps, chunks, A.xs, A.pitch, 0, x_ok, acc[t]);
             tr.end(kTrCompute);
             release_unit(s);
         }
@@ -1131,7 +1201,7 @@ __device__ bool tiled_product(const StepParams& p, Stream& s, int tiles, int chu
         for (int tl = warp; tl < nt; tl += kWarps) {
             float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
             const unsigned char* tile = unit + (size_t)tl * chunks * 1024;
-            for (int c = 0; c < chunks; ++c) product_chunk<WT, 1, true>(tile, c, X, ldx, c * 32, x_ok, acc);
+            chunks_product<WT, 1, true>(tile, 0, 1, chunks, X, ldx, 0, x_ok, acc);
             const int n = (t0 + tl) * 16 + gq, rl = 2 * tq;
             emit(n, rl, acc[0][0]);
             emit(n, rl + 1, acc[0][1]);
@@ -1144,22 +1214,50 @@ __device__ bool tiled_product(const StepParams& p, Stream& s, int tiles, int chu
     return true;
 }
 
-// The same over weights read straight from global memory (not streamed).
+// The same over weights read straight from global memory (not streamed):
+// warp w takes tiles w and w+8 together, both tiles' chunks loaded before
+// any MMA, so a pair costs one memory latency.
 template <typename WT, typename Emit>
 __device__ void direct_tiled_product(const unsigned char* weights, int tiles, int chunks, const WT* X, int ldx,
                                      int rows_valid, Emit&& emit) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
     const bool x_ok[1] = {gq < rows_valid};
-    for (int t = warp; t < tiles; t += kWarps) {
-        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-        const unsigned char* tile = weights + (size_t)t * chunks * 1024;
-        for (int c = 0; c < chunks; ++c) product_chunk<WT, 1, true>(tile, c, X, ldx, c * 32, x_ok, acc);
-        const int n = t * 16 + gq, rl = 2 * tq;
+    for (int t = warp; t < tiles; t += 2 * kWarps) {
+        const int t2 = t + kWarps;
+        const bool second = t2 < tiles;
+        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, acc2[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+        const unsigned char* a = weights + (size_t)t * chunks * 1024;
+        const unsigned char* b = weights + (size_t)(second ? t2 : t) * chunks * 1024;
+        int c = 0;
+        for (; c + 1 < chunks; c += 2) {
+            // chunk c and c+1 of both tiles
+            float s1[1][4] = {{0.f, 0.f, 0.f, 0.f}}, s2[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+            product_chunk_pair<WT, 1, true>(a, c, c + 1, X, ldx, c * 32, (c + 1) * 32, x_ok, acc, s1);
+            product_chunk_pair<WT, 1, true>(b, c, c + 1, X, ldx, c * 32, (c + 1) * 32, x_ok, acc2, s2);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                acc[0][e] += s1[0][e];
+                acc2[0][e] += s2[0][e];
+            }
+        }
+        if (c < chunks) {
+            product_chunk<WT, 1, true>(a, c, X, ldx, c * 32, x_ok, acc);
+            product_chunk<WT, 1, true>(b, c, X, ldx, c * 32, x_ok, acc2);
+        }
+        const int rl = 2 * tq;
+        int n = t * 16 + gq;
         emit(n, rl, acc[0][0]);
         emit(n, rl + 1, acc[0][1]);
         emit(n + 8, rl, acc[0][2]);
         emit(n + 8, rl + 1, acc[0][3]);
+        if (second) {
+            n = t2 * 16 + gq;
+            emit(n, rl, acc2[0][0]);
+            emit(n, rl + 1, acc2[0][1]);
+            emit(n + 8, rl, acc2[0][2]);
+            emit(n + 8, rl + 1, acc2[0][3]);
+        }
     }
 }
 
@@ -1242,8 +1340,7 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
             }
         } else {
             const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-            if (warp < rows_valid) {
-                const int rl = warp;
+            for (int rl = warp; rl < rows_valid; rl += kWarps) {
                 const size_t base = (size_t)(r0 + rl) * p.max_positions * d + (size_t)head * D;
                 float* row = A.res + warp * 64;
                 const float2 ml = warp_attention<WT, false>(A.q + rl * 64, static_cast<const WT*>(op.self_keys) + base,
@@ -1325,8 +1422,7 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
             }
         } else {
             const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-            if (warp < rows_valid) {
-                const int rl = warp;
+            for (int rl = warp; rl < rows_valid; rl += kWarps) {
                 const size_t base = (size_t)(r0 + rl) * op.window_stride + (size_t)head * D;
                 float* out = partial_of(rl);
                 if (n_keys > 0) {
@@ -1455,6 +1551,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
     s.next = 0;
     if (threadIdx.x == 0) {
         stop_flag = 0;
+        for (int i = 0; i < kTrSections; ++i) trace_cycles[i] = 0;
         for (int i = 0; i < s.stages; ++i) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(s.full + i)) : "memory");
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_address(s.empty + i)), "r"(kWarps)
@@ -1487,6 +1584,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
             case kOpFeedForwardBlock: op_ffn_block<WT, NT>(p, op, s, work); break;
             }
             if (!grid_barrier(p.barrier, epoch, p.state)) {
+                trace_flush(p);
                 if (threadIdx.x == 0) *stop = 1;
                 return;
             }
@@ -1494,6 +1592,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
         }
         if (p.stop_enabled && ld_volatile(p.state + kAllEnded)) break;
     }
+    trace_flush(p);
     if (threadIdx.x == 0) *stop = 1;
 }
 
