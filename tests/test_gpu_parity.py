@@ -68,8 +68,12 @@ def test_teacher_forced_steps_match_the_oracle(config, storage, steps):
           f"{decided} greedy ids decided by the margin")
 
 
-@pytest.mark.parametrize("config,storage,steps", [("tiny_en_b1", "float16", 40)])
-def test_greedy_transcript_follows_the_oracle(config, storage, steps):
+@pytest.mark.parametrize("config,storage,steps", [("tiny_en_b1", "float16", 40), ("base_en_b1", "bfloat16", 16)])
+@pytest.mark.parametrize("path", ["general", "fused"])
+def test_greedy_transcript_follows_the_oracle(config, storage, steps, path, monkeypatch):
+    """Both single-token step forms: the general op list (the default) and
+    the fused per-layer blocks (WSP_SINGLE_TOKEN_PATH=fused)."""
+    monkeypatch.setenv("WSP_SINGLE_TOKEN_PATH", path)
     run = S.CONFIGS[config]
     shape = run.shape
     tensors = stored_tensors(S.normal_weights(shape, seed=21), storage)
@@ -130,3 +134,33 @@ def test_batched_windows_follow_the_oracle():
         for k in range(1, 12):
             _, logits = session.step([int(together[b][k - 1])])
             check_tokens([together[b][k]], logits, later)
+
+
+def test_wide_batched_windows_follow_the_oracle():
+    """Forty windows of a 1024-wide decoder with the full vocabulary: 32 KB
+    weight-stream stages leave room for fewer stages than warps, the logits
+    run as two row tiles with each warp owning every seventh vocabulary tile,
+    and the general (unfused) single-token step runs.  Each window's
+    transcript, replayed through the oracle, is its greedy choice wherever
+    the margin decides it."""
+    from whispereacp_b200.decoder import DecoderShape
+    shape = DecoderShape(width=1024, heads=16, layers=1, feed_forward_width=1024, vocabulary_size=51864,
+                         max_positions=32, cross_positions=24)
+    windows, steps = 40, 5
+    prompt = S.CONFIGS["medium_en_b64"].prompt
+    tensors = stored_tensors(S.normal_weights(shape, seed=51), "float16")
+    encoders = S.encoder_output(windows, shape.cross_positions, shape.width, seed=52)
+    first, later = S.suppression_masks(shape.vocabulary_size)
+    batched = make_decoder(oracle_shape(shape), tensors, windows=windows)
+    batched.set_generation(prompt, first, later, maximum_tokens=steps, stop_at_end_of_text=False)
+    together = batched.transcribe(encoders)
+    decided = 0
+    for b in range(windows):
+        session = O.Session(oracle_shape(shape), tensors, threads=THREADS)
+        session.begin(encoders[b])
+        _, logits = session.step(list(prompt))
+        decided += check_tokens([together[b][0]], logits[-1:], first)
+        for k in range(1, steps):
+            _, logits = session.step([int(together[b][k - 1])])
+            decided += check_tokens([together[b][k]], logits, later)
+    assert decided > windows * steps // 2

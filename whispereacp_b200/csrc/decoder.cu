@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -691,8 +692,16 @@ private:
         CUDA_CHECK(cudaMemcpy(state, state_.get(), sizeof state, cudaMemcpyDeviceToHost));
         if (state[kError] != 0) {
             CUDA_CHECK(cudaMemset(state_.get<int>() + kError, 0, sizeof(int)));
-            if (state[kError] & kErrBarrierTimeout)
-                throw CudaFailure("the decode kernel gave up waiting at a grid barrier", false);
+            if (state[kError] & kErrBarrierTimeout) {
+                static const char* const kinds[] = {"?", "a grid barrier", "a weight unit", "a free stage",
+                                                    "a landing copy", "an armed stage"};
+                const int kind = state[kFailKind] >= 1 && state[kFailKind] <= 5 ? state[kFailKind] : 0;
+                CUDA_CHECK(cudaMemset(state_.get<int>() + kFailKind, 0, 3 * sizeof(int)));
+                throw CudaFailure(std::string("the decode kernel gave up waiting for ") + kinds[kind] + " (CTA " +
+                                      std::to_string(state[kFailCta]) + ", index " +
+                                      std::to_string(state[kFailWhere]) + ")",
+                                  false);
+            }
             throw ModelError("a sampled or supplied token id fell outside the vocabulary");
         }
     }
@@ -891,6 +900,15 @@ private:
         return ops;
     }
 
+    // The general op list is the default single-token step: measured on
+    // B200 it beats the fused blocks at every configuration from tiny.en B1
+    // to large-v3 B128.  WSP_SINGLE_TOKEN_PATH=fused selects the blocks
+    // (both compute the same step; kept for measurement).
+    bool use_fused_blocks() const {
+        const char* forced = std::getenv("WSP_SINGLE_TOKEN_PATH");
+        return forced && std::string(forced) == "fused";
+    }
+
     // The weight-stream schedule of every CTA (schedule.h), into device memory.
     void upload_schedule(StepParams& p, const std::vector<StepOp>& ops, int grid) {
         build_schedule(p, ops, grid, decode_tile_rows(p), schedule_host_, offsets_host_);
@@ -1005,8 +1023,7 @@ private:
         StepParams p = base_params(T, sample, mask, logits, hidden, row_tokens, steps, stop);
         p.profile = profile;
         const bool half = storage_ == Storage::f16;
-        // Single-token sampled steps run as fused blocks (step.cuh).
-        const bool fused = sample && T == 1 && fc_ > 0;
+        const bool fused = sample && T == 1 && fc_ > 0 && use_fused_blocks();
         configure_stream(half, p, fused);
         const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk, fused);
         if (blocks <= 0) throw CudaFailure("the decode kernel does not fit on an SM", false);

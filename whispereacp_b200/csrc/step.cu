@@ -129,6 +129,16 @@ constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
 // waits, with acquire loads, until every CTA has arrived `epoch` times.  The
 // wait gives up after kWaitTimeoutNs (or as soon as another CTA gave up): it
 // records kErrBarrierTimeout, raises the abort word and the kernel returns.
+// Records the first wait that gave up: its kind, CTA and op/unit index.
+__device__ __forceinline__ void record_timeout(int* state, int kind, long long where) {
+    atomicOr(state + kError, kErrBarrierTimeout);
+    if (atomicCAS(state + kFailKind, 0, kind) == 0) {
+        state[kFailCta] = (int)blockIdx.x;
+        state[kFailWhere] = (int)where;
+    }
+    atomicExch(state + kAbort, 1);
+}
+
 __device__ bool grid_barrier(unsigned* count, unsigned& epoch, int* state) {
     __shared__ int aborted;
     consumer_sync();
@@ -140,8 +150,7 @@ __device__ bool grid_barrier(unsigned* count, unsigned& epoch, int* state) {
         while (ld_acquire(count) < target) {
             if (ld_volatile(state + kAbort)) break;
             if (global_ns() - start > kWaitTimeoutNs) {
-                atomicOr(state + kError, kErrBarrierTimeout);
-                atomicExch(state + kAbort, 1);
+                record_timeout(state, kWaitGrid, (long long)epoch);
                 break;
             }
         }
@@ -173,6 +182,7 @@ struct Stream {
     int stages;
     int stage_bytes;
     unsigned long long next;      // the next unit this CTA's consumers reach
+    volatile unsigned long long* armed;  // units the producer has armed full[] for
 };
 
 __device__ __forceinline__ bool try_parity(uint64_t* bar, uint32_t parity) {
@@ -190,14 +200,14 @@ __device__ __forceinline__ bool try_parity(uint64_t* bar, uint32_t parity) {
 // Waits for the phase of `parity` to complete, for at most kWaitTimeoutNs;
 // gives up early when *stop is raised.  On a timeout it records
 // kErrBarrierTimeout and raises the abort word.
-__device__ bool wait_parity(const StepParams& p, uint64_t* bar, uint32_t parity, const volatile int* stop) {
+__device__ bool wait_parity(const StepParams& p, uint64_t* bar, uint32_t parity, const volatile int* stop, int kind,
+                            unsigned long long index) {
     if (try_parity(bar, parity)) return true;
     const unsigned long long start = global_ns();
     while (!try_parity(bar, parity)) {
         if (stop && *stop) return false;
         if (global_ns() - start > kWaitTimeoutNs) {
-            atomicOr(p.state + kError, kErrBarrierTimeout);
-            atomicExch(p.state + kAbort, 1);
+            record_timeout(p.state, kind, (long long)index);
             return false;
         }
     }
@@ -211,9 +221,32 @@ __device__ __forceinline__ const unsigned char* unit_at(const StepParams& p, con
     Trace tr = trace_of(p.profile);
     tr.begin();
     const int stage = (int)(index % s.stages);
-    wait_parity(p, s.full + stage, (uint32_t)((index / s.stages) & 1), nullptr);
+    wait_parity(p, s.full + stage, (uint32_t)((index / s.stages) & 1), nullptr, kWaitUnit, index);
     tr.end(kTrWait);
     return s.ring + (size_t)stage * s.stage_bytes;
+}
+
+// A warp that owns whole units (the logits) skips the units between its own,
+// so it may reach unit `index` before unit index - stages, which shares the
+// stage, has landed; the stage's parity would then read as index's.  Once the
+// producer has armed full[] for `index` (after index - stages was released,
+// so after it landed), the parity names `index` alone: wait for that first.
+__device__ __forceinline__ const unsigned char* owned_unit_at(const StepParams& p, const Stream& s,
+                                                              unsigned long long index) {
+    if (*s.armed <= index) {
+        Trace tr = trace_of(p.profile);
+        tr.begin();
+        const unsigned long long start = global_ns();
+        while (*s.armed <= index) {
+            if (global_ns() - start > kWaitTimeoutNs) {
+                record_timeout(p.state, kWaitArmed, (long long)index);
+                break;
+            }
+        }
+        tr.end(kTrWait);
+    }
+    __threadfence_block();
+    return unit_at(p, s, index);
 }
 
 // Consumers: this warp is done with unit `index` (its share of it, or the
@@ -247,7 +280,7 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
         for (unsigned i = 0; i < count; ++i, ++u) {
             const int stage = (int)(u % s.stages);
             if (u >= (unsigned long long)s.stages &&
-                !wait_parity(p, s.empty + stage, (uint32_t)((u / s.stages - 1) & 1), stop)) {
+                !wait_parity(p, s.empty + stage, (uint32_t)((u / s.stages - 1) & 1), stop, kWaitEmpty, u)) {
                 go = false;
                 break;
             }
@@ -260,11 +293,13 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
                 "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
                 "l"(e.x), "r"(bytes), "r"(bar)
                 : "memory");
+            __threadfence_block();
+            *s.armed = u + 1;
         }
     }
     const unsigned long long stages = (unsigned long long)s.stages;
     for (unsigned long long v = u > stages ? u - stages : 0; v < u; ++v)
-        if (!wait_parity(p, s.full + v % stages, (uint32_t)((v / stages) & 1), nullptr)) break;
+        if (!wait_parity(p, s.full + v % stages, (uint32_t)((v / stages) & 1), nullptr, kWaitDrain, v)) break;
 }
 
 // -------------------------------------------------------------------- embed
@@ -296,10 +331,13 @@ constexpr int kNormMaxPerLane = 48;  // widths up to 1536
 // output row rl reads h row (r0 + rl)*row_step + row_offset.  One warp a row,
 // the row in registers: the mean, then the centred variance, as
 // LayerNorm.h:19-98 does.  hidden_out, when given, receives the fp32 rows.
+// forward_to, when given, also receives input + forward_bias for every
+// element read, by fp32 reduction: the residual and the bias a fused block
+// adds into the next residual buffer once per row.
 template <typename WT>
 __device__ void layer_norm_tile(const StepParams& p, const float* input, const float* gamma, const float* beta,
                                 int r0, int rows_in_tile, int row_step, int row_offset, WT* xs, int ldx,
-                                float* hidden_out) {
+                                float* hidden_out, float* forward_to = nullptr, const float* forward_bias = nullptr) {
     const int d = p.width;
     if (rows_in_tile <= 2) {
         // A row or two: the whole CTA on each row, every load of the row,
@@ -315,6 +353,13 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
                 v[i] = c < d ? ld_cg(x + c) : 0.f;
                 g[i] = c < d ? __ldg(gamma + c) : 0.f;
                 b[i] = c < d ? __ldg(beta + c) : 0.f;
+            }
+            if (forward_to) {
+#pragma unroll
+                for (int i = 0; i < kPer; ++i) {
+                    const int c = threadIdx.x + i * kThreads;
+                    if (c < d) atomicAdd(forward_to + (size_t)(r0 + rl) * d + c, v[i] + __ldg(forward_bias + c));
+                }
             }
             float total = 0.f;
 #pragma unroll
@@ -351,6 +396,13 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
         for (int i = 0; i < kNormMaxPerLane; ++i) {
             const int c = lane + 32 * i;
             v[i] = c < d ? ld_cg(x + c) : 0.f;
+        }
+        if (forward_to) {
+#pragma unroll
+            for (int i = 0; i < kNormMaxPerLane; ++i) {
+                const int c = lane + 32 * i;
+                if (c < d) atomicAdd(forward_to + (size_t)(r0 + rl) * d + c, v[i] + __ldg(forward_bias + c));
+            }
         }
         float total = 0.f;
 #pragma unroll
@@ -692,7 +744,7 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
             for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
             for (int b = 0; b < blocks; ++b) {
                 const unsigned long long index = base + (unsigned long long)(mine + k) * blocks + b;
-                const unsigned char* unit = unit_at(p, s, index);
+                const unsigned char* unit = owned_unit_at(p, s, index);
                 Trace tr = trace_of(p.profile);
                 tr.begin();
                 const int c0 = b * stage_chunks, n = min(stage_chunks, chunks - c0);
@@ -1299,11 +1351,13 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
     for (int item = blockIdx.x; item < H * r_tiles; item += gridDim.x) {
         const int head = item % H, r_tile = item / H;
         const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
-        if (cached != r_tile) {
+        // Head 0's item also forwards X0 + the out_proj bias into X1.
+        if (cached != r_tile || head == 0) {
             consumer_sync();
             Trace trn = trace_of(p.profile);
             trn.begin();
-            layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
+            layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr,
+                                head == 0 ? p.x1 : nullptr, op.bias2);
             consumer_sync();
             trn.end(kTrNorm);
             cached = r_tile;
@@ -1352,17 +1406,14 @@ __device__ void op_self_block(const StepParams& p, const StepOp& op, int positio
             consumer_sync();
         }
         tra.end(kTrAttention);
-        // X1 += the head's slice of out_proj; head 0 adds the bias and X0.
-        const bool first = head == 0;
+        // X1 += the head's slice of out_proj.
         if (!tiled_product<WT, NT>(p, s, round16(d) / 16, op.kp2 / 32, op.group2, A.o16, ps, rows_valid,
                                    [&](int n, int rl, float v) {
                                        if (n >= d || rl >= rows_valid) return;
-                                       const size_t at = (size_t)(r0 + rl) * d + n;
-                                       if (first) v += __ldg(op.bias2 + n) + ld_cg(p.h + at);
-                                       atomicAdd(p.x1 + at, v);
+                                       atomicAdd(p.x1 + (size_t)(r0 + rl) * d + n, v);
                                    }))
             return;
-        if (first) zero_rows(p.x2, r0, rows_valid, d);
+        if (head == 0) zero_rows(p.x2, r0, rows_valid, d);
         consumer_sync();
     }
 }
@@ -1381,11 +1432,14 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
     for (int item = blockIdx.x; item < H * r_tiles * S; item += gridDim.x) {
         const int split = item % S, head = (item / S) % H, r_tile = item / (S * H);
         const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
-        if (cached != r_tile) {
+        // Item (head 0, split 0) also forwards X1 + the out_proj bias into X2.
+        const bool forward = head == 0 && split == 0;
+        if (cached != r_tile || forward) {
             consumer_sync();
             Trace trn = trace_of(p.profile);
             trn.begin();
-            layer_norm_tile<WT>(p, p.x1, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
+            layer_norm_tile<WT>(p, p.x1, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr,
+                                forward ? p.x2 : nullptr, op.bias2);
             consumer_sync();
             trn.end(kTrNorm);
             cached = r_tile;
@@ -1473,16 +1527,13 @@ __device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s,
             A.o16[rl * ps + c] = Half16<WT>::from_float(y);
         }
         consumer_sync();
-        // X2 += the head's slice of out_proj; head 0 adds the bias and X1.
-        const bool first = head == 0;
+        // X2 += the head's slice of out_proj.
         Trace trd = trace_of(p.profile);
         trd.begin();
         direct_tiled_product<WT>(static_cast<const unsigned char*>(op.weight2) + (size_t)head * op.item_stride2,
                                  round16(d) / 16, op.kp2 / 32, A.o16, ps, rows_valid, [&](int n, int rl, float v) {
                                      if (n >= d || rl >= rows_valid) return;
-                                     const size_t at = (size_t)(r0 + rl) * d + n;
-                                     if (first) v += __ldg(op.bias2 + n) + ld_cg(p.x1 + at);
-                                     atomicAdd(p.x2 + at, v);
+                                     atomicAdd(p.x2 + (size_t)(r0 + rl) * d + n, v);
                                  });
         consumer_sync();
         trd.end(kTrEpilogue);
@@ -1501,11 +1552,13 @@ __device__ void op_ffn_block(const StepParams& p, const StepOp& op, Stream& s, u
     for (int item = blockIdx.x; item < chunks_n * r_tiles; item += gridDim.x) {
         const int j = item % chunks_n, r_tile = item / chunks_n;
         const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
-        if (cached != r_tile) {
+        // Chunk 0's item also forwards X2 + the fc2 bias into X0.
+        if (cached != r_tile || j == 0) {
             consumer_sync();
             Trace trn = trace_of(p.profile);
             trn.begin();
-            layer_norm_tile<WT>(p, p.x2, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr);
+            layer_norm_tile<WT>(p, p.x2, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr,
+                                j == 0 ? p.h : nullptr, op.bias2);
             consumer_sync();
             trn.end(kTrNorm);
             cached = r_tile;
@@ -1518,17 +1571,14 @@ __device__ void op_ffn_block(const StepParams& p, const StepOp& op, Stream& s, u
             A.o16[rl * ps + c] = Half16<WT>::from_float(v);
         }
         consumer_sync();
-        // X0 += the fc2 slice of this chunk; chunk 0 adds the bias and X2.
-        const bool first = j == 0;
+        // X0 += the fc2 slice of this chunk.
         if (!tiled_product<WT, NT>(p, s, round16(d) / 16, op.kp2 / 32, op.group2, A.o16, ps, rows_valid,
                                    [&](int n, int rl, float v) {
                                        if (n >= d || rl >= rows_valid) return;
-                                       const size_t at = (size_t)(r0 + rl) * d + n;
-                                       if (first) v += __ldg(op.bias2 + n) + ld_cg(p.x2 + at);
-                                       atomicAdd(p.h + at, v);
+                                       atomicAdd(p.h + (size_t)(r0 + rl) * d + n, v);
                                    }))
             return;
-        if (first) zero_rows(p.x1, r0, rows_valid, d);
+        if (j == 0) zero_rows(p.x1, r0, rows_valid, d);
         consumer_sync();
     }
 }
@@ -1541,6 +1591,7 @@ template <typename WT, int NT>
 __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int stop_flag;
+    __shared__ unsigned long long armed_units;
     Stream s;
     s.stages = p.stages;
     s.stage_bytes = p.stage_bytes;
@@ -1549,8 +1600,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
     s.empty = s.full + kMaxStages;
     unsigned char* work = smem + (size_t)s.stages * s.stage_bytes + 16 * kMaxStages;
     s.next = 0;
+    s.armed = &armed_units;
     if (threadIdx.x == 0) {
         stop_flag = 0;
+        armed_units = 0;
         for (int i = 0; i < kTrSections; ++i) trace_cycles[i] = 0;
         for (int i = 0; i < s.stages; ++i) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(s.full + i)) : "memory");

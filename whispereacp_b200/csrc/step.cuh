@@ -60,8 +60,14 @@ enum OpKind : int {
 };
 enum EpilogueKind : int { kEpQkv = 0, kEpStore = 1, kEpResidual = 2, kEpGelu = 3 };
 
-// state words (int): position, error bits, abort, steps done, all windows ended
-enum StateWord : int { kPosition = 0, kError = 1, kAbort = 2, kStepsDone = 3, kAllEnded = 4, kStateWords = 8 };
+// state words (int): position, error bits, abort, steps done, all windows
+// ended, and where the first bounded wait gave up: its kind (WaitKind), CTA,
+// and op or unit index
+enum StateWord : int {
+    kPosition = 0, kError = 1, kAbort = 2, kStepsDone = 3, kAllEnded = 4,
+    kFailKind = 5, kFailCta = 6, kFailWhere = 7, kStateWords = 8
+};
+enum WaitKind : int { kWaitGrid = 1, kWaitUnit = 2, kWaitEmpty = 3, kWaitDrain = 4, kWaitArmed = 5 };
 enum ErrorBit : int { kErrToken = 1, kErrBarrierTimeout = 2 };
 
 // Weight matrices are stored fragment-packed: the 16-row tiles of an [n, kp]
