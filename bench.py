@@ -48,6 +48,8 @@ def parse_args():
     p.add_argument("--config", default=DEFAULT_CONFIG)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--tokens", type=int, default=0,
+                   help="tokens per window (default: the config's); smaller for profiler captures")
     return p.parse_args()
 
 
@@ -125,11 +127,12 @@ def peaks():
 
 
 def committed_traffic(kernel: str, config: str):
-    """dram bytes per launch of `kernel` from the committed ncu summary, if any."""
+    """DRAM bytes (read + write) per single-token step of `kernel` from the
+    committed ncu summary of that kernel and config, if there is one."""
     path = os.path.join(ROOT, "profiles", f"{kernel}_{config}.md")
     if not os.path.exists(path):
         return None
-    match = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    match = re.search(r"traffic_bytes_per_step:\s*([0-9.eE+]+)", open(path).read())
     return float(match.group(1)) if match else None
 
 
@@ -173,6 +176,7 @@ def cpu_baseline_port(run, tensors, encoder, threads: int) -> dict:
 def run_ours(args, run):
     import torch
     from whispereacp_b200 import Decoder, synthetic as S
+    from whispereacp_b200.ranks import max_over_ranks
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -182,13 +186,14 @@ def run_ours(args, run):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
 
     shape = run.shape
+    tokens_per_window = args.tokens or run.steps
     tensors = S.normal_weights(shape, seed=0)
     encoder = S.encoder_output(run.windows, shape.cross_positions, shape.width, seed=1 + rank)
     first, later = S.suppression_masks(shape.vocabulary_size)
 
     decoder = Decoder(shape, windows=run.windows, device=local, storage=run.storage)
     decoder.load_weights(tensors)
-    decoder.set_generation(run.prompt, first, later, maximum_tokens=run.steps,
+    decoder.set_generation(run.prompt, first, later, maximum_tokens=tokens_per_window,
                            end_of_text=S.END_OF_TEXT, stop_at_end_of_text=False)
     stream = torch.cuda.ExternalStream(decoder.stream, device=local)
     device_rows = torch.from_numpy(encoder).to(f"cuda:{local}")
@@ -196,7 +201,7 @@ def run_ours(args, run):
     torch.cuda.synchronize()
 
     def one_step():
-        decoder.enqueue_transcribe(device_rows.data_ptr(), run.steps)
+        decoder.enqueue_transcribe(device_rows.data_ptr(), tokens_per_window)
 
     for _ in range(args.warmup):
         one_step()
@@ -209,12 +214,16 @@ def run_ours(args, run):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     clocks.start()
+    phases = []
     for i in range(args.steps):
         with torch.cuda.stream(stream):
             flush.zero_()              # L2 flush, outside the timed intervals
             starts[i].record(stream)
         one_step()
         stops[i].record(stream)
+        # The step's own launches, from the decoder's CUDA events on the same
+        # stream (this waits for the step; the next flush is queued after).
+        phases.append(decoder.phase_ms())
     decoder.synchronize()
     torch.cuda.synchronize()
     clock_record = clocks.stop()
@@ -222,7 +231,7 @@ def run_ours(args, run):
         torch.distributed.barrier()
     elapsed_ms = sum(s.elapsed_time(e) for s, e in zip(starts, stops))
     transcript = decoder.read_transcript()
-    assert all(len(t) == run.steps for t in transcript)
+    assert all(len(t) == tokens_per_window for t in transcript)
 
     # End to end through the public call: pinned host rows in, token ids out.
     pinned = torch.from_numpy(encoder).pin_memory()
@@ -240,32 +249,28 @@ def run_ours(args, run):
 
     # Per-kernel launch durations, measured live (events around each launch).
     decoder.enqueue_transcribe(device_rows.data_ptr(), 2)
-    per_kernel = decoder.time_kernels(min(64, shape.max_positions - len(run.prompt) - 2))
+    per_kernel = decoder.time_kernels(min(64, shape.max_positions - len(run.prompt) - 2, tokens_per_window))
     decoder.synchronize()
 
     step_ms = elapsed_ms / args.steps
-    if world > 1:
-        t = torch.tensor([step_ms, e2e_step_ms], device=f"cuda:{local}")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        step_ms, e2e_step_ms = t.tolist()
+    # The slowest rank's device-timed step (an all-reduce MAX over NCCL).
+    step_ms, e2e_step_ms = max_over_ranks([step_ms, e2e_step_ms], device=f"cuda:{local}")
 
-    tokens = run.windows * run.steps * world
+    tokens = run.windows * tokens_per_window * world
     result = None
     if rank == 0:
         peak, peak_kind = peaks()
-        mean_keys = len(run.prompt) + run.steps / 2
+        # The dominant kernel: the decode kernel's launch that runs every
+        # single-token step of the transcription (the prompt launch and the
+        # sequence start are the rest of the step).
+        later_steps = tokens_per_window - 1
+        mean_keys = len(run.prompt) + later_steps / 2
         nbytes = step_bytes(run, mean_keys)
-        launches = per_kernel
-        # The dominant phase of a single-token step (the decode kernel stamps
-        # %globaltimer after every op): the class with the largest share.
-        share = {k: v[0] * v[1] for k, v in launches.items()}
-        dominant = max(share, key=share.get)
-        algorithmic = {"logits_argmax": nbytes["logits_launch"], "cross_attention": nbytes["cross_launch"],
-                       "projection": nbytes["projection_launch"],
-                       "self_attention": nbytes["self_launch"]}.get(dominant, 0)
-        duration = launches[dominant][0]
-        achieved = algorithmic / (duration * 1e-3) / 1e9 if duration > 0 else 0.0
-        step_ms_single = sum(v[0] * v[1] for v in launches.values())
+        per_step_bytes = nbytes["weights"] + nbytes["kv"]
+        launch_ms = statistics.median(p["steps"] for p in phases)
+        algorithmic = later_steps * per_step_bytes
+        achieved = algorithmic / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else 0.0
+        traffic_step = committed_traffic("decode_kernel", run.name)
         h2d = encoder.nbytes
         d2h = run.windows * (shape.max_positions + 1) * 4
         result = {
@@ -275,27 +280,27 @@ def run_ours(args, run):
             "vs_baseline": None, "dtype": "f16" if run.storage == "float16" else "bf16",
             "data": "synthetic (random-init weights N(0,0.02), encoder rows N(0,1))",
             "config": {"workload": run.description, "name": run.name, "windows_per_gpu": run.windows,
-                       "tokens_per_window": run.steps, "prompt": list(run.prompt),
+                       "tokens_per_window": tokens_per_window, "prompt": list(run.prompt),
                        "cross_positions": shape.cross_positions, "d_model": shape.width,
                        "decoder_layers": shape.layers, "vocabulary": shape.vocabulary_size,
                        "step": "sequence start + prompt step + greedy single-token steps (one persistent launch)",
                        "l2": "flushed (256 MiB write) between timed steps, outside the timed intervals",
                        "parallelism": f"dp{world} (independent windows per GPU)"},
-            "batch1_ms_per_token_step": step_ms / run.steps,
+            "batch1_ms_per_token_step": launch_ms / max(1, later_steps),
             "e2e": {"value": tokens / (e2e_step_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * decoder.step_launches(),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": committed_traffic(dominant, run.name),
-                         "kernel": dominant, "peak_source": f"{peak_kind} hbm_gbs (burst)",
+                         "frac": achieved / peak,
+                         "traffic": traffic_step * later_steps if traffic_step else None,
+                         "kernel": "decode_kernel (launch of the single-token steps)",
+                         "peak_source": f"{peak_kind} hbm_gbs (burst)",
                          "algorithmic_bytes_per_launch": algorithmic,
-                         "launch_ms": duration},
-            "step_roofline": {"algorithmic_bytes": nbytes["weights"] + nbytes["kv"],
-                              "single_step_ms_profiled": step_ms_single,
-                              "graph_step_ms": step_ms / run.steps,
-                              "frac_of_peak": (nbytes["weights"] + nbytes["kv"]) /
-                              (step_ms / run.steps * 1e-3) / 1e9 / peak},
-            "phases_ms": {k: {"ms_per_op": v[0], "ops_per_step": v[1]} for k, v in launches.items() if v[1]},
+                         "algorithmic_bytes_per_token_step": per_step_bytes,
+                         "token_steps_per_launch": later_steps, "launch_ms": launch_ms},
+            "phases_ms": {k: statistics.median(p[k] for p in phases) for k in phases[0]},
+            "op_classes_us": {k: {"us_per_op": v[0] * 1e3, "ops_per_token_step": v[1]}
+                              for k, v in per_kernel.items() if v[1]},
             "clocks": clock_record,
         }
         if not args.no_cpu_baseline:

@@ -154,7 +154,9 @@ int wsp_decoder_set_generation(wsp_decoder* decoder, const wsp_generation_config
  * (Whisper.cpp:1375-1377).  tokens receives uint32 [windows, step limit] (the
  * sampled ids, end-of-text excluded) and counts int32 [windows] (each
  * window's transcript length: up to its first end-of-text when stopping on
- * it).  The single-token step runs as one CUDA graph.
+ * it).  The prompt is one launch of the persistent decode kernel and every
+ * later step runs inside a second launch, which samples each window's id
+ * into the token ring the next step embeds, with no host round trip.
  */
 int wsp_decoder_transcribe(wsp_decoder* decoder, const float* encoder_rows,
                            int cross_positions, uint32_t* tokens, int32_t* counts);
@@ -205,6 +207,15 @@ int wsp_decoder_time_barriers(wsp_decoder* decoder, int count, float* microsecon
  * run; `count` entries (7 are defined).
  */
 int wsp_decoder_trace_cycles(const wsp_decoder* decoder, double* cycles, int count);
+
+/*
+ * Milliseconds of the last transcription's three phases, from CUDA events on
+ * the decoder's stream: ms[0] the sequence start (encoder-row narrowing and
+ * the cross K/V product), ms[1] the prompt step's launch, ms[2] the launch
+ * that runs every later step (0 when there was none).  Waits for them.
+ * Measurement only; no counterpart in the reference.
+ */
+int wsp_decoder_phase_ms(wsp_decoder* decoder, float* ms);
 
 /* Kernel launches of this library per transcription (wsp_decoder_transcribe). */
 int wsp_decoder_step_launches(const wsp_decoder* decoder, int* launches);

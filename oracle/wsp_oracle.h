@@ -30,7 +30,7 @@
  *
  * Parity pin: oracle/Makefile compiles the reference's own scalar decoder
  * from the lines where they lie in the reference checkout into
- * oracle/_ref/libref_oracle.so, and tests/golden/make_golden.py uses it to
+ * oracle/_ref/libref_decoder.so, and tests/golden/make_golden.py uses it to
  * write the fixtures this oracle is checked against.
  */
 #ifndef WSP_ORACLE_H

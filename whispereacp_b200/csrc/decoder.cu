@@ -155,6 +155,7 @@ public:
         CUDA_CHECK(cudaDeviceGetAttribute(&max_shared_, cudaDevAttrMaxSharedMemoryPerBlockOptin, device_));
         cublas_check(cublasCreate(&cublas_), "cublasCreate");
         cublas_check(cublasSetStream(cublas_, stream_), "cublasSetStream");
+        for (cudaEvent_t& e : phase_events_) CUDA_CHECK(cudaEventCreate(&e));
         allocate_weights();
         allocate_state();
         ensure_row_capacity(4);
@@ -163,6 +164,8 @@ public:
     ~Decoder() {
         cudaSetDevice(device_);
         if (cublas_) cublasDestroy(cublas_);
+        for (cudaEvent_t e : phase_events_)
+            if (e) cudaEventDestroy(e);
         if (stream_) cudaStreamDestroy(stream_);
     }
 
@@ -415,13 +418,17 @@ public:
     // prompt in one step, sampling under the first-step mask.
     void enqueue_start(const float* encoder_rows, int cross_positions) {
         if (!generation_set_) throw LogicError("set the generation config before transcribing");
+        CUDA_CHECK(cudaEventRecord(phase_events_[0], stream_));
         begin_sequence(encoder_rows, cross_positions);
+        CUDA_CHECK(cudaEventRecord(phase_events_[1], stream_));
         CUDA_CHECK(cudaMemcpyAsync(ring_.get(), ring_prompt_.get(), ring_prompt_.bytes(), cudaMemcpyDeviceToDevice,
                                    stream_));
         CUDA_CHECK(cudaMemsetAsync(ended_.get(), 0, ended_.bytes(), stream_));
         ensure_row_capacity((int)prompt_.size());
         launch_steps((int)prompt_.size(), /*sample=*/true, masks_.get<float>(), nullptr, nullptr, nullptr, 1,
                      stop_at_end_of_text_, nullptr);
+        CUDA_CHECK(cudaEventRecord(phase_events_[2], stream_));
+        CUDA_CHECK(cudaEventRecord(phase_events_[3], stream_));
         position_ = (int)prompt_.size();
         sampled_steps_ = 1;
         queued_steps_ = 0;
@@ -435,6 +442,7 @@ public:
         if (position_ + steps > shape_.max_positions) throw ModelError("the window is full");
         launch_steps(1, /*sample=*/true, masks_.get<float>() + shape_.vocabulary_size, nullptr, nullptr, nullptr,
                      steps, stop_at_end_of_text_, nullptr);
+        CUDA_CHECK(cudaEventRecord(phase_events_[3], stream_));
         position_ += steps;
         queued_steps_ += steps;
     }
@@ -566,6 +574,16 @@ public:
     // Section cycles of CTA 0 per step, from the last time_kernels run.
     void trace_cycles(double* out, int count) const {
         for (int i = 0; i < count; ++i) out[i] = i < (int)trace_cycles_.size() ? trace_cycles_[i] : 0.0;
+    }
+
+    // Milliseconds of the last transcription's phases, from CUDA events on
+    // the decoder's stream: the sequence start (encoder-row narrowing and the
+    // cross K/V product), the prompt step's launch, and the launch that runs
+    // every later step (0 when there was none).
+    void phase_ms(float* ms) {
+        CUDA_CHECK(cudaSetDevice(device_));
+        CUDA_CHECK(cudaEventSynchronize(phase_events_[3]));
+        for (int i = 0; i < 3; ++i) CUDA_CHECK(cudaEventElapsedTime(ms + i, phase_events_[i], phase_events_[i + 1]));
     }
 
     // Kernel launches of this library per transcription: the encoder-row
@@ -1169,6 +1187,7 @@ private:
     int max_shared_ = 232448;
     int fc_ = 0;
     cudaStream_t stream_ = nullptr;
+    cudaEvent_t phase_events_[4] = {nullptr, nullptr, nullptr, nullptr};
     cublasHandle_t cublas_ = nullptr;
 
     DeviceBuffer token_table_, position_table_, final_w_, final_b_, cross_kv_w_;
@@ -1381,6 +1400,14 @@ int wsp_decoder_trace_cycles(const wsp_decoder* decoder, double* cycles, int cou
         WSP_NEED(decoder);
         if (!cycles || count < 0) throw wsp::InvalidArgument("cycles is NULL");
         decoder->impl->trace_cycles(cycles, count);
+    });
+}
+
+int wsp_decoder_phase_ms(wsp_decoder* decoder, float* ms) {
+    return guarded([&] {
+        WSP_NEED(decoder);
+        if (!ms) throw wsp::InvalidArgument("ms is NULL");
+        decoder->impl->phase_ms(ms);
     });
 }
 

@@ -228,6 +228,13 @@ class Decoder:
         check(self._lib.wsp_decoder_step_launches(self._handle, ctypes.byref(value)))
         return value.value
 
+    def phase_ms(self) -> dict:
+        """Milliseconds of the last transcription's phases (CUDA events on the
+        decoder's stream): sequence start, prompt launch, later-steps launch."""
+        ms = (ctypes.c_float * 3)()
+        check(self._lib.wsp_decoder_phase_ms(self._handle, ms))
+        return {"sequence_start": ms[0], "prompt": ms[1], "steps": ms[2]}
+
     def time_barriers(self, count: int = 40) -> float:
         """Mean microseconds of one grid barrier of the decode kernel."""
         value = ctypes.c_float()
