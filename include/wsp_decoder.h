@@ -231,6 +231,38 @@ int wsp_decoder_step_launches(const wsp_decoder* decoder, int* launches);
 int wsp_argmax(const float* logits, const float* mask, uint32_t* indices, int row_count,
                int row_length, void* stream);
 
+/*
+ * wsp_argmax for callers that must not allocate device memory: the same
+ * masked argmax, the same result, but no cudaMalloc, cudaMallocAsync,
+ * cudaFree or allocating library call.  No counterpart in the reference
+ * (Argmax::encode, Argmax.h:207-262, records into buffers KernelNet sized up
+ * front); it is for host code that cannot enter the CUDA allocator -- a
+ * real-time audio thread, where an allocation may block on driver locks or
+ * wait on other work in the stream's pool, or a runtime that has already
+ * reserved every byte of its memory budget.
+ *
+ * Its scratch is a fixed 512 KB array inside this library (static device
+ * memory, loaded with the module), so row_count x ceil(row_length / 2048)
+ * may be at most WSP_ARGMAX_NO_ALLOC_MAX_GROUPS (65536: e.g. 2520 rows of
+ * 51866); more is WSP_INVALID_ARGUMENT before anything is launched.  Nothing
+ * in the scratch has to start at zero.
+ *
+ * The first call on a device looks the scratch's address up
+ * (cudaGetSymbolAddress) with that device current and remembers it: make
+ * that first call during set-up, before any stream capture.  The call works
+ * on the current device; logits, mask and indices are device pointers there.
+ * It queues two kernels on `stream` (NULL: the legacy stream) and returns
+ * without waiting; indices hold the result once the stream has passed them.
+ *
+ * Every call on a device shares the one scratch: two calls whose work
+ * overlaps on the device (different streams, or different host threads,
+ * without ordering between them) race and may return wrong indices.  Calls
+ * queued on one stream are ordered and safe.
+ */
+#define WSP_ARGMAX_NO_ALLOC_MAX_GROUPS 65536
+int wsp_argmax_no_alloc(const float* logits, const float* mask, uint32_t* indices, int row_count,
+                        int row_length, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

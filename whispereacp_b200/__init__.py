@@ -5,7 +5,7 @@ include/wsp_decoder.h; this package is the host-side mirror of the
 reference's Decoder / Argmax / greedy-search interface over that ABI.
 """
 from ._native import CudaError, LogicError, ModelError, library  # noqa: F401
-from .decoder import Decoder, DecoderShape, StepResult, argmax  # noqa: F401
+from .decoder import Decoder, DecoderShape, StepResult, argmax, argmax_no_alloc  # noqa: F401
 
 __all__ = ["Decoder", "DecoderShape", "StepResult", "ModelError", "LogicError", "CudaError",
-           "argmax", "library"]
+           "argmax", "argmax_no_alloc", "library"]

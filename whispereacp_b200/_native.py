@@ -83,6 +83,7 @@ SIGNATURES = {
     "wsp_decoder_step_launches": ([_P, ctypes.POINTER(_I)], _I),
     "wsp_decoder_phase_ms": ([_P, ctypes.POINTER(ctypes.c_float)], _I),
     "wsp_argmax": ([_P, _P, _P, _I, _I, _P], _I),
+    "wsp_argmax_no_alloc": ([_P, _P, _P, _I, _I, _P], _I),
 }
 
 _lib = None

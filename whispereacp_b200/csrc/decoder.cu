@@ -1438,4 +1438,28 @@ int wsp_argmax(const float* logits, const float* mask, uint32_t* indices, int ro
     });
 }
 
+int wsp_argmax_no_alloc(const float* logits, const float* mask, uint32_t* indices, int row_count,
+                        int row_length, void* stream) {
+    return guarded([&] {
+        if (!logits || !indices) throw wsp::InvalidArgument("logits and indices must not be NULL");
+        if (row_count <= 0 || row_length <= 0) throw wsp::InvalidArgument("argmax needs rows of positive length");
+        const int groups = wsp::argmax_groups_per_row(row_length);
+        if ((long long)row_count * groups > wsp::kNoAllocArgmaxCandidates)
+            throw wsp::InvalidArgument("wsp_argmax_no_alloc holds at most " +
+                                       std::to_string(wsp::kNoAllocArgmaxCandidates) +
+                                       " row groups (rows x ceil(length / 2048)); " + std::to_string(row_count) +
+                                       " rows of " + std::to_string(row_length) + " need " +
+                                       std::to_string((long long)row_count * groups));
+        int device = 0;
+        wsp::cuda_check(cudaGetDevice(&device), "cudaGetDevice");
+        void* scratch = nullptr;
+        wsp::cuda_check(wsp::no_alloc_argmax_scratch(device, &scratch), "cudaGetSymbolAddress (argmax scratch)");
+        float* values = static_cast<float*>(scratch);
+        uint32_t* candidates = reinterpret_cast<uint32_t*>(values + wsp::kNoAllocArgmaxCandidates);
+        wsp::launch_argmax_rows(logits, mask, indices, row_count, row_length, values, candidates, groups,
+                                static_cast<cudaStream_t>(stream));
+        wsp::cuda_check(cudaGetLastError(), "argmax launch");
+    });
+}
+
 }  // extern "C"

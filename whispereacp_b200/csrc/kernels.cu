@@ -5,6 +5,7 @@
 #include "kernels.cuh"
 
 #include <algorithm>
+#include <mutex>
 #include <stdexcept>
 
 namespace wsp {
@@ -85,6 +86,28 @@ __global__ void to_storage_kernel(const float* in, WT* out, long long count) {
 }
 
 }  // namespace
+
+// The no-allocation argmax's scratch: 65536 candidate pairs (512 KB), values
+// first.  It is part of the module's static device memory, loaded with the
+// library, so a call that uses it allocates nothing.  Nothing in it has to
+// start at zero: the partial pass writes every slot the final pass reads.
+static __device__ __align__(256) unsigned char no_alloc_scratch[kNoAllocArgmaxCandidates * 8];
+
+cudaError_t no_alloc_argmax_scratch(int device, void** scratch) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex lock;
+    static void* addresses[kMaxDevices] = {};
+    if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> guard(lock);
+    if (addresses[device] == nullptr) {
+        void* address = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&address, no_alloc_scratch);
+        if (e != cudaSuccess) return e;
+        addresses[device] = address;
+    }
+    *scratch = addresses[device];
+    return cudaSuccess;
+}
 
 void launch_argmax_final(const ArgmaxFinalArgs& a, cudaStream_t stream) {
     argmax_final_kernel<<<a.rows, kThreads, 0, stream>>>(a);

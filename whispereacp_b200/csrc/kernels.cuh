@@ -31,6 +31,15 @@ void launch_argmax_rows(const float* logits, const float* mask, uint32_t* out, i
                         int groups_per_row, cudaStream_t stream);
 int argmax_groups_per_row(int length);
 
+// The fixed scratch of wsp_argmax_no_alloc: room for this many per-group
+// (value, index) candidate pairs, rows x argmax_groups_per_row(length).
+constexpr int kNoAllocArgmaxCandidates = 65536;
+
+// This device's address of that scratch (kNoAllocArgmaxCandidates floats,
+// then as many uint32 indices), looked up with cudaGetSymbolAddress the first
+// time a device asks, with that device current, and remembered after.
+cudaError_t no_alloc_argmax_scratch(int device, void** scratch);
+
 // ------------------------------------------------------------- plumbing ---
 void launch_to_storage(Storage s, const float* in, void* out, long long count, cudaStream_t stream);
 

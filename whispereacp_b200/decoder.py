@@ -26,7 +26,7 @@ import numpy as np
 from ._native import (CGeneration, CShape, KERNEL_CLASSES, TRACE_SECTIONS, LogicError, ModelError,
                       WSP_BFLOAT16, WSP_FLOAT16, WSP_FLOAT32, check, library)
 
-__all__ = ["DecoderShape", "Decoder", "StepResult", "ModelError", "LogicError", "argmax",
+__all__ = ["DecoderShape", "Decoder", "StepResult", "ModelError", "LogicError", "argmax", "argmax_no_alloc",
            "STORAGE"]
 
 STORAGE = {"float16": WSP_FLOAT16, "bfloat16": WSP_BFLOAT16}
@@ -280,3 +280,16 @@ def argmax(logits_pointer: int, mask_pointer: int | None, out_pointer: int, row_
                                ctypes.c_void_p(mask_pointer) if mask_pointer else None,
                                ctypes.c_void_p(out_pointer), row_count, row_length,
                                ctypes.c_void_p(stream) if stream else None))
+
+
+def argmax_no_alloc(logits_pointer: int, mask_pointer: int | None, out_pointer: int, row_count: int,
+                    row_length: int, stream: int = 0) -> None:
+    """argmax without allocating device memory (wsp_argmax_no_alloc): scratch
+    is a fixed array inside the library, at most 65536 row groups
+    (rows x ceil(length / 2048)).  Queues the work on `stream` and returns
+    without waiting.  Calls that overlap on one device race on the scratch;
+    calls on one stream are ordered."""
+    check(library().wsp_argmax_no_alloc(ctypes.c_void_p(logits_pointer),
+                                        ctypes.c_void_p(mask_pointer) if mask_pointer else None,
+                                        ctypes.c_void_p(out_pointer), row_count, row_length,
+                                        ctypes.c_void_p(stream) if stream else None))
