@@ -69,11 +69,7 @@ def test_teacher_forced_steps_match_the_oracle(config, storage, steps):
 
 
 @pytest.mark.parametrize("config,storage,steps", [("tiny_en_b1", "float16", 40), ("base_en_b1", "bfloat16", 16)])
-@pytest.mark.parametrize("path", ["general", "fused"])
-def test_greedy_transcript_follows_the_oracle(config, storage, steps, path, monkeypatch):
-    """Both single-token step forms: the general op list (the default) and
-    the fused per-layer blocks (WSP_SINGLE_TOKEN_PATH=fused)."""
-    monkeypatch.setenv("WSP_SINGLE_TOKEN_PATH", path)
+def test_greedy_transcript_follows_the_oracle(config, storage, steps):
     run = S.CONFIGS[config]
     shape = run.shape
     tensors = stored_tensors(S.normal_weights(shape, seed=21), storage)
@@ -139,8 +135,8 @@ def test_batched_windows_follow_the_oracle():
 def test_wide_batched_windows_follow_the_oracle():
     """Forty windows of a 1024-wide decoder with the full vocabulary: 32 KB
     weight-stream stages leave room for fewer stages than warps, the logits
-    run as two row tiles with each warp owning every seventh vocabulary tile,
-    and the general (unfused) single-token step runs.  Each window's
+    run as two row tiles with each warp owning every seventh vocabulary tile.
+    Each window's
     transcript, replayed through the oracle, is its greedy choice wherever
     the margin decides it."""
     from whispereacp_b200.decoder import DecoderShape

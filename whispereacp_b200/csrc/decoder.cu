@@ -139,9 +139,6 @@ struct LayerBuffers {
     DeviceBuffer ln1_w, ln1_b, qkv_w, qkv_b, o_w, o_b;
     DeviceBuffer ln2_w, ln2_b, qc_w, qc_b, vc_b, oc_w, oc_b;
     DeviceBuffer ln3_w, ln3_b, fc1_w, fc1_b, fc2_w, fc2_b;
-    // Per-head slices of the two out_proj weights and per-chunk slices of
-    // fc2, fragment-packed on their own, for the single-token fused blocks.
-    DeviceBuffer wo_heads, woc_heads, w2_chunks;
 };
 
 class Decoder {
@@ -240,7 +237,6 @@ public:
         case 7:
             require_extents(name, extents, rank, {d, d});
             upload_packed(L.o_w, 0, d, d, kpd, dtype, data);
-            patch_head_slices(L.wo_heads, dtype, data);
             break;
         case 8: require_extents(name, extents, rank, {d}); upload_floats(L.o_b, 0, d, dtype, data); break;
         case 9: require_extents(name, extents, rank, {d}); upload_floats(L.ln2_w, 0, d, dtype, data); break;
@@ -265,7 +261,6 @@ public:
         case 16:
             require_extents(name, extents, rank, {d, d});
             upload_packed(L.oc_w, 0, d, d, kpd, dtype, data);
-            patch_head_slices(L.woc_heads, dtype, data);
             break;
         case 17: require_extents(name, extents, rank, {d}); upload_floats(L.oc_b, 0, d, dtype, data); break;
         case 18: require_extents(name, extents, rank, {d}); upload_floats(L.ln3_w, 0, d, dtype, data); break;
@@ -275,7 +270,6 @@ public:
         case 22:
             require_extents(name, extents, rank, {d, f});
             upload_packed(L.fc2_w, 0, d, f, kpf, dtype, data);
-            if (fc_ > 0) patch_chunk_slices(L.w2_chunks, dtype, data);
             break;
         case 23: require_extents(name, extents, rank, {d}); upload_floats(L.fc2_b, 0, d, dtype, data); break;
         }
@@ -556,13 +550,13 @@ public:
         p.n_ops = count;
         p.steps = 1;
         const bool half = storage_ == Storage::f16;
-        configure_stream(half, p, false);
-        const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk, false);
+        configure_stream(half, p);
+        const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk);
         if (blocks <= 0) throw CudaFailure("the decode kernel does not fit on an SM", false);
         upload_schedule(p, ops, sm_count_ * std::min(blocks, kMaxBlocksPerSm));
         CUDA_CHECK(cudaMemsetAsync(state_.get<int>() + kAbort, 0, 2 * sizeof(int), stream_));
         CUDA_CHECK(cudaMemsetAsync(barrier_.get(), 0, barrier_.bytes(), stream_));
-        launch_decode(half, p, kMaxCrossChunk, false, sm_count_ * std::min(blocks, kMaxBlocksPerSm), stream_);
+        launch_decode(half, p, kMaxCrossChunk, sm_count_ * std::min(blocks, kMaxBlocksPerSm), stream_);
         std::vector<unsigned long long> stamps(count + 1);
         CUDA_CHECK(cudaMemcpyAsync(stamps.data(), profile_.get(), stamps.size() * 8, cudaMemcpyDeviceToHost, stream_));
         CUDA_CHECK(cudaStreamSynchronize(stream_));
@@ -609,9 +603,6 @@ private:
 
     static size_t round16(size_t n) { return (n + 15) / 16 * 16; }
 
-    // The single-token blocks take fc1 in chunks of fc_ rows (0: no chunking
-    // fits, and single-token steps use the general ops).
-    static int feed_forward_chunk(int f) { return f % 64 == 0 ? 64 : (f % 32 == 0 ? 32 : (f % 16 == 0 ? 16 : 0)); }
     int head_width() const { return shape_.width / shape_.heads; }
     // Packed row of the q (0), k (1) or v (2) row i of a head-grouped q/k/v
     // matrix: head h owns rows [h*G, h*G + 3D), G = 3D rounded to a tile.
@@ -624,13 +615,10 @@ private:
         const int D = head_width();
         return (i / D) * (int)round16(D) + i % D;
     }
-    size_t head_slice_bytes() const { return round16(shape_.width) * padded(head_width()) * 2; }
-    size_t chunk_slice_bytes() const { return round16(shape_.width) * padded(fc_) * 2; }
 
     void allocate_weights() {
         const size_t d = shape_.width, f = shape_.feed_forward_width, L = shape_.layers;
         const size_t H = shape_.heads, D = d / H;
-        fc_ = feed_forward_chunk((int)f);
         const size_t kpd = padded(d), kpf = padded(f);
         token_table_.allocate(round16(shape_.vocabulary_size) * kpd * 2);
         position_table_.allocate((size_t)shape_.max_positions * d * 4);
@@ -649,9 +637,6 @@ private:
             l.ln3_w.allocate(d * 4); l.ln3_b.allocate(d * 4);
             l.fc1_w.allocate(round16(f) * kpd * 2); l.fc1_b.allocate(f * 4);
             l.fc2_w.allocate(round16(d) * kpf * 2); l.fc2_b.allocate(d * 4);
-            l.wo_heads.allocate(H * head_slice_bytes());
-            l.woc_heads.allocate(H * head_slice_bytes());
-            if (fc_ > 0) l.w2_chunks.allocate((f / fc_) * chunk_slice_bytes());
         }
         present_.assign(4 + 24 * L, false);
     }
@@ -679,7 +664,7 @@ private:
         const int X = shape_.cross_positions;
         int s = (kMaxBlocksPerSm * sm_count_ + shape_.heads - 1) / shape_.heads;
         s = std::min(s, std::max(1, (X + 31) / 32));
-        return std::max({1, s, (X + kWarpKeyLimit - 1) / kWarpKeyLimit});
+        return std::max({1, s, (X + kMaxCrossChunk - 1) / kMaxCrossChunk});
     }
 
     void ensure_row_capacity(int tokens) {
@@ -688,8 +673,6 @@ private:
         const size_t R = (size_t)windows_ * token_capacity_;
         const size_t d = shape_.width, f = shape_.feed_forward_width, H = shape_.heads, D = d / H;
         hidden_.allocate(R * d * 4);
-        x1_.allocate(R * d * 4);
-        x2_.allocate(R * d * 4);
         queries_.allocate(R * d * 4);
         attended_.allocate(R * padded(d) * 2);
         feed_forward_.allocate(R * padded(f) * 2);
@@ -731,19 +714,15 @@ private:
         case kOpSelfAttention: return WSP_KERNEL_SELF_ATTENTION;
         case kOpCrossAttention: return WSP_KERNEL_CROSS_ATTENTION;
         case kOpLogits: return WSP_KERNEL_LOGITS_ARGMAX;
-        case kOpSelfBlock: return WSP_KERNEL_SELF_ATTENTION;
-        case kOpCrossBlock: return WSP_KERNEL_CROSS_ATTENTION;
-        case kOpFeedForwardBlock: return WSP_KERNEL_PROJECTION;
         }
         return WSP_KERNEL_OTHER;
     }
 
     static constexpr int kMaxCrossChunk = 2048;
-    static constexpr int kWarpKeyLimit = 512;  // keys a warp scores at once in the fused cross block
     static constexpr int kMaxBlocksPerSm = 2;
 
     // The step: recordDecoderStep (Decoder.cpp:151-177) with decoderLayer
-    // (Decoder.cpp:73-115), lowered onto the fused ops of step.cuh.
+    // (Decoder.cpp:73-115), lowered onto the ops of step.cuh.
     std::vector<StepOp> build_ops(int R, int grid, int* max_chunk) const {
         const int d = shape_.width, f = shape_.feed_forward_width, H = shape_.heads;
         const int kpd = padded(d), kpf = padded(f);
@@ -842,91 +821,6 @@ private:
         return ops;
     }
 
-    // The single-token step as fused blocks (step.cuh): embed, then per layer
-    // the self, cross and feed-forward blocks, then the logits.
-    std::vector<StepOp> build_fused_ops(int grid, int stage_bytes, int* max_chunk) const {
-        const int d = shape_.width, H = shape_.heads, D = d / H;
-        const size_t elem = 2;
-        const size_t self_layer = (size_t)windows_ * shape_.max_positions * d * elem;
-        const size_t n_cross = (size_t)2 * d * shape_.layers;
-        const int r_tiles = (windows_ + 7) / 8;
-        const int stage_chunks = stage_bytes / 1024;
-        // Enough (head, rows, split) items for the grid; chunks of 32..512 keys.
-        int splits = grid / (H * r_tiles);
-        splits = std::min(splits, std::max(1, (active_cross_ + 31) / 32));
-        splits = std::max({1, splits, (active_cross_ + kWarpKeyLimit - 1) / kWarpKeyLimit});
-        const int chunk = (active_cross_ + splits - 1) / splits;
-        *max_chunk = chunk;
-        std::vector<StepOp> ops;
-        StepOp e{};
-        e.kind = kOpEmbed;
-        ops.push_back(e);
-        for (int l = 0; l < shape_.layers; ++l) {
-            const LayerBuffers& W = layers_[l];
-            StepOp self{};
-            self.kind = kOpSelfBlock;
-            self.gamma = W.ln1_w.get<float>();
-            self.beta = W.ln1_b.get<float>();
-            self.weight = W.qkv_w.get();
-            self.bias = W.qkv_b.get<float>();
-            self.self_keys = self_keys_.get<char>() + l * self_layer;
-            self.self_values = self_values_.get<char>() + l * self_layer;
-            self.weight2 = W.wo_heads.get();
-            self.item_stride2 = (long long)head_slice_bytes();
-            self.kp2 = padded(D);
-            self.group2 = std::max(1, stage_chunks / (self.kp2 / 32));
-            self.bias2 = W.o_b.get<float>();
-            self.slice = D;
-            ops.push_back(self);
-            StepOp cross{};
-            cross.kind = kOpCrossBlock;
-            cross.gamma = W.ln2_w.get<float>();
-            cross.beta = W.ln2_b.get<float>();
-            cross.weight = W.qc_w.get();
-            cross.bias = W.qc_b.get<float>();
-            cross.keys = cross_kv_.get<char>() + (size_t)l * 2 * d * elem;
-            cross.values = cross_kv_.get<char>() + ((size_t)l * 2 * d + d) * elem;
-            cross.key_stride = (long long)n_cross;
-            cross.window_stride = (long long)shape_.cross_positions * n_cross;
-            cross.key_count = active_cross_;
-            cross.splits = splits;
-            cross.chunk = chunk;
-            cross.value_bias = W.vc_b.get<float>();
-            cross.weight2 = W.woc_heads.get();
-            cross.item_stride2 = (long long)head_slice_bytes();
-            cross.kp2 = padded(D);
-            cross.bias2 = W.oc_b.get<float>();
-            cross.slice = D;
-            ops.push_back(cross);
-            StepOp ffn{};
-            ffn.kind = kOpFeedForwardBlock;
-            ffn.gamma = W.ln3_w.get<float>();
-            ffn.beta = W.ln3_b.get<float>();
-            ffn.weight = W.fc1_w.get();
-            ffn.bias = W.fc1_b.get<float>();
-            ffn.weight2 = W.w2_chunks.get();
-            ffn.item_stride2 = (long long)chunk_slice_bytes();
-            ffn.kp2 = padded(fc_);
-            ffn.group2 = std::max(1, stage_chunks / (ffn.kp2 / 32));
-            ffn.bias2 = W.fc2_b.get<float>();
-            ffn.slice = fc_;
-            ops.push_back(ffn);
-        }
-        StepOp logits{};
-        logits.kind = kOpLogits;
-        ops.push_back(logits);
-        return ops;
-    }
-
-    // The general op list is the default single-token step: measured on
-    // B200 it beats the fused blocks at every configuration from tiny.en B1
-    // to large-v3 B128.  WSP_SINGLE_TOKEN_PATH=fused selects the blocks
-    // (both compute the same step; kept for measurement).
-    bool use_fused_blocks() const {
-        const char* forced = std::getenv("WSP_SINGLE_TOKEN_PATH");
-        return forced && std::string(forced) == "fused";
-    }
-
     // The weight-stream schedule of every CTA (schedule.h), into device memory.
     void upload_schedule(StepParams& p, const std::vector<StepOp>& ops, int grid) {
         build_schedule(p, ops, grid, decode_tile_rows(p), schedule_host_, offsets_host_);
@@ -956,7 +850,6 @@ private:
         for (int l = 0; l < shape_.layers; ++l) {
             const LayerBuffers& W = layers_[l];
             add(W.qkv_w); add(W.o_w); add(W.qc_w); add(W.oc_w); add(W.fc1_w); add(W.fc2_w);
-            add(W.wo_heads); add(W.woc_heads); add(W.w2_chunks);
         }
         std::sort(ranges.begin(), ranges.end());
         for (size_t i = 0; i < schedule_host_.size(); ++i) {
@@ -972,10 +865,10 @@ private:
 
     // Stage size: one 16-row tile over kpd (at least 16 KB); as many stages
     // (2..8) as the shared memory left by the work area holds.
-    void configure_stream(bool half, StepParams& p, bool fused) const {
+    void configure_stream(bool half, StepParams& p) const {
         const int tile = 16 * padded(shape_.width) * 2;
         p.stage_bytes = std::max(16384, (tile + 1023) / 1024 * 1024);
-        const size_t work = decode_work_bytes(half, p, kMaxCrossChunk, fused);
+        const size_t work = decode_work_bytes(half, p, kMaxCrossChunk);
         const long long room = (long long)max_shared_ - (long long)work;
         p.stages = (int)std::min<long long>(8, room / p.stage_bytes);
         if (p.stages < 2) throw CudaFailure("the decode kernel's shared memory does not fit", false);
@@ -1007,8 +900,6 @@ private:
         p.final_gamma = final_w_.get<float>();
         p.final_beta = final_b_.get<float>();
         p.h = hidden_.get<float>();
-        p.x1 = x1_.get<float>();
-        p.x2 = x2_.get<float>();
         p.q = queries_.get<float>();
         p.attn16 = attended_.get();
         p.ffn16 = feed_forward_.get();
@@ -1041,15 +932,14 @@ private:
         StepParams p = base_params(T, sample, mask, logits, hidden, row_tokens, steps, stop);
         p.profile = profile;
         const bool half = storage_ == Storage::f16;
-        const bool fused = sample && T == 1 && fc_ > 0 && use_fused_blocks();
-        configure_stream(half, p, fused);
-        const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk, fused);
+        configure_stream(half, p);
+        const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk);
         if (blocks <= 0) throw CudaFailure("the decode kernel does not fit on an SM", false);
         const int grid = sm_count_ * std::min(blocks, kMaxBlocksPerSm);
         int max_chunk = 0;
         std::vector<StepOp>& ops = sample ? (T == 1 ? ops_step_ : ops_prompt_) : ops_teacher_;
         DeviceBuffer& ops_dev = sample ? (T == 1 ? ops_step_dev_ : ops_prompt_dev_) : ops_teacher_dev_;
-        ops = fused ? build_fused_ops(grid, p.stage_bytes, &max_chunk) : build_ops(R, grid, &max_chunk);
+        ops = build_ops(R, grid, &max_chunk);
         if (ops_dev.bytes() < ops.size() * sizeof(StepOp)) ops_dev.allocate(ops.size() * sizeof(StepOp));
         CUDA_CHECK(cudaMemcpyAsync(ops_dev.get(), ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice,
                                    stream_));
@@ -1060,10 +950,8 @@ private:
         // the prompt step to the steps after it.
         CUDA_CHECK(cudaMemsetAsync(state_.get<int>() + kAbort, 0, 2 * sizeof(int), stream_));
         CUDA_CHECK(cudaMemsetAsync(barrier_.get(), 0, barrier_.bytes(), stream_));
-        // The fused blocks accumulate into X1 first; it starts at zero.
-        if (fused) CUDA_CHECK(cudaMemsetAsync(x1_.get(), 0, (size_t)R * shape_.width * 4, stream_));
         try {
-            launch_decode(half, p, kMaxCrossChunk, fused, grid, stream_);
+            launch_decode(half, p, kMaxCrossChunk, grid, stream_);
         } catch (const std::runtime_error& e) {
             throw CudaFailure(e.what(), false);
         }
@@ -1121,23 +1009,6 @@ private:
         patch16(dst, d, d, dtype, data, [&](int r, int c) { return packed_offset(qkv_row(which, r), c, chunks); });
     }
 
-    // out_proj [d, d] as H packed [d, D] slices: column h*D + c of row n is
-    // element (n, c) of slice h.
-    void patch_head_slices(DeviceBuffer& dst, wsp_dtype dtype, const void* data) {
-        const int d = shape_.width, D = head_width(), chunks = padded(D) / 32;
-        const size_t slice = head_slice_bytes() / 2;
-        patch16(dst, d, d, dtype, data,
-                [&](int n, int col) { return (col / D) * slice + packed_offset(n, col % D, chunks); });
-    }
-
-    // fc2 [d, F] as F/fc_ packed [d, fc_] slices.
-    void patch_chunk_slices(DeviceBuffer& dst, wsp_dtype dtype, const void* data) {
-        const int d = shape_.width, f = shape_.feed_forward_width, chunks = padded(fc_) / 32;
-        const size_t slice = chunk_slice_bytes() / 2;
-        patch16(dst, d, f, dtype, data,
-                [&](int n, int col) { return (col / fc_) * slice + packed_offset(n, col % fc_, chunks); });
-    }
-
     void upload_floats(DeviceBuffer& dst, size_t offset, size_t count, wsp_dtype dtype, const void* data) {
         std::vector<float> v(count);
         for (size_t i = 0; i < count; ++i) v[i] = widen(data, dtype, i);
@@ -1185,7 +1056,6 @@ private:
     Storage storage_;
     int sm_count_ = 148;
     int max_shared_ = 232448;
-    int fc_ = 0;
     cudaStream_t stream_ = nullptr;
     cudaEvent_t phase_events_[4] = {nullptr, nullptr, nullptr, nullptr};
     cublasHandle_t cublas_ = nullptr;
@@ -1196,7 +1066,7 @@ private:
 
     DeviceBuffer self_keys_, self_values_, cross_kv_, encoder_staging_, encoder16_;
     DeviceBuffer ring_, ring_prompt_, state_, masks_;
-    DeviceBuffer hidden_, x1_, x2_, queries_, attended_, feed_forward_, partial_;
+    DeviceBuffer hidden_, queries_, attended_, feed_forward_, partial_;
     DeviceBuffer candidate_values_, candidate_indices_, row_tokens_, counters_;
     DeviceBuffer barrier_, ended_, profile_;
     DeviceBuffer logits_staging_, hidden_staging_;

@@ -23,21 +23,17 @@ inline int schedule_row_tiles(int rows, int rt) { return (rows + rt - 1) / rt; }
 inline int schedule_round16(int n) { return (n + 15) / 16 * 16; }
 
 // Items of an op; CTA c takes items c, c + grid, ...  rt: input rows of a
-// general product's tile (8 * NT of the launch); fused blocks take 8.
+// product's tile (8 * NT of the launch).
 inline int op_items(const StepParams& p, const StepOp& op, int rt) {
     switch (op.kind) {
     case kOpProduct: return ((op.n + 15) / 16) * schedule_row_tiles(p.rows, rt);
     case kOpLogits: return ((p.vocabulary + 15) / 16) * schedule_row_tiles(p.out_rows, rt);
-    case kOpSelfBlock: return p.heads * schedule_row_tiles(p.rows, 8);
-    case kOpCrossBlock: return p.heads * schedule_row_tiles(p.rows, 8) * op.splits;
-    case kOpFeedForwardBlock: return (p.ffn / op.slice) * schedule_row_tiles(p.rows, 8);
     }
     return 0;
 }
 
 // Weight region `region` of item `item` of an op; false when there is none.
 inline bool item_region(const StepParams& p, const StepOp& op, int item, int region, Region& out) {
-    const int chunks_d = p.kpd / 32;
     switch (op.kind) {
     case kOpProduct:
     case kOpLogits: {
@@ -48,44 +44,6 @@ inline bool item_region(const StepParams& p, const StepOp& op, int item, int reg
         const int tile = item % ((n + 15) / 16);
         out = Region{static_cast<const unsigned char*>(w) + (size_t)tile * (kp / 32) * 1024, 1, kp / 32, 1};
         return true;
-    }
-    case kOpSelfBlock: {
-        const int head = item % p.heads;
-        if (region == 0) {
-            const int tiles = schedule_round16(3 * p.head_width) / 16;
-            out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)head * tiles * chunks_d * 1024, tiles,
-                         chunks_d, 1};
-            return true;
-        }
-        if (region == 1) {
-            out = Region{static_cast<const unsigned char*>(op.weight2) + (size_t)head * op.item_stride2,
-                         schedule_round16(p.width) / 16, op.kp2 / 32, op.group2};
-            return true;
-        }
-        return false;
-    }
-    case kOpCrossBlock: {
-        if (region != 0) return false;
-        const int head = (item / op.splits) % p.heads;
-        const int tiles = schedule_round16(p.head_width) / 16;
-        out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)head * tiles * chunks_d * 1024, tiles,
-                     chunks_d, 1};
-        return true;
-    }
-    case kOpFeedForwardBlock: {
-        const int chunk = item % (p.ffn / op.slice);
-        if (region == 0) {
-            const int tiles = op.slice / 16;
-            out = Region{static_cast<const unsigned char*>(op.weight) + (size_t)chunk * tiles * chunks_d * 1024, tiles,
-                         chunks_d, 1};
-            return true;
-        }
-        if (region == 1) {
-            out = Region{static_cast<const unsigned char*>(op.weight2) + (size_t)chunk * op.item_stride2,
-                         schedule_round16(p.width) / 16, op.kp2 / 32, op.group2};
-            return true;
-        }
-        return false;
     }
     }
     return false;

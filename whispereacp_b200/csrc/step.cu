@@ -331,13 +331,10 @@ constexpr int kNormMaxPerLane = 48;  // widths up to 1536
 // output row rl reads h row (r0 + rl)*row_step + row_offset.  One warp a row,
 // the row in registers: the mean, then the centred variance, as
 // LayerNorm.h:19-98 does.  hidden_out, when given, receives the fp32 rows.
-// forward_to, when given, also receives input + forward_bias for every
-// element read, by fp32 reduction: the residual and the bias a fused block
-// adds into the next residual buffer once per row.
 template <typename WT>
 __device__ void layer_norm_tile(const StepParams& p, const float* input, const float* gamma, const float* beta,
                                 int r0, int rows_in_tile, int row_step, int row_offset, WT* xs, int ldx,
-                                float* hidden_out, float* forward_to = nullptr, const float* forward_bias = nullptr) {
+                                float* hidden_out) {
     const int d = p.width;
     if (rows_in_tile <= 2) {
         // A row or two: the whole CTA on each row, every load of the row,
@@ -353,13 +350,6 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
                 v[i] = c < d ? ld_cg(x + c) : 0.f;
                 g[i] = c < d ? __ldg(gamma + c) : 0.f;
                 b[i] = c < d ? __ldg(beta + c) : 0.f;
-            }
-            if (forward_to) {
-#pragma unroll
-                for (int i = 0; i < kPer; ++i) {
-                    const int c = threadIdx.x + i * kThreads;
-                    if (c < d) atomicAdd(forward_to + (size_t)(r0 + rl) * d + c, v[i] + __ldg(forward_bias + c));
-                }
             }
             float total = 0.f;
 #pragma unroll
@@ -397,13 +387,6 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
             const int c = lane + 32 * i;
             v[i] = c < d ? ld_cg(x + c) : 0.f;
         }
-        if (forward_to) {
-#pragma unroll
-            for (int i = 0; i < kNormMaxPerLane; ++i) {
-                const int c = lane + 32 * i;
-                if (c < d) atomicAdd(forward_to + (size_t)(r0 + rl) * d + c, v[i] + __ldg(forward_bias + c));
-            }
-        }
         float total = 0.f;
 #pragma unroll
         for (int i = 0; i < kNormMaxPerLane; ++i) total += v[i];
@@ -437,7 +420,6 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
     }
 }
 
-__device__ __forceinline__ int row_tiles(int rows, int rt) { return (rows + rt - 1) / rt; }
 __device__ __forceinline__ int round16(int n) { return (n + 15) / 16 * 16; }
 
 // ------------------------------------------------------------------ products
@@ -546,7 +528,6 @@ __device__ __forceinline__ void chunks_product(const unsigned char* unit, int c_
 template <typename WT, int NT, bool X_SHARED>
 __device__ bool product_tile(const StepParams& p, Stream& s, int kp, const WT* X, int ldx, int rows_valid,
                              float (&acc)[NT][4]) {
-    constexpr int RT = 8 * NT;
     const int warp = threadIdx.x >> 5, gq = (threadIdx.x & 31) >> 2;
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -977,58 +958,6 @@ __device__ __forceinline__ void attention_values(const float* scores, const WT* 
     consumer_sync();
 }
 
-// One warp's attention of one query over keys [k0, k0+n), n <= kWarpKeys:
-// lanes score keys, the warp folds the maximum and the sum, then lane c and
-// c+32 accumulate channels c and c+32 over the keys, eight loads in flight.
-// Leaves the unnormalised row in out[0..D) and returns (max, sum).
-constexpr int kWarpKeys = 512;
-
-template <typename WT, bool READ_ONLY>
-__device__ float2 warp_attention(const float* q, const WT* K, const WT* V, long long key_stride, int D, int k0,
-                                 int n, float* scores, float* out) {
-    const int lane = threadIdx.x & 31;
-    float mx = -INFINITY;
-    for (int j = lane; j < n; j += 32) {
-        const float sc = score_any<WT, READ_ONLY>(q, K + (size_t)(k0 + j) * key_stride, D);
-        scores[j] = sc;
-        mx = fmaxf(mx, sc);
-    }
-    mx = warp_max(mx);
-    float sum = 0.f;
-    for (int j = lane; j < n; j += 32) {
-        const float e = __expf(scores[j] - mx);
-        scores[j] = e;
-        sum += e;
-    }
-    sum = warp_sum(sum);
-    __syncwarp();
-    float a0 = 0.f, a1 = 0.f;
-    const bool c0 = lane < D, c1 = lane + 32 < D;
-    const WT* v = V + (size_t)k0 * key_stride;
-    int j = 0;
-    for (; j + 8 <= n; j += 8) {
-        float x0[8], x1[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            x0[u] = c0 ? load_kv1<WT, READ_ONLY>(v + (size_t)(j + u) * key_stride + lane) : 0.f;
-            x1[u] = c1 ? load_kv1<WT, READ_ONLY>(v + (size_t)(j + u) * key_stride + lane + 32) : 0.f;
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            a0 += scores[j + u] * x0[u];
-            a1 += scores[j + u] * x1[u];
-        }
-    }
-    for (; j < n; ++j) {
-        if (c0) a0 += scores[j] * load_kv1<WT, READ_ONLY>(v + (size_t)j * key_stride + lane);
-        if (c1) a1 += scores[j] * load_kv1<WT, READ_ONLY>(v + (size_t)j * key_stride + lane + 32);
-    }
-    if (c0) out[lane] = a0;
-    if (c1) out[lane + 32] = a1;
-    __syncwarp();
-    return make_float2(mx, sum);
-}
-
 // Shared memory of attention: [q: 64][scratch: 8][fold: 2048][result: 64][scores: ...]
 constexpr int kFold = 2048;
 constexpr int kAttentionFixed = 64 + 8 + kFold + 64;
@@ -1062,6 +991,48 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
         attention_values<WT, false>(scores, V, op.key_stride, D, 0, keys, fold, result);
         WT* out = static_cast<WT*>(p.attn16) + (size_t)r * p.kpd + head * D;
         for (int c = threadIdx.x; c < D; c += kThreads) out[c] = Half16<WT>::from_float(result[c] / l);
+    }
+}
+
+// The last split of a cross-attention (row, head) joins the splits' partials
+// the way a split softmax joins (SingleQueryAttention.h:11-37): every load is
+// issued before its value is needed -- the splits' (max, sum) one thread
+// each, then each channel by kThreads / D thread groups, several splits'
+// loads in flight per thread -- so the join costs a few L2 round trips, not
+// one per split.  `fold` holds at least 3 S + kThreads floats.
+template <typename WT>
+__device__ void combine_splits(const StepParams& p, const StepOp& op, int r, int head, float* fold) {
+    const int D = p.head_width, S = op.splits;
+    const float* part = p.partial + ((size_t)r * p.heads + head) * S * (D + 2);
+    float* m_s = fold;           // [S] split maxima
+    float* l_s = fold + S;       // [S] split sums
+    float* f_s = fold + 2 * S;   // [S] exp(max_s - max)
+    float* acc = fold + 3 * S;   // [groups][D]
+    for (int sp = threadIdx.x; sp < S; sp += kThreads) {
+        m_s[sp] = ld_cg(part + (size_t)sp * (D + 2));
+        l_s[sp] = ld_cg(part + (size_t)sp * (D + 2) + 1);
+    }
+    consumer_sync();
+    float mx = -INFINITY;
+    for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, m_s[sp]);
+    for (int sp = threadIdx.x; sp < S; sp += kThreads) f_s[sp] = m_s[sp] == -INFINITY ? 0.f : __expf(m_s[sp] - mx);
+    consumer_sync();
+    const int groups = kThreads / D;
+    const int c = threadIdx.x % D, g = threadIdx.x / D;
+    if (g < groups) {
+        float o = 0.f;
+#pragma unroll 8
+        for (int sp = g; sp < S; sp += groups) o += ld_cg(part + (size_t)sp * (D + 2) + 2 + c) * f_s[sp];
+        acc[g * D + c] = o;
+    }
+    consumer_sync();
+    if (threadIdx.x < D) {
+        float l = 0.f, o = 0.f;
+        for (int sp = 0; sp < S; ++sp) l += l_s[sp] * f_s[sp];
+        for (int gg = 0; gg < groups; ++gg) o += acc[gg * D + threadIdx.x];
+        float y = o / l;
+        if (op.value_bias) y += op.value_bias[head * D + threadIdx.x];
+        static_cast<WT*>(p.attn16)[(size_t)r * p.kpd + head * D + threadIdx.x] = Half16<WT>::from_float(y);
     }
 }
 
@@ -1121,465 +1092,7 @@ __device__ void op_cross_attention(const StepParams& p, const StepOp& op, unsign
         consumer_sync();
         if (!is_last) continue;
         __threadfence();
-        const float* part = p.partial + ((size_t)r * p.heads + head) * S * (D + 2);
-        // Every thread reads the splits' maxima; threads < D then fold a channel.
-        float mx = -INFINITY;
-        for (int s = 0; s < S; ++s) mx = fmaxf(mx, ld_cg(part + (size_t)s * (D + 2)));
-        if (threadIdx.x < D) {
-            float l = 0.f, o = 0.f;
-            for (int s = 0; s < S; ++s) {
-                const float ms = ld_cg(part + (size_t)s * (D + 2));
-                if (ms == -INFINITY) continue;
-                const float f = __expf(ms - mx);
-                l += ld_cg(part + (size_t)s * (D + 2) + 1) * f;
-                o += ld_cg(part + (size_t)s * (D + 2) + 2 + threadIdx.x) * f;
-            }
-            float y = o / l;
-            if (op.value_bias) y += op.value_bias[head * D + threadIdx.x];
-            static_cast<WT*>(p.attn16)[(size_t)r * p.kpd + head * D + threadIdx.x] = Half16<WT>::from_float(y);
-        }
-    }
-}
-
-// ---------------------------------------------------- fused blocks (T = 1)
-
-constexpr int kBlockRows = 8;        // rows of a fused-block item
-constexpr int kMaxSplitTiles = 12;   // 16-row tiles of a K-split product: 3 x 64 q/k/v rows
-constexpr int kSmallPitch = 96;      // shared pitch of a <= 64-wide product input
-
-__host__ __device__ __forceinline__ size_t align128(size_t n) { return (n + 127) / 128 * 128; }
-
-template <typename WT>
-struct BlockArea {
-    WT* xs;       // [8][pitch]       normalised rows
-    float* red;   // [8 warps][12 tiles][16][8]
-    float* res;   // [12*16][8]       reduced K-split products, [n][row]
-    float* q;     // [8][64]          scaled queries
-    WT* o16;      // [8][96]          attention or GELU rows, a product input
-    float* att;   // attention scratch
-    int pitch;
-};
-
-__host__ __device__ inline size_t block_area_bytes(int kpd, int wt_bytes, int max_positions) {
-    const size_t att = sizeof(float) * (size_t)max(8 + 2048 + 64 + max(max_positions, 512), kWarps * kWarpKeys);
-    return align128((size_t)kBlockRows * tile_pitch(kpd) * wt_bytes) + sizeof(float) * kWarps * kMaxSplitTiles * 16 * 8 +
-           sizeof(float) * kMaxSplitTiles * 16 * 8 + sizeof(float) * 8 * 64 +
-           align128((size_t)kBlockRows * kSmallPitch * wt_bytes) + att;
-}
-
-template <typename WT>
-__device__ BlockArea<WT> block_area(const StepParams& p, unsigned char* work) {
-    BlockArea<WT> a;
-    a.pitch = tile_pitch(p.kpd);
-    unsigned char* at = work;
-    a.xs = reinterpret_cast<WT*>(at);
-    at += align128((size_t)kBlockRows * a.pitch * sizeof(WT));
-    a.red = reinterpret_cast<float*>(at);
-    at += sizeof(float) * kWarps * kMaxSplitTiles * 16 * 8;
-    a.res = reinterpret_cast<float*>(at);
-    at += sizeof(float) * kMaxSplitTiles * 16 * 8;
-    a.q = reinterpret_cast<float*>(at);
-    at += sizeof(float) * 8 * 64;
-    a.o16 = reinterpret_cast<WT*>(at);
-    at += align128((size_t)kBlockRows * kSmallPitch * sizeof(WT));
-    a.att = reinterpret_cast<float*>(at);
-    return a;
-}
-
-// `tiles` units off the stream, each one 16-row tile over all of kpd; the 8
-// warps take alternate chunks of every tile into per-tile accumulators, and
-// one fold at the end leaves res[(t*16 + row)*8 + input row].
-template <typename WT, int NT>
-__device__ bool split_product(const StepParams& p, Stream& s, int tiles, const BlockArea<WT>& A, int rows_valid) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gq = lane >> 2, tq = lane & 3;
-    const bool x_ok[1] = {gq < rows_valid};
-    const int chunks = p.kpd / 32;
-    float acc[kMaxSplitTiles][1][4];
-#pragma unroll
-    for (int t = 0; t < kMaxSplitTiles; ++t) acc[t][0][0] = acc[t][0][1] = acc[t][0][2] = acc[t][0][3] = 0.f;
-#pragma unroll
-    for (int t = 0; t < kMaxSplitTiles; ++t) {
-        if (t < tiles) {
-            const unsigned char* unit = acquire_unit(p, s);
-            if (!unit) return false;
-            Trace tr = trace_of(p.profile);
-            tr.begin();
-            chunks_product<WT, 1, true>(unit, warp, kWarps, chunks, A.xs, A.pitch, 0, x_ok, acc[t]);
-            tr.end(kTrCompute);
-            release_unit(s);
-        }
-    }
-    Trace tr = trace_of(p.profile);
-    tr.begin();
-#pragma unroll
-    for (int t = 0; t < kMaxSplitTiles; ++t) {
-        if (t < tiles) {
-            float* r = A.red + (size_t)(warp * kMaxSplitTiles + t) * 128;
-            r[gq * 8 + 2 * tq] = acc[t][0][0];
-            r[gq * 8 + 2 * tq + 1] = acc[t][0][1];
-            r[(gq + 8) * 8 + 2 * tq] = acc[t][0][2];
-            r[(gq + 8) * 8 + 2 * tq + 1] = acc[t][0][3];
-        }
-    }
-    consumer_sync();
-    for (int o = threadIdx.x; o < tiles * 128; o += kThreads) {
-        const int t = o / 128, within = o % 128;
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) v += A.red[(size_t)(w * kMaxSplitTiles + t) * 128 + within];
-        A.res[o] = v;
-    }
-    consumer_sync();
-    tr.end(kTrEpilogue);
-    return true;
-}
-
-// A product whose tiles each fit a warp whole (K <= 64): warp w takes tiles
-// w, w+8, ... over all K and hands every output to emit(n, row, value).
-// Streamed: `group` tiles to a unit.
-template <typename WT, int NT, typename Emit>
-__device__ bool tiled_product(const StepParams& p, Stream& s, int tiles, int chunks, int group, const WT* X,
-                              int ldx, int rows_valid, Emit&& emit) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gq = lane >> 2, tq = lane & 3;
-    const bool x_ok[1] = {gq < rows_valid};
-    for (int t0 = 0; t0 < tiles; t0 += group) {
-        const int nt = min(group, tiles - t0);
-        const unsigned char* unit = acquire_unit(p, s);
-        if (!unit) return false;
-        Trace tr = trace_of(p.profile);
-        tr.begin();
-        for (int tl = warp; tl < nt; tl += kWarps) {
-            float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-            const unsigned char* tile = unit + (size_t)tl * chunks * 1024;
-            chunks_product<WT, 1, true>(tile, 0, 1, chunks, X, ldx, 0, x_ok, acc);
-            const int n = (t0 + tl) * 16 + gq, rl = 2 * tq;
-            emit(n, rl, acc[0][0]);
-            emit(n, rl + 1, acc[0][1]);
-            emit(n + 8, rl, acc[0][2]);
-            emit(n + 8, rl + 1, acc[0][3]);
-        }
-        tr.end(kTrCompute);
-        release_unit(s);
-    }
-    return true;
-}
-
-// The same over weights read straight from global memory (not streamed):
-// warp w takes tiles w and w+8 together, both tiles' chunks loaded before
-// any MMA, so a pair costs one memory latency.
-template <typename WT, typename Emit>
-__device__ void direct_tiled_product(const unsigned char* weights, int tiles, int chunks, const WT* X, int ldx,
-                                     int rows_valid, Emit&& emit) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gq = lane >> 2, tq = lane & 3;
-    const bool x_ok[1] = {gq < rows_valid};
-    for (int t = warp; t < tiles; t += 2 * kWarps) {
-        const int t2 = t + kWarps;
-        const bool second = t2 < tiles;
-        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}}, acc2[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-        const unsigned char* a = weights + (size_t)t * chunks * 1024;
-        const unsigned char* b = weights + (size_t)(second ? t2 : t) * chunks * 1024;
-        int c = 0;
-        for (; c + 1 < chunks; c += 2) {
-            // chunk c and c+1 of both tiles
-            float s1[1][4] = {{0.f, 0.f, 0.f, 0.f}}, s2[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-            product_chunk_pair<WT, 1, true>(a, c, c + 1, X, ldx, c * 32, (c + 1) * 32, x_ok, acc, s1);
-            product_chunk_pair<WT, 1, true>(b, c, c + 1, X, ldx, c * 32, (c + 1) * 32, x_ok, acc2, s2);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                acc[0][e] += s1[0][e];
-                acc2[0][e] += s2[0][e];
-            }
-        }
-        if (c < chunks) {
-            product_chunk<WT, 1, true>(a, c, X, ldx, c * 32, x_ok, acc);
-            product_chunk<WT, 1, true>(b, c, X, ldx, c * 32, x_ok, acc2);
-        }
-        const int rl = 2 * tq;
-        int n = t * 16 + gq;
-        emit(n, rl, acc[0][0]);
-        emit(n, rl + 1, acc[0][1]);
-        emit(n + 8, rl, acc[0][2]);
-        emit(n + 8, rl + 1, acc[0][3]);
-        if (second) {
-            n = t2 * 16 + gq;
-            emit(n, rl, acc2[0][0]);
-            emit(n, rl + 1, acc2[0][1]);
-            emit(n + 8, rl, acc2[0][2]);
-            emit(n + 8, rl + 1, acc2[0][3]);
-        }
-    }
-}
-
-// One query of one row over keys [k0, k0+n) by the whole CTA: the
-// unnormalised row lands in att[8 + 2048 .. + D); returns (max, sum).
-template <typename WT, bool READ_ONLY>
-__device__ float2 cta_attention(const float* q, const WT* K, const WT* V, long long key_stride, int D, int k0, int n,
-                                float* att) {
-    float* scratch = att;
-    float* fold = att + 8;
-    float* result = fold + kFold;
-    float* scores = result + 64;
-    if (n <= 0) return make_float2(-INFINITY, 0.f);
-    const float m = consumer_max(attention_scores<WT, READ_ONLY>(q, K, key_stride, D, k0, n, scores), scratch);
-    float local = 0.f;
-    for (int j = threadIdx.x; j < n; j += kThreads) {
-        const float e = __expf(scores[j] - m);
-        scores[j] = e;
-        local += e;
-    }
-    const float l = consumer_sum(local, scratch);
-    attention_values<WT, READ_ONLY>(scores, V, key_stride, D, k0, n, fold, result);
-    return make_float2(m, l);
-}
-
-__device__ __forceinline__ void zero_rows(float* x, int r0, int rows, int width) {
-    for (int o = threadIdx.x; o < rows * width; o += kThreads) x[(size_t)r0 * width + o] = 0.f;
-}
-
-// Self block: item (head, 8 rows).  Reads X0, adds into X1, zeroes X2.
-template <typename WT, int NT>
-__device__ void op_self_block(const StepParams& p, const StepOp& op, int position, Stream& s, unsigned char* work) {
-    const BlockArea<WT> A = block_area<WT>(p, work);
-    const int D = p.head_width, H = p.heads, d = p.width;
-    const int r_tiles = row_tiles(p.rows, kBlockRows);
-    const int group = round16(3 * D);
-    const int ps = tile_pitch(op.kp2);
-    int cached = -1;
-    for (int item = blockIdx.x; item < H * r_tiles; item += gridDim.x) {
-        const int head = item % H, r_tile = item / H;
-        const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
-        // Head 0's item also forwards X0 + the out_proj bias into X1.
-        if (cached != r_tile || head == 0) {
-            consumer_sync();
-            Trace trn = trace_of(p.profile);
-            trn.begin();
-            layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr,
-                                head == 0 ? p.x1 : nullptr, op.bias2);
-            consumer_sync();
-            trn.end(kTrNorm);
-            cached = r_tile;
-        }
-        if (!split_product<WT, NT>(p, s, group / 16, A, rows_valid)) return;
-        // The head's query (scaled) to shared; its key and value rows of this
-        // position into the cache (Decoder.cpp:29-48; row r is window r).
-        const float* bias = op.bias + (size_t)head * group;
-        for (int o = threadIdx.x; o < 3 * D * rows_valid; o += kThreads) {
-            const int n = o / rows_valid, rl = o % rows_valid;
-            const float v = A.res[n * 8 + rl] + __ldg(bias + n);
-            const int which = n / D, c = n % D;
-            if (which == 0) {
-                A.q[rl * 64 + c] = v * p.scale;
-            } else {
-                WT* cache = static_cast<WT*>(which == 1 ? op.self_keys : op.self_values);
-                cache[((size_t)(r0 + rl) * p.max_positions + position) * d + head * D + c] = Half16<WT>::from_float(v);
-            }
-        }
-        consumer_sync();
-        const int keys = position + 1;
-        Trace tra = trace_of(p.profile);
-        tra.begin();
-        if (rows_valid <= 2) {
-            for (int rl = 0; rl < rows_valid; ++rl) {
-                const size_t base = (size_t)(r0 + rl) * p.max_positions * d + (size_t)head * D;
-                const float2 ml = cta_attention<WT, false>(A.q + rl * 64, static_cast<const WT*>(op.self_keys) + base,
-                                                           static_cast<const WT*>(op.self_values) + base, d, D, 0,
-                                                           keys, A.att);
-                const float* row = A.att + 8 + kFold;
-                for (int c = threadIdx.x; c < op.kp2; c += kThreads)
-                    A.o16[rl * ps + c] = Half16<WT>::from_float(c < D ? row[c] / ml.y : 0.f);
-                consumer_sync();
-            }
-        } else {
-            const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-            for (int rl = warp; rl < rows_valid; rl += kWarps) {
-                const size_t base = (size_t)(r0 + rl) * p.max_positions * d + (size_t)head * D;
-                float* row = A.res + warp * 64;
-                const float2 ml = warp_attention<WT, false>(A.q + rl * 64, static_cast<const WT*>(op.self_keys) + base,
-                                                            static_cast<const WT*>(op.self_values) + base, d, D, 0,
-                                                            keys, A.att + warp * kWarpKeys, row);
-                for (int c = lane; c < op.kp2; c += 32)
-                    A.o16[rl * ps + c] = Half16<WT>::from_float(c < D ? row[c] / ml.y : 0.f);
-            }
-            consumer_sync();
-        }
-        tra.end(kTrAttention);
-        // X1 += the head's slice of out_proj.
-        if (!tiled_product<WT, NT>(p, s, round16(d) / 16, op.kp2 / 32, op.group2, A.o16, ps, rows_valid,
-                                   [&](int n, int rl, float v) {
-                                       if (n >= d || rl >= rows_valid) return;
-                                       atomicAdd(p.x1 + (size_t)(r0 + rl) * d + n, v);
-                                   }))
-            return;
-        if (head == 0) zero_rows(p.x2, r0, rows_valid, d);
-        consumer_sync();
-    }
-}
-
-// Cross block: item (head, 8 rows, key split).  Reads X1, adds into X2,
-// zeroes X0.
-template <typename WT, int NT>
-__device__ void op_cross_block(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
-    const BlockArea<WT> A = block_area<WT>(p, work);
-    const int D = p.head_width, H = p.heads, d = p.width, S = op.splits;
-    const int r_tiles = row_tiles(p.rows, kBlockRows);
-    const int group = round16(D);
-    const int ps = tile_pitch(op.kp2);
-    __shared__ int is_last;
-    int cached = -1;
-    for (int item = blockIdx.x; item < H * r_tiles * S; item += gridDim.x) {
-        const int split = item % S, head = (item / S) % H, r_tile = item / (S * H);
-        const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
-        // Item (head 0, split 0) also forwards X1 + the out_proj bias into X2.
-        const bool forward = head == 0 && split == 0;
-        if (cached != r_tile || forward) {
-            consumer_sync();
-            Trace trn = trace_of(p.profile);
-            trn.begin();
-            layer_norm_tile<WT>(p, p.x1, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr,
-                                forward ? p.x2 : nullptr, op.bias2);
-            consumer_sync();
-            trn.end(kTrNorm);
-            cached = r_tile;
-        }
-        if (!split_product<WT, NT>(p, s, group / 16, A, rows_valid)) return;
-        const float* bias = op.bias + (size_t)head * group;
-        for (int o = threadIdx.x; o < D * rows_valid; o += kThreads) {
-            const int n = o / rows_valid, rl = o % rows_valid;
-            A.q[rl * 64 + n] = (A.res[n * 8 + rl] + __ldg(bias + n)) * p.scale;
-        }
-        consumer_sync();
-        // This split's partial (max, sum, unnormalised row) of every row.
-        Trace tra = trace_of(p.profile);
-        tra.begin();
-        const int k0 = split * op.chunk;
-        const int n_keys = min(op.key_count, k0 + op.chunk) - k0;
-        auto partial_of = [&](int rl) {
-            return p.partial + (((size_t)(r0 + rl) * H + head) * S + split) * (D + 2);
-        };
-        if (rows_valid <= 2) {
-            for (int rl = 0; rl < rows_valid; ++rl) {
-                const size_t base = (size_t)(r0 + rl) * op.window_stride + (size_t)head * D;
-                const float2 ml = cta_attention<WT, true>(A.q + rl * 64, static_cast<const WT*>(op.keys) + base,
-                                                          static_cast<const WT*>(op.values) + base, op.key_stride, D,
-                                                          k0, n_keys, A.att);
-                const float* row = A.att + 8 + kFold;
-                float* out = partial_of(rl);
-                for (int c = threadIdx.x; c < D; c += kThreads) out[2 + c] = n_keys > 0 ? row[c] : 0.f;
-                if (threadIdx.x == 0) {
-                    out[0] = ml.x;
-                    out[1] = ml.y;
-                }
-                consumer_sync();
-            }
-        } else {
-            const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-            for (int rl = warp; rl < rows_valid; rl += kWarps) {
-                const size_t base = (size_t)(r0 + rl) * op.window_stride + (size_t)head * D;
-                float* out = partial_of(rl);
-                if (n_keys > 0) {
-                    const float2 ml = warp_attention<WT, true>(A.q + rl * 64, static_cast<const WT*>(op.keys) + base,
-                                                               static_cast<const WT*>(op.values) + base,
-                                                               op.key_stride, D, k0, n_keys, A.att + warp * kWarpKeys,
-                                                               out + 2);
-                    if (lane == 0) {
-                        out[0] = ml.x;
-                        out[1] = ml.y;
-                    }
-                } else {
-                    for (int c = lane; c < D + 2; c += 32) out[c] = c == 0 ? -INFINITY : 0.f;
-                }
-            }
-        }
-        if (head == 0 && split == 0) zero_rows(p.h, r0, rows_valid, d);
-        __threadfence();
-        consumer_sync();
-        tra.end(kTrAttention);
-        if (threadIdx.x == 0) {
-            unsigned* counter = p.combine_counters + (size_t)r_tile * H + head;
-            is_last = atomicAdd(counter, 1u) == (unsigned)(S - 1);
-            if (is_last) atomicExch(counter, 0u);
-        }
-        consumer_sync();
-        if (!is_last) continue;
-        __threadfence();
-        // The last split joins the splits of every row (SingleQueryAttention.h:11-37)
-        // and adds the v_proj bias (the weights sum to one).
-        for (int o = threadIdx.x; o < rows_valid * op.kp2; o += kThreads) {
-            const int rl = o / op.kp2, c = o % op.kp2;
-            float y = 0.f;
-            if (c < D) {
-                const float* part = p.partial + ((size_t)(r0 + rl) * H + head) * S * (D + 2);
-                float mx = -INFINITY;
-                for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, ld_cg(part + (size_t)sp * (D + 2)));
-                float l = 0.f, acc = 0.f;
-                for (int sp = 0; sp < S; ++sp) {
-                    const float ms = ld_cg(part + (size_t)sp * (D + 2));
-                    if (ms == -INFINITY) continue;
-                    const float f = __expf(ms - mx);
-                    l += ld_cg(part + (size_t)sp * (D + 2) + 1) * f;
-                    acc += ld_cg(part + (size_t)sp * (D + 2) + 2 + c) * f;
-                }
-                y = acc / l + __ldg(op.value_bias + head * D + c);
-            }
-            A.o16[rl * ps + c] = Half16<WT>::from_float(y);
-        }
-        consumer_sync();
-        // X2 += the head's slice of out_proj.
-        Trace trd = trace_of(p.profile);
-        trd.begin();
-        direct_tiled_product<WT>(static_cast<const unsigned char*>(op.weight2) + (size_t)head * op.item_stride2,
-                                 round16(d) / 16, op.kp2 / 32, A.o16, ps, rows_valid, [&](int n, int rl, float v) {
-                                     if (n >= d || rl >= rows_valid) return;
-                                     atomicAdd(p.x2 + (size_t)(r0 + rl) * d + n, v);
-                                 });
-        consumer_sync();
-        trd.end(kTrEpilogue);
-    }
-}
-
-// Feed-forward block: item (fc1 chunk, 8 rows).  Reads X2, adds into X0,
-// zeroes X1.
-template <typename WT, int NT>
-__device__ void op_ffn_block(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
-    const BlockArea<WT> A = block_area<WT>(p, work);
-    const int d = p.width, FC = op.slice, chunks_n = p.ffn / FC;
-    const int r_tiles = row_tiles(p.rows, kBlockRows);
-    const int ps = tile_pitch(op.kp2);
-    int cached = -1;
-    for (int item = blockIdx.x; item < chunks_n * r_tiles; item += gridDim.x) {
-        const int j = item % chunks_n, r_tile = item / chunks_n;
-        const int r0 = r_tile * kBlockRows, rows_valid = min(kBlockRows, p.rows - r0);
-        // Chunk 0's item also forwards X2 + the fc2 bias into X0.
-        if (cached != r_tile || j == 0) {
-            consumer_sync();
-            Trace trn = trace_of(p.profile);
-            trn.begin();
-            layer_norm_tile<WT>(p, p.x2, op.gamma, op.beta, r0, rows_valid, 1, 0, A.xs, A.pitch, nullptr,
-                                j == 0 ? p.h : nullptr, op.bias2);
-            consumer_sync();
-            trn.end(kTrNorm);
-            cached = r_tile;
-        }
-        if (!split_product<WT, NT>(p, s, FC / 16, A, rows_valid)) return;
-        const float* bias = op.bias + (size_t)j * FC;
-        for (int o = threadIdx.x; o < rows_valid * op.kp2; o += kThreads) {
-            const int rl = o / op.kp2, c = o % op.kp2;
-            const float v = c < FC ? gelu_exact(A.res[c * 8 + rl] + __ldg(bias + c)) : 0.f;
-            A.o16[rl * ps + c] = Half16<WT>::from_float(v);
-        }
-        consumer_sync();
-        // X0 += the fc2 slice of this chunk.
-        if (!tiled_product<WT, NT>(p, s, round16(d) / 16, op.kp2 / 32, op.group2, A.o16, ps, rows_valid,
-                                   [&](int n, int rl, float v) {
-                                       if (n >= d || rl >= rows_valid) return;
-                                       atomicAdd(p.h + (size_t)(r0 + rl) * d + n, v);
-                                   }))
-            return;
-        if (j == 0) zero_rows(p.x1, r0, rows_valid, d);
-        consumer_sync();
+        combine_splits<WT>(p, op, r, head, fold);
     }
 }
 
@@ -1632,9 +1145,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
             case kOpSelfAttention: op_self_attention<WT>(p, op, position, work); break;
             case kOpCrossAttention: op_cross_attention<WT>(p, op, work); break;
             case kOpLogits: op_logits<WT, NT>(p, position, s, work); break;
-            case kOpSelfBlock: op_self_block<WT, NT>(p, op, position, s, work); break;
-            case kOpCrossBlock: op_cross_block<WT, NT>(p, op, s, work); break;
-            case kOpFeedForwardBlock: op_ffn_block<WT, NT>(p, op, s, work); break;
             }
             if (!grid_barrier(p.barrier, epoch, p.state)) {
                 trace_flush(p);
@@ -1651,25 +1161,24 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
 
 // Shared memory past the ring: the largest work area any op of the launch uses.
 template <typename WT, int NT>
-size_t work_bytes(const StepParams& p, int max_chunk, bool fused) {
+size_t work_bytes(const StepParams& p, int max_chunk) {
     constexpr int RT = 8 * NT;
     const size_t product = (size_t)RT * tile_pitch(p.kpd) * sizeof(WT) +
                            sizeof(float) * (kWarps * 16 * RT + 16 * RT) + (size_t)p.out_rows * 8 +
                            sizeof(float) * 2 * kWarps * RT;
     const size_t attention = sizeof(float) * (kAttentionFixed + std::max(max_chunk, p.max_positions));
     size_t work = std::max(product, attention);
-    if (fused) work = std::max(work, block_area_bytes(p.kpd, (int)sizeof(WT), p.max_positions));
     return (work + 127) / 128 * 128;
 }
 
 template <typename WT, int NT>
-size_t shared_bytes(const StepParams& p, int max_chunk, bool fused) {
-    return (size_t)p.stages * p.stage_bytes + 16 * kMaxStages + work_bytes<WT, NT>(p, max_chunk, fused);
+size_t shared_bytes(const StepParams& p, int max_chunk) {
+    return (size_t)p.stages * p.stage_bytes + 16 * kMaxStages + work_bytes<WT, NT>(p, max_chunk);
 }
 
 template <typename WT, int NT>
-void launch_typed(const StepParams& p, int max_chunk, bool fused, int grid, cudaStream_t stream) {
-    const size_t smem = shared_bytes<WT, NT>(p, max_chunk, fused);
+void launch_typed(const StepParams& p, int max_chunk, int grid, cudaStream_t stream) {
+    const size_t smem = shared_bytes<WT, NT>(p, max_chunk);
     auto kernel = decode_kernel<WT, NT>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) throw std::runtime_error(std::string("decode kernel shared memory: ") + cudaGetErrorString(e));
@@ -1680,8 +1189,8 @@ void launch_typed(const StepParams& p, int max_chunk, bool fused, int grid, cuda
 }
 
 template <typename WT, int NT>
-int occupancy_typed(const StepParams& p, int max_chunk, bool fused) {
-    const size_t smem = shared_bytes<WT, NT>(p, max_chunk, fused);
+int occupancy_typed(const StepParams& p, int max_chunk) {
+    const size_t smem = shared_bytes<WT, NT>(p, max_chunk);
     auto kernel = decode_kernel<WT, NT>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
         cudaGetLastError();
@@ -1702,29 +1211,29 @@ inline int tile_columns(const StepParams& p) {
 }
 
 template <typename WT>
-void launch_rows(const StepParams& p, int max_chunk, bool fused, int grid, cudaStream_t stream) {
+void launch_rows(const StepParams& p, int max_chunk, int grid, cudaStream_t stream) {
     switch (tile_columns(p)) {
-    case 1: launch_typed<WT, 1>(p, max_chunk, fused, grid, stream); break;
-    case 2: launch_typed<WT, 2>(p, max_chunk, fused, grid, stream); break;
-    default: launch_typed<WT, 4>(p, max_chunk, fused, grid, stream); break;
+    case 1: launch_typed<WT, 1>(p, max_chunk, grid, stream); break;
+    case 2: launch_typed<WT, 2>(p, max_chunk, grid, stream); break;
+    default: launch_typed<WT, 4>(p, max_chunk, grid, stream); break;
     }
 }
 
 template <typename WT>
-int occupancy_rows(const StepParams& p, int max_chunk, bool fused) {
+int occupancy_rows(const StepParams& p, int max_chunk) {
     switch (tile_columns(p)) {
-    case 1: return occupancy_typed<WT, 1>(p, max_chunk, fused);
-    case 2: return occupancy_typed<WT, 2>(p, max_chunk, fused);
-    default: return occupancy_typed<WT, 4>(p, max_chunk, fused);
+    case 1: return occupancy_typed<WT, 1>(p, max_chunk);
+    case 2: return occupancy_typed<WT, 2>(p, max_chunk);
+    default: return occupancy_typed<WT, 4>(p, max_chunk);
     }
 }
 
 template <typename WT>
-size_t work_rows(const StepParams& p, int max_chunk, bool fused) {
+size_t work_rows(const StepParams& p, int max_chunk) {
     switch (tile_columns(p)) {
-    case 1: return work_bytes<WT, 1>(p, max_chunk, fused);
-    case 2: return work_bytes<WT, 2>(p, max_chunk, fused);
-    default: return work_bytes<WT, 4>(p, max_chunk, fused);
+    case 1: return work_bytes<WT, 1>(p, max_chunk);
+    case 2: return work_bytes<WT, 2>(p, max_chunk);
+    default: return work_bytes<WT, 4>(p, max_chunk);
     }
 }
 
@@ -1732,22 +1241,22 @@ size_t work_rows(const StepParams& p, int max_chunk, bool fused) {
 
 int decode_tile_rows(const StepParams& p) { return 8 * tile_columns(p); }
 
-size_t decode_work_bytes(bool half, const StepParams& p, int max_chunk, bool fused) {
-    return (half ? work_rows<__half>(p, max_chunk, fused) : work_rows<__nv_bfloat16>(p, max_chunk, fused)) +
+size_t decode_work_bytes(bool half, const StepParams& p, int max_chunk) {
+    return (half ? work_rows<__half>(p, max_chunk) : work_rows<__nv_bfloat16>(p, max_chunk)) +
            16 * kMaxStages;
 }
 
-int decode_blocks_per_sm(bool half, const StepParams& p, int max_chunk, bool fused) {
-    return half ? occupancy_rows<__half>(p, max_chunk, fused) : occupancy_rows<__nv_bfloat16>(p, max_chunk, fused);
+int decode_blocks_per_sm(bool half, const StepParams& p, int max_chunk) {
+    return half ? occupancy_rows<__half>(p, max_chunk) : occupancy_rows<__nv_bfloat16>(p, max_chunk);
 }
 
-void launch_decode(bool half, const StepParams& p, int max_chunk, bool fused, int grid, cudaStream_t stream) {
+void launch_decode(bool half, const StepParams& p, int max_chunk, int grid, cudaStream_t stream) {
     if (p.width > 32 * kNormMaxPerLane) throw std::invalid_argument("widths above 1536 are not supported");
     if (p.head_width > 64) throw std::invalid_argument("heads wider than 64 are not supported");
     if (p.stages < 1 || p.stages > kMaxStages || p.stage_bytes % 1024 != 0)
         throw std::invalid_argument("weight stream stages out of range");
-    if (half) launch_rows<__half>(p, max_chunk, fused, grid, stream);
-    else launch_rows<__nv_bfloat16>(p, max_chunk, fused, grid, stream);
+    if (half) launch_rows<__half>(p, max_chunk, grid, stream);
+    else launch_rows<__nv_bfloat16>(p, max_chunk, grid, stream);
 }
 
 }  // namespace wsp

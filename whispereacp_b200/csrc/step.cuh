@@ -23,23 +23,7 @@
 // with a grid-wide barrier after each op.  The decode kernel runs the list
 // once per step for as many steps as it is given, so a whole greedy decode is
 // one launch.
-//
-// A single-token step (T = 1, the loop's hot path) is lowered further, to
-// three blocks per layer, each one barrier:
-//
-//   self block   item (head, 8 rows): LN1, the head's q/k/v, attention over
-//                the cache, the head's slice of out_proj added into the next
-//                residual buffer
-//   cross block  item (head, 8 rows, key split): LN2, the head's cross q,
-//                attention over the split's encoder rows; the last split of a
-//                (head, rows) joins them and adds the head's out_proj slice
-//   ffn block    item (64 columns of fc1, 8 rows): LN3, the fc1 slice, GELU,
-//                the matching fc2 slice added into the next residual buffer
-//
-// The residual stream rotates through three fp32 buffers X0 -> X1 -> X2 -> X0:
-// a block reads one, adds its partial products (and, once, the residual and
-// the bias) into the next with fp32 reductions, and zeroes the third for the
-// block after it.
+
 #pragma once
 
 #include "common.cuh"
@@ -53,10 +37,6 @@ enum OpKind : int {
     kOpCrossAttention = 3,
     kOpLogits = 4,
     kOpNone = 5,
-    // The fused blocks of a single-token step (below).
-    kOpSelfBlock = 6,
-    kOpCrossBlock = 7,
-    kOpFeedForwardBlock = 8,
 };
 enum EpilogueKind : int { kEpQkv = 0, kEpStore = 1, kEpResidual = 2, kEpGelu = 3 };
 
@@ -105,14 +85,7 @@ struct StepOp {
     int key_count;          // cross: encoder rows attended
     int chunk, splits;      // cross: keys per item, items per (row, head)
     const float* value_bias;  // cross: v_proj bias, added after normalising
-    // fused blocks: region 2 of an item's weights (out_proj or fc2 slices),
-    // fragment-packed [d, k2] per head or per fc1 chunk, item_stride2 bytes apart
-    const void* weight2;
-    long long item_stride2;
-    int kp2;                // inner size of a region-2 slice (padded D or fc1 chunk)
-    int group2;             // region-2 tiles per stream unit
-    const float* bias2;     // out_proj / fc2 bias, added once per row
-    int slice;              // rows of a q/k/v head (D) or fc1 chunk (FC)
+    int slice;              // kEpStore: rows of a head (D), each head padded to a whole tile
 };
 
 struct StepParams {
@@ -128,9 +101,7 @@ struct StepParams {
     const float* position_table;        // fp32 [max_positions, d]
     const float* final_gamma;
     const float* final_beta;
-    float* h;                           // fp32 [R, d] (X0 of the fused blocks)
-    float* x1;                          // fp32 [R, d] residual buffers of the fused blocks
-    float* x2;
+    float* h;                           // fp32 [R, d] residual stream
     float* q;                           // fp32 [R, d]
     void* attn16;                       // 16-bit [R, kpd]
     void* ffn16;                        // 16-bit [R, kpf]

@@ -9,14 +9,13 @@ namespace wsp {
 int decode_tile_rows(const StepParams& p);
 
 // Shared memory the kernel needs past its weight-stream ring (bytes).
-size_t decode_work_bytes(bool half, const StepParams& p, int max_chunk, bool fused);
+size_t decode_work_bytes(bool half, const StepParams& p, int max_chunk);
 
 // CTAs of the decode kernel one SM holds for these parameters (0: none fit).
-int decode_blocks_per_sm(bool half, const StepParams& p, int max_chunk, bool fused);
+int decode_blocks_per_sm(bool half, const StepParams& p, int max_chunk);
 
 // One cooperative launch running p.steps steps of p.ops; max_chunk bounds the
-// keys a cross-attention item holds in shared memory; fused: the op list has
-// single-token fused blocks.
-void launch_decode(bool half, const StepParams& p, int max_chunk, bool fused, int grid, cudaStream_t stream);
+// keys a cross-attention item holds in shared memory.
+void launch_decode(bool half, const StepParams& p, int max_chunk, int grid, cudaStream_t stream);
 
 }  // namespace wsp
