@@ -249,13 +249,10 @@ public:
             require_extents(name, extents, rank, {d});
             patch_floats(L.qc_b, d, dtype, data, [&](int i) { return q_row(i); });
             break;
-        case 13:  // cross keys: rows [l*2d, l*2d+d) of the all-layer projection
-            require_extents(name, extents, rank, {d, d});
-            upload_matrix(cross_kv_w_, (size_t)layer * 2 * d, d, d, d, dtype, data);
-            break;
+        case 13:  // cross keys and values: head h of layer l is rows [K_h; V_h]
         case 14:
             require_extents(name, extents, rank, {d, d});
-            upload_matrix(cross_kv_w_, (size_t)layer * 2 * d + d, d, d, d, dtype, data);
+            upload_cross_projection(layer, which == 14 ? 1 : 0, dtype, data);
             break;
         case 15: require_extents(name, extents, rank, {d}); upload_floats(L.vc_b, 0, d, dtype, data); break;
         case 16:
@@ -308,17 +305,23 @@ public:
         ++launches_;
 
         // recordSequenceStart (Decoder.cpp:121-146): every layer's cross keys
-        // and values in one product, [rows, 2dL] per window.  The value bias
-        // is added after the attention instead (the weights sum to one).
-        const int d = shape_.width, n = 2 * d * shape_.layers;
+        // and values, per window one batched product over the (layer, head)
+        // groups, each [rows, 2D] = encoder rows x [K_h; V_h]^T, written as
+        // the cache layout [window][layer][head][X][K | V].  The value bias is
+        // added after the attention instead (the weights sum to one).
+        const int d = shape_.width, D = d / shape_.heads, X = shape_.cross_positions;
+        const int groups = shape_.layers * shape_.heads;
         const float one = 1.f, zero = 0.f;
         const cudaDataType_t type = storage_ == Storage::f16 ? CUDA_R_16F : CUDA_R_16BF;
-        cublas_check(cublasGemmStridedBatchedEx(
-                         cublas_, CUBLAS_OP_T, CUBLAS_OP_N, n, rows, d, &one, cross_kv_w_.get(), type, d, 0,
-                         encoder16_.get(), type, d, (long long)shape_.cross_positions * d, &zero, cross_kv_.get(),
-                         type, n, (long long)shape_.cross_positions * n, windows_, CUBLAS_COMPUTE_32F,
-                         CUBLAS_GEMM_DEFAULT),
-                     "cross key/value projection");
+        for (int b = 0; b < windows_; ++b) {
+            const size_t window = (size_t)b * groups * X * 2 * D;
+            cublas_check(cublasGemmStridedBatchedEx(
+                             cublas_, CUBLAS_OP_T, CUBLAS_OP_N, 2 * D, rows, d, &one, cross_kv_w_.get(), type, d,
+                             (long long)2 * D * d, encoder16_.get<uint16_t>() + (size_t)b * X * d, type, d, 0,
+                             &zero, cross_kv_.get<uint16_t>() + window, type, 2 * D, (long long)X * 2 * D, groups,
+                             CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
+                         "cross key/value projection");
+        }
         CUDA_CHECK(cudaMemsetAsync(state_.get(), 0, kStateWords * sizeof(int), stream_));
         CUDA_CHECK(cudaGetLastError());
         active_cross_ = rows;
@@ -658,14 +661,6 @@ private:
         masks_.allocate(2 * (size_t)shape_.vocabulary_size * 4);
     }
 
-    // Most cross-attention splits a step can use: enough items for the grid
-    // at one row, never chunks under 32 keys or over 2048.
-    int max_cross_splits() const {
-        const int X = shape_.cross_positions;
-        int s = (kMaxBlocksPerSm * sm_count_ + shape_.heads - 1) / shape_.heads;
-        s = std::min(s, std::max(1, (X + 31) / 32));
-        return std::max({1, s, (X + kMaxCrossChunk - 1) / kMaxCrossChunk});
-    }
 
     void ensure_row_capacity(int tokens) {
         if (tokens <= token_capacity_) return;
@@ -674,9 +669,10 @@ private:
         const size_t d = shape_.width, f = shape_.feed_forward_width, H = shape_.heads, D = d / H;
         hidden_.allocate(R * d * 4);
         queries_.allocate(R * d * 4);
+        normalised_.allocate(R * padded(d) * 2);
         attended_.allocate(R * padded(d) * 2);
         feed_forward_.allocate(R * padded(f) * 2);
-        partial_.allocate(R * H * max_cross_splits() * (D + 2) * 4);
+        partial_.allocate(R * H * kMaxCrossSplits * (D + 2) * 4);
         const size_t grid = (size_t)kMaxBlocksPerSm * sm_count_;
         candidate_values_.allocate(R * grid * 4);
         candidate_indices_.allocate(R * grid * 4);
@@ -714,31 +710,56 @@ private:
         case kOpSelfAttention: return WSP_KERNEL_SELF_ATTENTION;
         case kOpCrossAttention: return WSP_KERNEL_CROSS_ATTENTION;
         case kOpLogits: return WSP_KERNEL_LOGITS_ARGMAX;
+        case kOpNorm: return WSP_KERNEL_LAYER_NORM;
         }
         return WSP_KERNEL_OTHER;
     }
 
-    static constexpr int kMaxCrossChunk = 2048;
+    // Keys a CTA-wide attention item scores at once beyond the self
+    // capacity (the self attention holds max_positions scores).
+    static constexpr int kMaxCrossChunk = 0;
     static constexpr int kMaxBlocksPerSm = 2;
 
     // The step: recordDecoderStep (Decoder.cpp:151-177) with decoderLayer
     // (Decoder.cpp:73-115), lowered onto the ops of step.cuh.
-    std::vector<StepOp> build_ops(int R, int grid, int* max_chunk) const {
+    // With more rows than this, each LayerNorm runs once as a norm op rather
+    // than in the prologue of every CTA's product.
+    static constexpr int kInlineNormRows = 8;
+
+    // A product's LayerNorm prologue (gamma, beta), or -- past
+    // kInlineNormRows rows -- a norm op ahead of it and the product reading
+    // the normalised rows.
+    void normalised_input(std::vector<StepOp>& ops, StepOp& product, const DeviceBuffer& gamma,
+                          const DeviceBuffer& beta, int R) const {
+        if (R <= kInlineNormRows) {
+            product.gamma = gamma.get<float>();
+            product.beta = beta.get<float>();
+            return;
+        }
+        StepOp norm{};
+        norm.kind = kOpNorm;
+        norm.gamma = gamma.get<float>();
+        norm.beta = beta.get<float>();
+        norm.out = normalised_.get();
+        norm.ld_out = padded(shape_.width);
+        norm.norm_rows = R;
+        norm.norm_step = 1;
+        norm.norm_offset = 0;
+        ops.push_back(norm);
+        product.input16 = normalised_.get();
+        product.ld_input = padded(shape_.width);
+    }
+
+    std::vector<StepOp> build_ops(int R, int grid, int stage_bytes, const StepParams& p) const {
         const int d = shape_.width, f = shape_.feed_forward_width, H = shape_.heads;
         const int kpd = padded(d), kpf = padded(f);
         const size_t elem = 2;
         const size_t self_layer = (size_t)windows_ * shape_.max_positions * d * elem;
-        const size_t n_cross = (size_t)2 * d * shape_.layers;
+        const CrossSplit cs = cross_split(R, grid, stage_bytes);
         std::vector<StepOp> ops;
         StepOp e{};
         e.kind = kOpEmbed;
         ops.push_back(e);
-        int splits = (grid + R * H - 1) / (R * H);
-        splits = std::max(splits, (active_cross_ + kMaxCrossChunk - 1) / kMaxCrossChunk);
-        splits = std::min(splits, std::max(1, (active_cross_ + 31) / 32));
-        splits = std::max(1, splits);
-        const int chunk = (active_cross_ + splits - 1) / splits;
-        *max_chunk = chunk;
         for (int l = 0; l < shape_.layers; ++l) {
             const LayerBuffers& W = layers_[l];
             auto product = [&](int epilogue, const DeviceBuffer& w, int n, int kp, const DeviceBuffer& bias) {
@@ -754,8 +775,7 @@ private:
             // h += out_proj(self_attention(self_attn_layer_norm(h)))  (Decoder.cpp:80-91)
             const int D = d / H;
             StepOp qkv = product(kEpQkv, W.qkv_w, H * (int)round16(3 * D), kpd, W.qkv_b);
-            qkv.gamma = W.ln1_w.get<float>();
-            qkv.beta = W.ln1_b.get<float>();
+            normalised_input(ops, qkv, W.ln1_w, W.ln1_b, R);
             qkv.out = queries_.get();
             qkv.ld_out = d;
             qkv.self_keys = self_keys_.get<char>() + l * self_layer;
@@ -777,20 +797,21 @@ private:
             // h += out_proj(cross_attention(encoder_attn_layer_norm(h)))  (Decoder.cpp:93-104)
             StepOp cq = product(kEpStore, W.qc_w, H * (int)round16(D), kpd, W.qc_b);
             cq.slice = D;
-            cq.gamma = W.ln2_w.get<float>();
-            cq.beta = W.ln2_b.get<float>();
+            normalised_input(ops, cq, W.ln2_w, W.ln2_b, R);
             cq.out = queries_.get();
             cq.ld_out = d;
             ops.push_back(cq);
             StepOp cross{};
             cross.kind = kOpCrossAttention;
-            cross.keys = cross_kv_.get<char>() + (size_t)l * 2 * d * elem;
-            cross.values = cross_kv_.get<char>() + ((size_t)l * 2 * d + d) * elem;
-            cross.key_stride = (long long)n_cross;
-            cross.window_stride = (long long)shape_.cross_positions * n_cross;
+            const long long head_block = (long long)shape_.cross_positions * 2 * D;
+            cross.keys = cross_kv_.get<char>() + (size_t)l * H * head_block * elem;
+            cross.key_stride = 2 * D;
+            cross.head_stride = head_block;
+            cross.window_stride = (long long)shape_.layers * H * head_block;
             cross.key_count = active_cross_;
-            cross.splits = splits;
-            cross.chunk = chunk;
+            cross.chunk = cs.chunk;
+            cross.span = cs.span;
+            cross.splits = cs.splits;
             cross.value_bias = W.vc_b.get<float>();
             ops.push_back(cross);
             StepOp cout = product(kEpResidual, W.oc_w, d, kpd, W.oc_b);
@@ -801,8 +822,7 @@ private:
             ops.push_back(cout);
             // h += fc2(gelu(fc1(final_layer_norm(h))))  (Decoder.cpp:106-114)
             StepOp up = product(kEpGelu, W.fc1_w, f, kpd, W.fc1_b);
-            up.gamma = W.ln3_w.get<float>();
-            up.beta = W.ln3_b.get<float>();
+            normalised_input(ops, up, W.ln3_w, W.ln3_b, R);
             up.out = feed_forward_.get();
             up.ld_out = kpf;
             ops.push_back(up);
@@ -817,8 +837,49 @@ private:
         // (Decoder.cpp:170-176, Whisper::encodeSampling Whisper.cpp:1169-1184).
         StepOp logits{};
         logits.kind = kOpLogits;
+        if (p.out_rows > kInlineNormRows) {
+            StepOp norm{};
+            norm.kind = kOpNorm;
+            norm.gamma = final_w_.get<float>();
+            norm.beta = final_b_.get<float>();
+            norm.out = normalised_.get();
+            norm.ld_out = kpd;
+            norm.norm_rows = p.out_rows;
+            norm.norm_step = p.row_step;
+            norm.norm_offset = p.row_offset;
+            norm.norm_hidden = p.hidden_out;
+            ops.push_back(norm);
+            logits.input16 = normalised_.get();
+            logits.ld_input = kpd;
+        }
         ops.push_back(logits);
         return ops;
+    }
+
+    // How a step splits its cross attention: `chunk` keys per stream unit (a
+    // stage's worth), and for each (row, head) `splits` items of `span`
+    // units.  A CTA works through its items one after another, so the cost
+    // is its items' units plus a fixed cost per item (the query load, and
+    // with several splits the join), in units.
+    struct CrossSplit { int chunk, span, splits; };
+    CrossSplit cross_split(int R, int grid, int stage_bytes) const {
+        const int D = head_width();
+        const int chunk = std::max(1, std::min({kMaxCrossUnitKeys, stage_bytes / (4 * D), active_cross_}));
+        const int units = (active_cross_ + chunk - 1) / chunk;
+        const long long pairs = (long long)R * shape_.heads;
+        CrossSplit best{chunk, units, 1};
+        double best_cost = 1e30;
+        for (int span = 1; span <= units; ++span) {
+            const int splits = (units + span - 1) / span;
+            if (splits > kMaxCrossSplits) continue;
+            const long long per_cta = (pairs * splits + grid - 1) / grid;
+            const double cost = (double)per_cta * (span + (splits > 1 ? 2.0 : 1.0));
+            if (cost < best_cost) {
+                best_cost = cost;
+                best = CrossSplit{chunk, span, splits};
+            }
+        }
+        return best;
     }
 
     // The weight-stream schedule of every CTA (schedule.h), into device memory.
@@ -847,6 +908,7 @@ private:
             if (b.get()) ranges.push_back({(size_t)b.get(), (size_t)b.get() + b.bytes()});
         };
         add(token_table_);
+        add(cross_kv_);
         for (int l = 0; l < shape_.layers; ++l) {
             const LayerBuffers& W = layers_[l];
             add(W.qkv_w); add(W.o_w); add(W.qc_w); add(W.oc_w); add(W.fc1_w); add(W.fc2_w);
@@ -936,10 +998,9 @@ private:
         const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk);
         if (blocks <= 0) throw CudaFailure("the decode kernel does not fit on an SM", false);
         const int grid = sm_count_ * std::min(blocks, kMaxBlocksPerSm);
-        int max_chunk = 0;
         std::vector<StepOp>& ops = sample ? (T == 1 ? ops_step_ : ops_prompt_) : ops_teacher_;
         DeviceBuffer& ops_dev = sample ? (T == 1 ? ops_step_dev_ : ops_prompt_dev_) : ops_teacher_dev_;
-        ops = build_ops(R, grid, &max_chunk);
+        ops = build_ops(R, grid, p.stage_bytes, p);
         if (ops_dev.bytes() < ops.size() * sizeof(StepOp)) ops_dev.allocate(ops.size() * sizeof(StepOp));
         CUDA_CHECK(cudaMemcpyAsync(ops_dev.get(), ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice,
                                    stream_));
@@ -1017,14 +1078,21 @@ private:
 
     // rows x cols of a row-major [rows, cols] tensor into dst rows
     // [row_offset, row_offset+rows) of pitch ld, narrowed to the storage type.
-    void upload_matrix(DeviceBuffer& dst, size_t row_offset, int rows, int cols, int ld, wsp_dtype dtype,
-                       const void* data) {
-        std::vector<uint16_t> v((size_t)rows * ld, 0);
-        for (int r = 0; r < rows; ++r)
-            for (int c = 0; c < cols; ++c)
-                v[(size_t)r * ld + c] = narrow(widen(data, dtype, (size_t)r * cols + c), storage_);
-        CUDA_CHECK(cudaMemcpy(dst.get<uint16_t>() + row_offset * ld, v.data(), v.size() * 2, cudaMemcpyHostToDevice));
+    // Cross k_proj (kv 0) or v_proj (kv 1) of a layer into the projection
+    // that writes the cross caches: per layer and head, the head's D key rows
+    // then its D value rows, [L][H][2D][d], so the product of a window's
+    // encoder rows with one (layer, head) group is [X][K | V].
+    void upload_cross_projection(int layer, int kv, wsp_dtype dtype, const void* data) {
+        const int d = shape_.width, H = shape_.heads, D = d / H;
+        std::vector<uint16_t> v((size_t)d * d);
+        for (size_t i = 0; i < v.size(); ++i) v[i] = narrow(widen(data, dtype, i), storage_);
+        for (int h = 0; h < H; ++h) {
+            const size_t row = ((size_t)(layer * H + h) * 2 + kv) * D;
+            CUDA_CHECK(cudaMemcpy(cross_kv_w_.get<uint16_t>() + row * d, v.data() + (size_t)h * D * d,
+                                  (size_t)D * d * 2, cudaMemcpyHostToDevice));
+        }
     }
+
 
     // rows x cols of a row-major [rows, cols] tensor into rows
     // [row_offset, row_offset+rows) of a fragment-packed [*, kp] matrix
@@ -1066,7 +1134,7 @@ private:
 
     DeviceBuffer self_keys_, self_values_, cross_kv_, encoder_staging_, encoder16_;
     DeviceBuffer ring_, ring_prompt_, state_, masks_;
-    DeviceBuffer hidden_, queries_, attended_, feed_forward_, partial_;
+    DeviceBuffer hidden_, queries_, normalised_, attended_, feed_forward_, partial_;
     DeviceBuffer candidate_values_, candidate_indices_, row_tokens_, counters_;
     DeviceBuffer barrier_, ended_, profile_;
     DeviceBuffer logits_staging_, hidden_staging_;

@@ -67,6 +67,28 @@ inline void append_region(const Region& r, int stage_chunks, std::vector<Schedul
     }
 }
 
+// Cross attention: the CTA's items (cta, cta + grid, ...), each item's
+// units (one per `chunk` keys) in order, as op_cross_attention reads them.
+inline void append_cross_units(const StepParams& p, const StepOp& op, int cta, int grid,
+                               std::vector<ScheduleEntry>& out) {
+    const int S = op.splits, H = p.heads;
+    const int items = p.rows * H * S;
+    const int units = (op.key_count + op.chunk - 1) / op.chunk;
+    const size_t key_bytes = 4 * (size_t)p.head_width;
+    for (int it = cta; it < items; it += grid) {
+        const int split = it % S, head = (it / S) % H, r = it / (S * H), b = r / p.tokens;
+        const int count = std::max(0, std::min(op.span, units - split * op.span));
+        for (int t = 0; t < count; ++t) {
+            const int k0 = (split * op.span + t) * op.chunk;
+            const int n = std::min(op.chunk, op.key_count - k0);
+            const size_t element = (size_t)b * op.window_stride + (size_t)head * op.head_stride +
+                                   (size_t)k0 * op.key_stride;
+            out.push_back(schedule_entry(static_cast<const unsigned char*>(op.keys) + element * 2,
+                                         (unsigned)(n * key_bytes)));
+        }
+    }
+}
+
 // The per-CTA schedules of a launch, concatenated, and their offsets.
 inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, int grid, int rt,
                            std::vector<ScheduleEntry>& units, std::vector<unsigned>& offsets) {
@@ -75,6 +97,10 @@ inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, 
     offsets.assign(1, 0u);
     for (int cta = 0; cta < grid; ++cta) {
         for (const StepOp& op : ops) {
+            if (op.kind == kOpCrossAttention) {
+                append_cross_units(p, op, cta, grid, units);
+                continue;
+            }
             const int items = op_items(p, op, rt);
             for (int item = cta; item < items; item += grid) {
                 Region r;

@@ -24,7 +24,7 @@ namespace {
 // Consumer warps of the decode kernel: 7, so that with the producer warp a
 // CTA is 8 warps -- two per SM sub-partition, each thread keeping the full
 // register budget.
-constexpr int kWarps = 7;
+constexpr int kWarps = kStepWarps;
 constexpr int kThreads = 32 * kWarps;
 
 // ------------------------------------------------------------ memory access
@@ -422,6 +422,31 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
 
 __device__ __forceinline__ int round16(int n) { return (n + 15) / 16 * 16; }
 
+// Copies rows r0 .. r0+rows-1 of 16-bit rows X [.., ld] into the tile xs
+// [rows][ldx], kp values a row (a multiple of 8), all loads in flight.
+template <typename WT>
+__device__ void stage_rows(const WT* X, int ld, int r0, int rows, int kp, WT* xs, int ldx) {
+    const int per_row = kp / 8;
+    const int total = rows * per_row;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < total; i += kThreads) {
+        const int rl = i / per_row, c = (i % per_row) * 8;
+        *reinterpret_cast<uint4*>(xs + (size_t)rl * ldx + c) = ld_cg4(X + (size_t)(r0 + rl) * ld + c);
+    }
+}
+
+// LayerNorm of op.norm_rows rows into 16-bit rows, a row per CTA at a time
+// with the whole CTA on it.
+template <typename WT>
+__device__ void op_norm(const StepParams& p, const StepOp& op) {
+    WT* out = static_cast<WT*>(op.out);
+    for (int row = blockIdx.x; row < op.norm_rows; row += gridDim.x) {
+        consumer_sync();
+        layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, row, 1, op.norm_step, op.norm_offset,
+                            out + (size_t)row * op.ld_out, op.ld_out, op.norm_hidden);
+    }
+}
+
 // ------------------------------------------------------------------ products
 
 // Pitch (elements) of a normalised input tile in shared memory: rows 64
@@ -592,12 +617,17 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
         const int rows_valid = min(RT, p.rows - r0);
         float acc[NT][4];
         bool ok;
-        if (normalise) {
+        if (normalise || op.kp == p.kpd) {
+            // The tile's input rows in shared memory, once per row tile:
+            // normalised here, or copied from 16-bit rows.
             if (cached_tile != r_tile) {
                 consumer_sync();
                 Trace trn = trace_of(p.profile);
                 trn.begin();
-                layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, xs, pitch, nullptr);
+                if (normalise)
+                    layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, xs, pitch, nullptr);
+                else
+                    stage_rows<WT>(static_cast<const WT*>(op.input16), op.ld_input, r0, rows_valid, op.kp, xs, pitch);
                 consumer_sync();
                 trn.end(kTrNorm);
                 cached_tile = r_tile;
@@ -665,7 +695,7 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
 // writes each window's sampled id into its next token slot and advances the
 // position.
 template <typename WT, int NT>
-__device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned char* work) {
+__device__ void op_logits(const StepParams& p, const StepOp& op, int position, Stream& s, unsigned char* work) {
     constexpr int RT = 8 * NT;
     const int pitch = tile_pitch(p.kpd);
     WT* xs = reinterpret_cast<WT*>(work);
@@ -703,8 +733,11 @@ __device__ void op_logits(const StepParams& p, int position, Stream& s, unsigned
         consumer_sync();
         Trace trn = trace_of(p.profile);
         trn.begin();
-        layer_norm_tile<WT>(p, p.h, p.final_gamma, p.final_beta, r0, rows_valid, p.row_step, p.row_offset, xs, pitch,
-                            p.hidden_out);
+        if (op.input16)  // rows normalised by a norm op
+            stage_rows<WT>(static_cast<const WT*>(op.input16), op.ld_input, r0, rows_valid, p.kpd, xs, pitch);
+        else
+            layer_norm_tile<WT>(p, p.h, p.final_gamma, p.final_beta, r0, rows_valid, p.row_step, p.row_offset, xs,
+                                pitch, p.hidden_out);
         consumer_sync();
         trn.end(kTrNorm);
 
@@ -994,105 +1027,242 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
     }
 }
 
-// The last split of a cross-attention (row, head) joins the splits' partials
-// the way a split softmax joins (SingleQueryAttention.h:11-37): every load is
-// issued before its value is needed -- the splits' (max, sum) one thread
-// each, then each channel by kThreads / D thread groups, several splits'
-// loads in flight per thread -- so the join costs a few L2 round trips, not
-// one per split.  `fold` holds at least 3 S + kThreads floats.
+// ------------------------------------------------------- cross attention
+
+// The keys and values of one (window, layer, head) are one contiguous block
+// of encoder rows [K | V], 2D 16-bit values each, so `chunk` consecutive
+// keys are one bulk copy: they stream through the ring like weights, and the
+// producer fetches them while the ops before this one run.  An item (row,
+// head, split) covers `span` chunks; CTA c takes items c, c + grid, ... and
+// all its warps work on every chunk, each on its own keys: key j belongs to
+// warp (j / 4) % kWarps.  Per chunk, a warp scores its keys, the CTA agrees
+// on the running maximum (one barrier), each warp weights its keys' values,
+// and the CTA folds the warps' sums (a second barrier) into an online
+// softmax held by threads < D (SingleQueryAttention.h:11-37 joins splits the
+// same way).  With several splits per (row, head) the last to finish joins
+// the partials.
+
+__device__ __forceinline__ int cross_units(const StepOp& op) { return (op.key_count + op.chunk - 1) / op.chunk; }
+__device__ __forceinline__ int cross_item_units(const StepOp& op, int item, int units) {
+    return max(0, min(op.span, units - (item % op.splits) * op.span));
+}
+// Key of this warp's i-th owned key slot (keys 4g..4g+3 for g = warp, warp + kWarps, ...).
+__device__ __forceinline__ int owned_key(int warp, int i) { return 4 * (warp + kWarps * (i >> 2)) + (i & 3); }
+
+// Scores of this warp's keys of the chunk into sc[]; returns their maximum.
+// 64-wide heads: 8 lanes a key, each one 16-byte piece (a conflict-free
+// 128-byte row per 8 lanes), joined by 3 shuffles.
 template <typename WT>
-__device__ void combine_splits(const StepParams& p, const StepOp& op, int r, int head, float* fold) {
-    const int D = p.head_width, S = op.splits;
-    const float* part = p.partial + ((size_t)r * p.heads + head) * S * (D + 2);
-    float* m_s = fold;           // [S] split maxima
-    float* l_s = fold + S;       // [S] split sums
-    float* f_s = fold + 2 * S;   // [S] exp(max_s - max)
-    float* acc = fold + 3 * S;   // [groups][D]
-    for (int sp = threadIdx.x; sp < S; sp += kThreads) {
-        m_s[sp] = ld_cg(part + (size_t)sp * (D + 2));
-        l_s[sp] = ld_cg(part + (size_t)sp * (D + 2) + 1);
-    }
-    consumer_sync();
+__device__ __forceinline__ float cross_scores(const WT* rows, int n, int D, const float* q, float* sc) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float mx = -INFINITY;
-    for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, m_s[sp]);
-    for (int sp = threadIdx.x; sp < S; sp += kThreads) f_s[sp] = m_s[sp] == -INFINITY ? 0.f : __expf(m_s[sp] - mx);
-    consumer_sync();
-    const int groups = kThreads / D;
-    const int c = threadIdx.x % D, g = threadIdx.x / D;
-    if (g < groups) {
-        float o = 0.f;
-#pragma unroll 8
-        for (int sp = g; sp < S; sp += groups) o += ld_cg(part + (size_t)sp * (D + 2) + 2 + c) * f_s[sp];
-        acc[g * D + c] = o;
+    if (D == 64) {
+        const int sub = lane >> 3, piece = lane & 7;
+        const float4 qa = *reinterpret_cast<const float4*>(q + piece * 8);
+        const float4 qb = *reinterpret_cast<const float4*>(q + piece * 8 + 4);
+#pragma unroll 2
+        for (int g = warp; 4 * g < n; g += kWarps) {
+            const int j = 4 * g + sub;
+            float part = 0.f;
+            if (j < n) {
+                const uint4 u = *reinterpret_cast<const uint4*>(rows + (size_t)j * 128 + piece * 8);
+                const float2 f0 = Half16<WT>::pair_to_float2(u.x), f1 = Half16<WT>::pair_to_float2(u.y);
+                const float2 f2 = Half16<WT>::pair_to_float2(u.z), f3 = Half16<WT>::pair_to_float2(u.w);
+                part = qa.x * f0.x + qa.y * f0.y + qa.z * f1.x + qa.w * f1.y + qb.x * f2.x + qb.y * f2.y +
+                       qb.z * f3.x + qb.w * f3.y;
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            part += __shfl_xor_sync(0xffffffffu, part, 4);
+            if (j < n) {
+                if (piece == 0) sc[j] = part;
+                mx = fmaxf(mx, part);
+            }
+        }
+    } else {
+        for (int i = lane;; i += 32) {
+            const int j = owned_key(warp, i);
+            if (j >= n) break;
+            const WT* k = rows + (size_t)j * 2 * D;
+            float sum = 0.f;
+            for (int c = 0; c < D; c += 2) {
+                const float2 f = Half16<WT>::pair_to_float2(*reinterpret_cast<const uint32_t*>(k + c));
+                sum += q[c] * f.x + q[c + 1] * f.y;
+            }
+            sc[j] = sum;
+            mx = fmaxf(mx, sum);
+        }
     }
-    consumer_sync();
-    if (threadIdx.x < D) {
-        float l = 0.f, o = 0.f;
-        for (int sp = 0; sp < S; ++sp) l += l_s[sp] * f_s[sp];
-        for (int gg = 0; gg < groups; ++gg) o += acc[gg * D + threadIdx.x];
-        float y = o / l;
-        if (op.value_bias) y += op.value_bias[head * D + threadIdx.x];
-        static_cast<WT*>(p.attn16)[(size_t)r * p.kpd + head * D + threadIdx.x] = Half16<WT>::from_float(y);
+    return warp_max(mx);
+}
+
+// exp(sc[j] - m) for this warp's keys, written back; returns their sum.
+__device__ __forceinline__ float cross_weights(int n, float m, float* sc) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float sum = 0.f;
+    for (int i = lane;; i += 32) {
+        const int j = owned_key(warp, i);
+        if (j >= n) break;
+        const float e = __expf(sc[j] - m);
+        sc[j] = e;
+        sum += e;
+    }
+    __syncwarp();
+    return warp_sum(sum);
+}
+
+// sum over this warp's keys of sc[j] V[j] into a[4]: 64-wide heads give
+// lane l channels 4*(l%16) .. +3 (the half-warps take alternate keys,
+// 128-byte rows, then join); other widths give lane l channels l and l + 32.
+template <typename WT>
+__device__ __forceinline__ void cross_values(const WT* rows, int n, int D, const float* sc, float (&a)[4]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    a[0] = a[1] = a[2] = a[3] = 0.f;
+    if (D == 64) {
+        const int half = lane >> 4, hl = lane & 15;
+#pragma unroll 4
+        for (int i = half;; i += 2) {
+            const int j = owned_key(warp, i);
+            if (j >= n) break;
+            const uint2 v = *reinterpret_cast<const uint2*>(rows + (size_t)j * 128 + 64 + 4 * hl);
+            const float w = sc[j];
+            const float2 f0 = Half16<WT>::pair_to_float2(v.x), f1 = Half16<WT>::pair_to_float2(v.y);
+            a[0] += w * f0.x;
+            a[1] += w * f0.y;
+            a[2] += w * f1.x;
+            a[3] += w * f1.y;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] += __shfl_xor_sync(0xffffffffu, a[i], 16);
+    } else {
+        for (int i = 0;; ++i) {
+            const int j = owned_key(warp, i);
+            if (j >= n) break;
+            const WT* v = rows + (size_t)j * 2 * D + D;
+            const float w = sc[j];
+            if (lane < D) a[0] += w * Half16<WT>::to_float(v[lane]);
+            if (lane + 32 < D) a[1] += w * Half16<WT>::to_float(v[lane + 32]);
+        }
     }
 }
 
-// Cross-attention item (row, head, split): the split's max, sum and
-// unnormalised row; the last split of a (row, head) to finish joins them the
-// way a split softmax joins (SingleQueryAttention.h:11-37) and adds the
-// v_proj bias (the weights sum to one, so the bias passes through).
+// Channel of accumulator i of this lane (-1: none).
+__device__ __forceinline__ int cross_channel(int D, int i) {
+    const int lane = threadIdx.x & 31;
+    if (D == 64) return lane < 16 ? 4 * lane + i : -1;
+    const int c = lane + 32 * i;
+    return i < 2 && c < D ? c : -1;
+}
+
+// The last split of a (row, head), one warp: joins the splits' partials
+// [max, sum, D values] with every load of a lane in flight at once.
 template <typename WT>
-__device__ void op_cross_attention(const StepParams& p, const StepOp& op, unsigned char* smem) {
-    float* q = reinterpret_cast<float*>(smem);
-    float* scratch = q + 64;
-    float* fold = scratch + 8;
-    float* result = fold + kFold;
-    float* scores = result + 64;
+__device__ void cross_join(const StepParams& p, const StepOp& op, int r, int head) {
+    const int lane = threadIdx.x & 31;
+    const int D = p.head_width, S = op.splits;
+    const float* part = p.partial + ((size_t)r * p.heads + head) * S * (D + 2);
+    const float m_own = lane < S ? ld_cg(part + (size_t)lane * (D + 2)) : -INFINITY;
+    const float l_own = lane < S ? ld_cg(part + (size_t)lane * (D + 2) + 1) : 0.f;
+    const float mx = warp_max(m_own);
+    const float f_own = m_own == -INFINITY ? 0.f : __expf(m_own - mx);
+    const float l = warp_sum(l_own * f_own);
+    float o[2] = {0.f, 0.f};
+    const int c0 = lane, c1 = lane + 32;
+#pragma unroll 8
+    for (int sp = 0; sp < S; ++sp) {
+        const float f = __shfl_sync(0xffffffffu, f_own, sp);
+        const float* ps = part + (size_t)sp * (D + 2) + 2;
+        if (c0 < D) o[0] += ld_cg(ps + c0) * f;
+        if (c1 < D) o[1] += ld_cg(ps + c1) * f;
+    }
+    WT* out = static_cast<WT*>(p.attn16) + (size_t)r * p.kpd + head * D;
+    if (c0 < D) out[c0] = Half16<WT>::from_float(o[0] / l + (op.value_bias ? __ldg(op.value_bias + head * D + c0) : 0.f));
+    if (c1 < D) out[c1] = Half16<WT>::from_float(o[1] / l + (op.value_bias ? __ldg(op.value_bias + head * D + c1) : 0.f));
+}
+
+// Shared memory: [q: 64][max: 2 x 8][sum: 2 x 8][fold: 2 x kWarps x 64][scores: kMaxCrossUnitKeys]
+template <typename WT>
+__device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int D = p.head_width, H = p.heads, S = op.splits;
+    const int units = cross_units(op);
+    const int items = p.rows * H * S;
+    float* q = reinterpret_cast<float*>(work);
+    float* wmax = q + 64;
+    float* wsum = wmax + 16;
+    float* fold = wsum + 16;
+    float* sc = fold + 2 * kWarps * 64;
     __shared__ int is_last;
-    const int D = p.head_width;
-    const int S = op.splits;
-    for (int item = blockIdx.x; item < p.rows * p.heads * S; item += gridDim.x) {
-        const int split = item % S;
-        const int head = (item / S) % p.heads;
-        const int r = item / (S * p.heads);
-        const int b = r / p.tokens;
-        const int k0 = split * op.chunk;
-        const int n = min(op.key_count, k0 + op.chunk) - k0;
-        float* out = p.partial + (((size_t)r * p.heads + head) * S + split) * (D + 2);
+    int par = 0;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int split = item % S, head = (item / S) % H, r = item / (S * H);
+        const int count = cross_item_units(op, item, units);
         consumer_sync();
-        if (n <= 0) {
-            for (int c = threadIdx.x; c < D + 2; c += kThreads) out[c] = c == 0 ? -INFINITY : 0.f;
-        } else {
-            for (int c = threadIdx.x; c < D; c += kThreads)
-                q[c] = ld_cg(p.q + (size_t)r * p.width + head * D + c) * p.scale;
+        for (int c = threadIdx.x; c < D; c += kThreads) q[c] = ld_cg(p.q + (size_t)r * p.width + head * D + c) * p.scale;
+        consumer_sync();
+        float m_run = -INFINITY, l_run = 0.f, o_run = 0.f;  // o_run: channel threadIdx.x < D
+        for (int t = 0; t < count; ++t) {
+            const WT* rows = reinterpret_cast<const WT*>(acquire_unit(p, s));
+            const int k0 = (split * op.span + t) * op.chunk;
+            const int n = min(op.chunk, op.key_count - k0);
+            Trace tr = trace_of(p.profile);
+            tr.begin();
+            const float wm = cross_scores<WT>(rows, n, D, q, sc);
+            if (lane == 0) wmax[par * 8 + warp] = wm;
             consumer_sync();
-            const WT* K = static_cast<const WT*>(op.keys) + (size_t)b * op.window_stride + (size_t)head * D;
-            const WT* V = static_cast<const WT*>(op.values) + (size_t)b * op.window_stride + (size_t)head * D;
-            const float m = consumer_max(attention_scores<WT, true>(q, K, op.key_stride, D, k0, n, scores), scratch);
-            float local = 0.f;
-            for (int j = threadIdx.x; j < n; j += kThreads) {
-                const float e = __expf(scores[j] - m);
-                scores[j] = e;
-                local += e;
+            float cm = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) cm = fmaxf(cm, wmax[par * 8 + w]);
+            const float m_new = fmaxf(m_run, cm);
+            const float keep = m_run == -INFINITY ? 0.f : __expf(m_run - m_new);
+            const float ws = cross_weights(n, m_new, sc);
+            float a[4];
+            cross_values<WT>(rows, n, D, sc, a);
+            release_unit(s);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int c = cross_channel(D, i);
+                if (c >= 0) fold[(par * kWarps + warp) * 64 + c] = a[i];
             }
-            const float l = consumer_sum(local, scratch);
-            attention_values<WT, true>(scores, V, op.key_stride, D, k0, n, fold, result);
-            for (int c = threadIdx.x; c < D; c += kThreads) out[2 + c] = result[c];
-            if (threadIdx.x == 0) {
-                out[0] = m;
-                out[1] = l;
+            if (lane == 0) wsum[par * 8 + warp] = ws;
+            consumer_sync();
+            float l_chunk = 0.f, o_chunk = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) l_chunk += wsum[par * 8 + w];
+            if (threadIdx.x < D) {
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) o_chunk += fold[(par * kWarps + w) * 64 + threadIdx.x];
             }
+            o_run = o_run * keep + o_chunk;
+            l_run = l_run * keep + l_chunk;
+            m_run = m_new;
+            par ^= 1;
+            tr.end(kTrAttention);
+        }
+        if (S == 1) {
+            if (threadIdx.x < D)
+                static_cast<WT*>(p.attn16)[(size_t)r * p.kpd + head * D + threadIdx.x] = Half16<WT>::from_float(
+                    o_run / l_run + (op.value_bias ? __ldg(op.value_bias + head * D + threadIdx.x) : 0.f));
+            continue;
+        }
+        float* part = p.partial + (((size_t)r * H + head) * S + split) * (D + 2);
+        if (threadIdx.x < D) part[2 + threadIdx.x] = o_run;
+        if (threadIdx.x == 0) {
+            part[0] = m_run;
+            part[1] = l_run;
         }
         __threadfence();
         consumer_sync();
         if (threadIdx.x == 0) {
-            unsigned* counter = p.combine_counters + (size_t)r * p.heads + head;
+            unsigned* counter = p.combine_counters + (size_t)r * H + head;
             is_last = atomicAdd(counter, 1u) == (unsigned)(S - 1);
             if (is_last) atomicExch(counter, 0u);
         }
         consumer_sync();
-        if (!is_last) continue;
-        __threadfence();
-        combine_splits<WT>(p, op, r, head, fold);
+        if (is_last && warp == 0) {
+            __threadfence();
+            cross_join<WT>(p, op, r, head);
+        }
     }
 }
 
@@ -1143,8 +1313,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
             case kOpEmbed: op_embed<WT>(p, position); break;
             case kOpProduct: op_product<WT, NT>(p, op, position, s, work); break;
             case kOpSelfAttention: op_self_attention<WT>(p, op, position, work); break;
-            case kOpCrossAttention: op_cross_attention<WT>(p, op, work); break;
-            case kOpLogits: op_logits<WT, NT>(p, position, s, work); break;
+            case kOpCrossAttention: op_cross_attention<WT>(p, op, s, work); break;
+            case kOpLogits: op_logits<WT, NT>(p, op, position, s, work); break;
+            case kOpNorm: op_norm<WT>(p, op); break;
             }
             if (!grid_barrier(p.barrier, epoch, p.state)) {
                 trace_flush(p);
@@ -1166,7 +1337,8 @@ size_t work_bytes(const StepParams& p, int max_chunk) {
     const size_t product = (size_t)RT * tile_pitch(p.kpd) * sizeof(WT) +
                            sizeof(float) * (kWarps * 16 * RT + 16 * RT) + (size_t)p.out_rows * 8 +
                            sizeof(float) * 2 * kWarps * RT;
-    const size_t attention = sizeof(float) * (kAttentionFixed + std::max(max_chunk, p.max_positions));
+    const size_t attention = sizeof(float) * std::max<size_t>(kAttentionFixed + std::max(max_chunk, p.max_positions),
+                                                              64 + 32 + 2 * kWarps * 64 + kMaxCrossUnitKeys);
     size_t work = std::max(product, attention);
     return (work + 127) / 128 * 128;
 }

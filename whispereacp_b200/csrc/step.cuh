@@ -6,13 +6,18 @@
 // decoderLayer (:73-115) into StepOps:
 //
 //   embed                       h = token_table[id] + position_table[p]
+//   (norm)                      with more than a few rows, each LayerNorm
+//                               below runs once as its own op into 16-bit
+//                               rows instead of in every CTA's product
 //   per layer
 //     product  LN1 -> q,k,v     (k, v appended to the self cache)
 //     self attention            causal over keys 0..position+t
 //     product  out_proj + h     (residual)
 //     product  LN2 -> cross q
-//     cross attention           split over the encoder rows, the splits of a
-//                               (row, head) joined by the last to finish
+//     cross attention           the encoder rows' keys and values streamed
+//                               through the ring, split over warps; the
+//                               splits of a (row, head) joined by the last
+//                               to finish
 //     product  out_proj + h
 //     product  LN3 -> fc1, GELU
 //     product  fc2 + h
@@ -30,6 +35,13 @@
 
 namespace wsp {
 
+// Consumer warps of a decode-kernel CTA (a producer warp streams weights).
+constexpr int kStepWarps = 7;
+// Most keys one cross-attention stream unit carries, and most splits of a
+// (row, head).
+constexpr int kMaxCrossUnitKeys = 256;
+constexpr int kMaxCrossSplits = 32;
+
 enum OpKind : int {
     kOpEmbed = 0,
     kOpProduct = 1,
@@ -37,6 +49,7 @@ enum OpKind : int {
     kOpCrossAttention = 3,
     kOpLogits = 4,
     kOpNone = 5,
+    kOpNorm = 6,
 };
 enum EpilogueKind : int { kEpQkv = 0, kEpStore = 1, kEpResidual = 2, kEpGelu = 3 };
 
@@ -78,14 +91,27 @@ struct StepOp {
     void* self_keys;        // qkv: this layer's caches [B][max_positions][d]
     void* self_values;
     // attention
-    const void* keys;       // 16-bit: key j of window b, head h at
-    const void* values;     //   base + b*window_stride + j*key_stride + h*D
+    const void* keys;       // 16-bit.  self: key j of window b, head h at
+    const void* values;     //   base + b*window_stride + j*key_stride + h*D.
+                            // cross: keys = this layer's block; key j of
+                            // window b, head h is the row at base +
+                            // b*window_stride + h*head_stride + j*key_stride,
+                            // its D key values then its D value values
     long long key_stride;
     long long window_stride;
+    long long head_stride;
     int key_count;          // cross: encoder rows attended
-    int chunk, splits;      // cross: keys per item, items per (row, head)
+    int chunk;              // cross: keys per stream unit (<= kMaxCrossUnitKeys)
+    int span;               // cross: units per split
+    int splits;             // cross: splits per (row, head) (<= kMaxCrossSplits)
     const float* value_bias;  // cross: v_proj bias, added after normalising
     int slice;              // kEpStore: rows of a head (D), each head padded to a whole tile
+    // norm: LayerNorm(gamma, beta) of norm_rows rows of h -- row i reads h
+    // row i*norm_step + norm_offset -- into 16-bit rows `out` [norm_rows,
+    // ld_out] (zero past the width), and into fp32 norm_hidden when given.
+    // A product or the logits with input16 set and no gamma read such rows.
+    int norm_rows, norm_step, norm_offset;
+    float* norm_hidden;
 };
 
 struct StepParams {
