@@ -21,6 +21,11 @@ template <> struct Half16<__half> {
         __half2 h = *reinterpret_cast<__half2*>(&bits);
         return __half22float2(h);
     }
+    // a in the low half, b in the high half (an MMA fragment's element order).
+    static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
 };
 template <> struct Half16<__nv_bfloat16> {
     static __device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
@@ -29,7 +34,27 @@ template <> struct Half16<__nv_bfloat16> {
         __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&bits);
         return __bfloat1622float2(h);
     }
+    static __device__ __forceinline__ uint32_t pack2(float a, float b) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
 };
+
+// A pair of fp32 values as two 16-bit pairs, hi + lo, whose sum carries
+// about twice the 16-bit precision: the operand of two tensor-core products
+// that together act as one with a wider operand.
+template <typename T>
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const float ha = Half16<T>::to_float(Half16<T>::from_float(a));
+    const float hb = Half16<T>::to_float(Half16<T>::from_float(b));
+    hi = Half16<T>::pack2(a, b);
+    lo = Half16<T>::pack2(a - ha, b - hb);
+}
+
+// The position of 16-byte piece p (0..15) of cross key row j in memory and
+// in shared memory: the 8 key pieces and the 8 value pieces each rotate by
+// j % 8, so eight consecutive keys' same piece fall in eight bank groups.
+__host__ __device__ __forceinline__ int cross_piece(int p, int j) { return (p & 8) | ((p ^ j) & 7); }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

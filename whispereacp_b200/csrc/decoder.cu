@@ -322,6 +322,12 @@ public:
                              CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
                          "cross key/value projection");
         }
+        // 64-wide heads: rotate each key row's pieces into the order the
+        // tensor-core attention reads conflict-free (cross_piece).
+        if (D == 64) {
+            launch_swizzle_cross(cross_kv_.get(), (long long)windows_ * groups * X, X, stream_);
+            ++launches_;
+        }
         CUDA_CHECK(cudaMemsetAsync(state_.get(), 0, kStateWords * sizeof(int), stream_));
         CUDA_CHECK(cudaGetLastError());
         active_cross_ = rows;
@@ -584,8 +590,9 @@ public:
     }
 
     // Kernel launches of this library per transcription: the encoder-row
-    // narrowing, the prompt step, and the launch that runs every later step.
-    int step_launches() const { return 3; }
+    // narrowing, the cross-row rotation (64-wide heads), the prompt step, and
+    // the launch that runs every later step.
+    int step_launches() const { return head_width() == 64 ? 4 : 3; }
 
 private:
     int ring_stride() const { return shape_.max_positions + 1; }
@@ -864,7 +871,9 @@ private:
     struct CrossSplit { int chunk, span, splits; };
     CrossSplit cross_split(int R, int grid, int stage_bytes) const {
         const int D = head_width();
-        const int chunk = std::max(1, std::min({kMaxCrossUnitKeys, stage_bytes / (4 * D), active_cross_}));
+        int chunk = std::max(1, std::min({kMaxCrossUnitKeys, stage_bytes / (4 * D), active_cross_}));
+        // Units start on a multiple of 8 keys: the period of the rotated layout.
+        if (chunk < active_cross_) chunk = std::max(8, chunk / 8 * 8);
         const int units = (active_cross_ + chunk - 1) / chunk;
         const long long pairs = (long long)R * shape_.heads;
         CrossSplit best{chunk, units, 1};

@@ -40,6 +40,10 @@ constexpr int kNoAllocArgmaxCandidates = 65536;
 // time a device asks, with that device current, and remembered after.
 cudaError_t no_alloc_argmax_scratch(int device, void** scratch);
 
+// Rotates the pieces of `rows` 256-byte cross key rows (keys rows a block)
+// into the shared-memory order the tensor-core cross attention reads.
+void launch_swizzle_cross(void* data, long long rows, int keys, cudaStream_t stream);
+
 // ------------------------------------------------------------- plumbing ---
 void launch_to_storage(Storage s, const float* in, void* out, long long count, cudaStream_t stream);
 

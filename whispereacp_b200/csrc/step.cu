@@ -1049,49 +1049,23 @@ __device__ __forceinline__ int cross_item_units(const StepOp& op, int item, int 
 // Key of this warp's i-th owned key slot (keys 4g..4g+3 for g = warp, warp + kWarps, ...).
 __device__ __forceinline__ int owned_key(int warp, int i) { return 4 * (warp + kWarps * (i >> 2)) + (i & 3); }
 
-// Scores of this warp's keys of the chunk into sc[]; returns their maximum.
-// 64-wide heads: 8 lanes a key, each one 16-byte piece (a conflict-free
-// 128-byte row per 8 lanes), joined by 3 shuffles.
+// Scores of this warp's keys of the chunk into sc[] (lane per key); returns
+// their maximum.  Heads other than 64 wide.
 template <typename WT>
 __device__ __forceinline__ float cross_scores(const WT* rows, int n, int D, const float* q, float* sc) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float mx = -INFINITY;
-    if (D == 64) {
-        const int sub = lane >> 3, piece = lane & 7;
-        const float4 qa = *reinterpret_cast<const float4*>(q + piece * 8);
-        const float4 qb = *reinterpret_cast<const float4*>(q + piece * 8 + 4);
-#pragma unroll 2
-        for (int g = warp; 4 * g < n; g += kWarps) {
-            const int j = 4 * g + sub;
-            float part = 0.f;
-            if (j < n) {
-                const uint4 u = *reinterpret_cast<const uint4*>(rows + (size_t)j * 128 + piece * 8);
-                const float2 f0 = Half16<WT>::pair_to_float2(u.x), f1 = Half16<WT>::pair_to_float2(u.y);
-                const float2 f2 = Half16<WT>::pair_to_float2(u.z), f3 = Half16<WT>::pair_to_float2(u.w);
-                part = qa.x * f0.x + qa.y * f0.y + qa.z * f1.x + qa.w * f1.y + qb.x * f2.x + qb.y * f2.y +
-                       qb.z * f3.x + qb.w * f3.y;
-            }
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
-            part += __shfl_xor_sync(0xffffffffu, part, 2);
-            part += __shfl_xor_sync(0xffffffffu, part, 4);
-            if (j < n) {
-                if (piece == 0) sc[j] = part;
-                mx = fmaxf(mx, part);
-            }
+    for (int i = lane;; i += 32) {
+        const int j = owned_key(warp, i);
+        if (j >= n) break;
+        const WT* k = rows + (size_t)j * 2 * D;
+        float sum = 0.f;
+        for (int c = 0; c < D; c += 2) {
+            const float2 f = Half16<WT>::pair_to_float2(*reinterpret_cast<const uint32_t*>(k + c));
+            sum += q[c] * f.x + q[c + 1] * f.y;
         }
-    } else {
-        for (int i = lane;; i += 32) {
-            const int j = owned_key(warp, i);
-            if (j >= n) break;
-            const WT* k = rows + (size_t)j * 2 * D;
-            float sum = 0.f;
-            for (int c = 0; c < D; c += 2) {
-                const float2 f = Half16<WT>::pair_to_float2(*reinterpret_cast<const uint32_t*>(k + c));
-                sum += q[c] * f.x + q[c + 1] * f.y;
-            }
-            sc[j] = sum;
-            mx = fmaxf(mx, sum);
-        }
+        sc[j] = sum;
+        mx = fmaxf(mx, sum);
     }
     return warp_max(mx);
 }
@@ -1111,47 +1085,20 @@ __device__ __forceinline__ float cross_weights(int n, float m, float* sc) {
     return warp_sum(sum);
 }
 
-// sum over this warp's keys of sc[j] V[j] into a[4]: 64-wide heads give
-// lane l channels 4*(l%16) .. +3 (the half-warps take alternate keys,
-// 128-byte rows, then join); other widths give lane l channels l and l + 32.
+// sum over this warp's keys of sc[j] V[j] into a[2]: lane l holds channels
+// l and l + 32.  Heads other than 64 wide.
 template <typename WT>
-__device__ __forceinline__ void cross_values(const WT* rows, int n, int D, const float* sc, float (&a)[4]) {
+__device__ __forceinline__ void cross_values(const WT* rows, int n, int D, const float* sc, float (&a)[2]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    a[0] = a[1] = a[2] = a[3] = 0.f;
-    if (D == 64) {
-        const int half = lane >> 4, hl = lane & 15;
-#pragma unroll 4
-        for (int i = half;; i += 2) {
-            const int j = owned_key(warp, i);
-            if (j >= n) break;
-            const uint2 v = *reinterpret_cast<const uint2*>(rows + (size_t)j * 128 + 64 + 4 * hl);
-            const float w = sc[j];
-            const float2 f0 = Half16<WT>::pair_to_float2(v.x), f1 = Half16<WT>::pair_to_float2(v.y);
-            a[0] += w * f0.x;
-            a[1] += w * f0.y;
-            a[2] += w * f1.x;
-            a[3] += w * f1.y;
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] += __shfl_xor_sync(0xffffffffu, a[i], 16);
-    } else {
-        for (int i = 0;; ++i) {
-            const int j = owned_key(warp, i);
-            if (j >= n) break;
-            const WT* v = rows + (size_t)j * 2 * D + D;
-            const float w = sc[j];
-            if (lane < D) a[0] += w * Half16<WT>::to_float(v[lane]);
-            if (lane + 32 < D) a[1] += w * Half16<WT>::to_float(v[lane + 32]);
-        }
+    a[0] = a[1] = 0.f;
+    for (int i = 0;; ++i) {
+        const int j = owned_key(warp, i);
+        if (j >= n) break;
+        const WT* v = rows + (size_t)j * 2 * D + D;
+        const float w = sc[j];
+        if (lane < D) a[0] += w * Half16<WT>::to_float(v[lane]);
+        if (lane + 32 < D) a[1] += w * Half16<WT>::to_float(v[lane + 32]);
     }
-}
-
-// Channel of accumulator i of this lane (-1: none).
-__device__ __forceinline__ int cross_channel(int D, int i) {
-    const int lane = threadIdx.x & 31;
-    if (D == 64) return lane < 16 ? 4 * lane + i : -1;
-    const int c = lane + 32 * i;
-    return i < 2 && c < D ? c : -1;
 }
 
 // The last split of a (row, head), one warp: joins the splits' partials
@@ -1182,7 +1129,7 @@ __device__ void cross_join(const StepParams& p, const StepOp& op, int r, int hea
 
 // Shared memory: [q: 64][max: 2 x 8][sum: 2 x 8][fold: 2 x kWarps x 64][scores: kMaxCrossUnitKeys]
 template <typename WT>
-__device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
+__device__ void cross_attention_cores(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int D = p.head_width, H = p.heads, S = op.splits;
     const int units = cross_units(op);
@@ -1216,14 +1163,11 @@ __device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream
             const float m_new = fmaxf(m_run, cm);
             const float keep = m_run == -INFINITY ? 0.f : __expf(m_run - m_new);
             const float ws = cross_weights(n, m_new, sc);
-            float a[4];
+            float a[2];
             cross_values<WT>(rows, n, D, sc, a);
             release_unit(s);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int c = cross_channel(D, i);
-                if (c >= 0) fold[(par * kWarps + warp) * 64 + c] = a[i];
-            }
+            if (lane < D) fold[(par * kWarps + warp) * 64 + lane] = a[0];
+            if (lane + 32 < D) fold[(par * kWarps + warp) * 64 + lane + 32] = a[1];
             if (lane == 0) wsum[par * 8 + warp] = ws;
             consumer_sync();
             float l_chunk = 0.f, o_chunk = 0.f;
@@ -1264,6 +1208,196 @@ __device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream
             cross_join<WT>(p, op, r, head);
         }
     }
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&d)[4], const void* row) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(smem_address(row))
+                 : "memory");
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&d)[4], const void* row) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(smem_address(row))
+                 : "memory");
+}
+
+// 64-wide heads on the tensor cores.  A warp takes the unit's 16-key groups
+// 16*warp, 16*(warp + kWarps), ...:
+//   scores  m16n8k16 with q as row 0 of A (split hi + lo, so the product
+//           carries nearly fp32 q) and B = the keys, loaded by ldmatrix from
+//           rows whose pieces cross_piece rotates -- conflict-free;
+//   values  row 0 of A = the weights p (hi + lo), which the score fragments
+//           already hold in A's order, and B = the values by ldmatrix.trans.
+// Lanes 0..3 carry row 0: the scores of keys 2t, 2t+1 (and + 8), and
+// channels 8i+2t, 8i+2t+1 of the output.  Each warp keeps its own online
+// softmax over the item; the warps join once per item.
+// Shared memory: [q: 64][warp max: 8][warp sum: 8][warp rows: kWarps x 64]
+template <typename WT>
+__device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t4 = lane & 3;
+    const bool row0 = lane < 4;
+    const int H = p.heads, S = op.splits;
+    const int units = cross_units(op);
+    const int items = p.rows * H * S;
+    float* q = reinterpret_cast<float*>(work);
+    float* wmax = q + 64;
+    float* wsum = wmax + 8;
+    float* wrows = wsum + 8;
+    __shared__ int is_last;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int split = item % S, head = (item / S) % H, r = item / (S * H);
+        const int count = cross_item_units(op, item, units);
+        consumer_sync();
+        if (threadIdx.x < 64) q[threadIdx.x] = ld_cg(p.q + (size_t)r * p.width + head * 64 + threadIdx.x) * p.scale;
+        consumer_sync();
+        uint32_t qh[4][2], ql[4][2];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            if (row0) {
+                split_pair<WT>(q[16 * kk + 2 * t4], q[16 * kk + 2 * t4 + 1], qh[kk][0], ql[kk][0]);
+                split_pair<WT>(q[16 * kk + 2 * t4 + 8], q[16 * kk + 2 * t4 + 9], qh[kk][1], ql[kk][1]);
+            } else {
+                qh[kk][0] = qh[kk][1] = ql[kk][0] = ql[kk][1] = 0u;
+            }
+        }
+        float m_w = -INFINITY, l_w = 0.f;
+        float o[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+        // Matrix mi = lane / 8 of an x4 load, row rr = lane % 8 of it.
+        const int mi = lane >> 3, rr = lane & 7;
+        for (int t = 0; t < count; ++t) {
+            const WT* rows = reinterpret_cast<const WT*>(acquire_unit(p, s));
+            const int k0 = (split * op.span + t) * op.chunk;
+            const int n = min(op.chunk, op.key_count - k0);
+            Trace tr = trace_of(p.profile);
+            tr.begin();
+            for (int n0 = 16 * warp; n0 < n; n0 += 16 * kWarps) {
+                float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+                {
+                    // Keys n0 + 8*(mi/2) + rr, key pieces 2kk + mi%2 (rows past
+                    // the unit's keys read its last key; their scores are dropped).
+                    const int key = min(n0 + 8 * (mi >> 1) + rr, n - 1);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        uint32_t b[4];
+                        ldmatrix_x4(b, rows + (size_t)key * 128 + cross_piece(2 * kk + (mi & 1), key) * 8);
+                        const uint32_t ah[4] = {qh[kk][0], 0u, qh[kk][1], 0u};
+                        const uint32_t al[4] = {ql[kk][0], 0u, ql[kk][1], 0u};
+                        const uint32_t b0[2] = {b[0], b[1]}, b1[2] = {b[2], b[3]};
+                        mma_16816<WT>(s0, ah, b0);
+                        mma_16816<WT>(s1, ah, b1);
+                        mma_16816<WT>(s0, al, b0);
+                        mma_16816<WT>(s1, al, b1);
+                    }
+                }
+                // Row 0: keys n0+2t, n0+2t+1 (s0) and n0+8+2t, n0+9+2t (s1).
+                const int ka = n0 + 2 * t4;
+                float v[4];
+                v[0] = row0 && ka < n ? s0[0] : -INFINITY;
+                v[1] = row0 && ka + 1 < n ? s0[1] : -INFINITY;
+                v[2] = row0 && ka + 8 < n ? s1[0] : -INFINITY;
+                v[3] = row0 && ka + 9 < n ? s1[1] : -INFINITY;
+                float gm = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+                gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
+                gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 2));
+                gm = __shfl_sync(0xffffffffu, gm, 0);
+                const float m_new = fmaxf(m_w, gm);
+                const float keep = m_w == -INFINITY ? 0.f : __expf(m_w - m_new);
+                float e[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) e[i] = v[i] == -INFINITY ? 0.f : __expf(v[i] - m_new);
+                float ls = (e[0] + e[1]) + (e[2] + e[3]);
+                ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+                ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+                ls = __shfl_sync(0xffffffffu, ls, 0);
+                l_w = l_w * keep + ls;
+                m_w = m_new;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    o[i][0] *= keep;
+                    o[i][1] *= keep;
+                }
+                uint32_t ph0, pl0, ph2, pl2;
+                split_pair<WT>(e[0], e[1], ph0, pl0);
+                split_pair<WT>(e[2], e[3], ph2, pl2);
+                const uint32_t ah[4] = {row0 ? ph0 : 0u, 0u, row0 ? ph2 : 0u, 0u};
+                const uint32_t al[4] = {row0 ? pl0 : 0u, 0u, row0 ? pl2 : 0u, 0u};
+                {
+                    // Keys n0 + 8*(mi%2) + rr, value pieces 8 + 2cc + mi/2.
+                    const int key = min(n0 + 8 * (mi & 1) + rr, n - 1);
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        uint32_t b[4];
+                        ldmatrix_x4_trans(b, rows + (size_t)key * 128 + cross_piece(8 + 2 * cc + (mi >> 1), key) * 8);
+                        const uint32_t b0[2] = {b[0], b[1]}, b1[2] = {b[2], b[3]};
+                        mma_16816<WT>(o[2 * cc], ah, b0);
+                        mma_16816<WT>(o[2 * cc], al, b0);
+                        mma_16816<WT>(o[2 * cc + 1], ah, b1);
+                        mma_16816<WT>(o[2 * cc + 1], al, b1);
+                    }
+                }
+            }
+            tr.end(kTrAttention);
+            release_unit(s);
+        }
+        // Join the warps' softmaxes.
+        if (lane == 0) {
+            wmax[warp] = m_w;
+            wsum[warp] = l_w;
+        }
+        if (row0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                wrows[warp * 64 + 8 * i + 2 * t4] = o[i][0];
+                wrows[warp * 64 + 8 * i + 2 * t4 + 1] = o[i][1];
+            }
+        }
+        consumer_sync();
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wmax[w]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const float f = wmax[w] == -INFINITY ? 0.f : __expf(wmax[w] - M);
+            L += wsum[w] * f;
+            if (threadIdx.x < 64) O += wrows[w * 64 + threadIdx.x] * f;
+        }
+        if (S == 1) {
+            if (threadIdx.x < 64)
+                static_cast<WT*>(p.attn16)[(size_t)r * p.kpd + head * 64 + threadIdx.x] = Half16<WT>::from_float(
+                    O / L + (op.value_bias ? __ldg(op.value_bias + head * 64 + threadIdx.x) : 0.f));
+            continue;
+        }
+        float* part = p.partial + (((size_t)r * H + head) * S + split) * 66;
+        if (threadIdx.x < 64) part[2 + threadIdx.x] = O;
+        if (threadIdx.x == 0) {
+            part[0] = M;
+            part[1] = L;
+        }
+        __threadfence();
+        consumer_sync();
+        if (threadIdx.x == 0) {
+            unsigned* counter = p.combine_counters + (size_t)r * H + head;
+            is_last = atomicAdd(counter, 1u) == (unsigned)(S - 1);
+            if (is_last) atomicExch(counter, 0u);
+        }
+        consumer_sync();
+        if (is_last && warp == 0) {
+            __threadfence();
+            cross_join<WT>(p, op, r, head);
+        }
+    }
+}
+
+template <typename WT>
+__device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
+    if (p.head_width == 64) cross_attention_mma<WT>(p, op, s, work);
+    else cross_attention_cores<WT>(p, op, s, work);
 }
 
 // -------------------------------------------------------------- the kernel
