@@ -160,3 +160,33 @@ def test_wide_batched_windows_follow_the_oracle():
             _, logits = session.step([int(together[b][k - 1])])
             decided += check_tokens([together[b][k]], logits, later)
     assert decided > windows * steps // 2
+
+
+@pytest.mark.parametrize("storage", ["float16", "bfloat16"])
+def test_tensor_core_products_match_the_oracle(storage):
+    """Thirty-two windows: the products run as tcgen05 tiles (128 weight rows
+    against every window's row, accumulated in tensor memory).  Teacher-forced
+    logits of every window match its own oracle sequence within max-abs 2e-2."""
+    run = S.CONFIGS["tiny_en_b1"]
+    shape = run.shape
+    windows = 32
+    tensors = stored_tensors(S.normal_weights(shape, seed=61), storage)
+    encoders = S.encoder_output(windows, shape.cross_positions, shape.width, seed=62)
+    rng = np.random.default_rng(63)
+    ids = rng.integers(0, 50256, size=(windows, 5)).astype(np.uint32)
+    ids[:, :2] = run.prompt
+    decoder = make_decoder(oracle_shape(shape), tensors, storage, windows=windows)
+    decoder.begin_sequence(encoders)
+    steps = [decoder.step(ids[:, :2])] + [decoder.step(ids[:, k:k + 1]) for k in range(2, 5)]
+    worst = 0.0
+    for b in range(0, windows, 5):
+        session = O.Session(oracle_shape(shape), tensors, threads=THREADS)
+        session.begin(encoders[b])
+        chunks = [list(ids[b, :2])] + [[int(ids[b, k])] for k in range(2, 5)]
+        for result, chunk in zip(steps, chunks):
+            _, logits = session.step([int(t) for t in chunk])
+            err = max_abs(result.logits[b], logits)
+            worst = max(worst, err)
+            assert err <= LOGIT_MAX_ABS, (b, err)
+            check_tokens(result.argmax[b], logits)
+    print(f"  tensor-core products {storage}: logits max-abs {worst:.3g}")

@@ -22,7 +22,7 @@ WSP_FLOAT32 = 0
 WSP_FLOAT16 = 1
 WSP_BFLOAT16 = 2
 
-TRACE_SECTIONS = ("wait", "compute", "release", "epilogue", "norm", "attention", "issue")
+TRACE_SECTIONS = ("wait", "compute", "barrier", "epilogue", "norm", "attention", "ops")
 
 KERNEL_CLASSES = ("embed", "layer_norm", "projection", "self_attention", "cross_attention",
                   "attention_combine", "logits_argmax", "argmax_final", "other")

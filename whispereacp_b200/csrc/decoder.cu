@@ -146,6 +146,7 @@ public:
     Decoder(const wsp_decoder_shape& shape, int device, int windows, Storage storage)
         : shape_(shape), device_(device), windows_(windows), storage_(storage) {
         validate_shape();
+        umma_ = choose_umma();
         CUDA_CHECK(cudaSetDevice(device_));
         CUDA_CHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
         CUDA_CHECK(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, device_));
@@ -236,14 +237,14 @@ public:
             break;
         case 7:
             require_extents(name, extents, rank, {d, d});
-            upload_packed(L.o_w, 0, d, d, kpd, dtype, data);
+            patch16(L.o_w, d, d, dtype, data, [&](int r, int c) { return weight_offset(r, c, kpd); });
             break;
         case 8: require_extents(name, extents, rank, {d}); upload_floats(L.o_b, 0, d, dtype, data); break;
         case 9: require_extents(name, extents, rank, {d}); upload_floats(L.ln2_w, 0, d, dtype, data); break;
         case 10: require_extents(name, extents, rank, {d}); upload_floats(L.ln2_b, 0, d, dtype, data); break;
         case 11:
             require_extents(name, extents, rank, {d, d});
-            patch16(L.qc_w, d, d, dtype, data, [&](int r, int c) { return packed_offset(q_row(r), c, kpd / 32); });
+            patch16(L.qc_w, d, d, dtype, data, [&](int r, int c) { return weight_offset(q_row(r), c, kpd); });
             break;
         case 12:
             require_extents(name, extents, rank, {d});
@@ -257,16 +258,19 @@ public:
         case 15: require_extents(name, extents, rank, {d}); upload_floats(L.vc_b, 0, d, dtype, data); break;
         case 16:
             require_extents(name, extents, rank, {d, d});
-            upload_packed(L.oc_w, 0, d, d, kpd, dtype, data);
+            patch16(L.oc_w, d, d, dtype, data, [&](int r, int c) { return weight_offset(r, c, kpd); });
             break;
         case 17: require_extents(name, extents, rank, {d}); upload_floats(L.oc_b, 0, d, dtype, data); break;
         case 18: require_extents(name, extents, rank, {d}); upload_floats(L.ln3_w, 0, d, dtype, data); break;
         case 19: require_extents(name, extents, rank, {d}); upload_floats(L.ln3_b, 0, d, dtype, data); break;
-        case 20: require_extents(name, extents, rank, {f, d}); upload_packed(L.fc1_w, 0, f, d, kpd, dtype, data); break;
+        case 20:
+            require_extents(name, extents, rank, {f, d});
+            patch16(L.fc1_w, f, d, dtype, data, [&](int r, int c) { return weight_offset(r, c, kpd); });
+            break;
         case 21: require_extents(name, extents, rank, {f}); upload_floats(L.fc1_b, 0, f, dtype, data); break;
         case 22:
             require_extents(name, extents, rank, {d, f});
-            upload_packed(L.fc2_w, 0, d, f, kpf, dtype, data);
+            patch16(L.fc2_w, d, f, dtype, data, [&](int r, int c) { return weight_offset(r, c, kpf); });
             break;
         case 23: require_extents(name, extents, rank, {d}); upload_floats(L.fc2_b, 0, d, dtype, data); break;
         }
@@ -613,6 +617,24 @@ private:
 
     static size_t round16(size_t n) { return (n + 15) / 16 * 16; }
 
+    // Tensor-core products (tcgen05) for batches of many windows: from this
+    // many windows, with widths and heads the umma layouts cover.
+    static constexpr int kUmmaWindows = 32;
+    bool choose_umma() const {
+        return windows_ >= kUmmaWindows && shape_.width % 64 == 0 && shape_.feed_forward_width % 64 == 0 &&
+               head_width() == 64;
+    }
+    // Rows a product weight matrix is allocated with: whole 16-row tiles, or
+    // whole 128-row tiles for the tensor-core products.
+    size_t weight_rows(size_t n) const { return umma_ ? (n + 127) / 128 * 128 : round16(n); }
+    // Element offset of (row n, column k) of a product weight with inner size kp.
+    size_t weight_offset(int n, int k, int kp) const {
+        return umma_ ? umma_offset(n, k, kp / 64) : packed_offset(n, k, kp / 32);
+    }
+    // Rows of an activation buffer: whole 16-row groups (a tensor-core item's
+    // rows round up to 16) of every row a step can hold.
+    int act_rows() const { return (windows_ * token_capacity_ + 15) / 16 * 16; }
+
     int head_width() const { return shape_.width / shape_.heads; }
     // Packed row of the q (0), k (1) or v (2) row i of a head-grouped q/k/v
     // matrix: head h owns rows [h*G, h*G + 3D), G = 3D rounded to a tile.
@@ -639,14 +661,15 @@ private:
         for (size_t i = 0; i < L; ++i) {
             LayerBuffers& l = layers_[i];
             l.ln1_w.allocate(d * 4); l.ln1_b.allocate(d * 4);
-            l.qkv_w.allocate(H * round16(3 * D) * kpd * 2); l.qkv_b.allocate(H * round16(3 * D) * 4);
-            l.o_w.allocate(round16(d) * kpd * 2); l.o_b.allocate(d * 4);
+            l.qkv_w.allocate(weight_rows(H * round16(3 * D)) * kpd * 2); l.qkv_b.allocate(H * round16(3 * D) * 4);
+            l.o_w.allocate(weight_rows(d) * kpd * 2); l.o_b.allocate(d * 4);
             l.ln2_w.allocate(d * 4); l.ln2_b.allocate(d * 4);
-            l.qc_w.allocate(H * round16(D) * kpd * 2); l.qc_b.allocate(H * round16(D) * 4); l.vc_b.allocate(d * 4);
-            l.oc_w.allocate(round16(d) * kpd * 2); l.oc_b.allocate(d * 4);
+            l.qc_w.allocate(weight_rows(H * round16(D)) * kpd * 2); l.qc_b.allocate(H * round16(D) * 4);
+            l.vc_b.allocate(d * 4);
+            l.oc_w.allocate(weight_rows(d) * kpd * 2); l.oc_b.allocate(d * 4);
             l.ln3_w.allocate(d * 4); l.ln3_b.allocate(d * 4);
-            l.fc1_w.allocate(round16(f) * kpd * 2); l.fc1_b.allocate(f * 4);
-            l.fc2_w.allocate(round16(d) * kpf * 2); l.fc2_b.allocate(d * 4);
+            l.fc1_w.allocate(weight_rows(f) * kpd * 2); l.fc1_b.allocate(f * 4);
+            l.fc2_w.allocate(weight_rows(d) * kpf * 2); l.fc2_b.allocate(d * 4);
         }
         present_.assign(4 + 24 * L, false);
     }
@@ -676,9 +699,10 @@ private:
         const size_t d = shape_.width, f = shape_.feed_forward_width, H = shape_.heads, D = d / H;
         hidden_.allocate(R * d * 4);
         queries_.allocate(R * d * 4);
-        normalised_.allocate(R * padded(d) * 2);
-        attended_.allocate(R * padded(d) * 2);
-        feed_forward_.allocate(R * padded(f) * 2);
+        const size_t A = (R + 15) / 16 * 16;
+        normalised_.allocate(A * padded(d) * 2);
+        attended_.allocate(A * padded(d) * 2);
+        feed_forward_.allocate(A * padded(f) * 2);
         partial_.allocate(R * H * kMaxCrossSplits * (D + 2) * 4);
         const size_t grid = (size_t)kMaxBlocksPerSm * sm_count_;
         candidate_values_.allocate(R * grid * 4);
@@ -698,8 +722,8 @@ private:
             CUDA_CHECK(cudaMemset(state_.get<int>() + kError, 0, sizeof(int)));
             if (state[kError] & kErrBarrierTimeout) {
                 static const char* const kinds[] = {"?", "a grid barrier", "a weight unit", "a free stage",
-                                                    "a landing copy", "an armed stage"};
-                const int kind = state[kFailKind] >= 1 && state[kFailKind] <= 5 ? state[kFailKind] : 0;
+                                                    "a landing copy", "an armed stage", "an op to start"};
+                const int kind = state[kFailKind] >= 1 && state[kFailKind] <= 6 ? state[kFailKind] : 0;
                 CUDA_CHECK(cudaMemset(state_.get<int>() + kFailKind, 0, 3 * sizeof(int)));
                 throw CudaFailure(std::string("the decode kernel gave up waiting for ") + kinds[kind] + " (CTA " +
                                       std::to_string(state[kFailCta]) + ", index " +
@@ -718,6 +742,7 @@ private:
         case kOpCrossAttention: return WSP_KERNEL_CROSS_ATTENTION;
         case kOpLogits: return WSP_KERNEL_LOGITS_ARGMAX;
         case kOpNorm: return WSP_KERNEL_LAYER_NORM;
+        case kOpReduce: return WSP_KERNEL_PROJECTION;
         }
         return WSP_KERNEL_OTHER;
     }
@@ -752,6 +777,7 @@ private:
         norm.norm_rows = R;
         norm.norm_step = 1;
         norm.norm_offset = 0;
+        norm.norm_umma = umma_ ? 1 : 0;
         ops.push_back(norm);
         product.input16 = normalised_.get();
         product.ld_input = padded(shape_.width);
@@ -891,6 +917,37 @@ private:
         return best;
     }
 
+    // Tensor-core products: split each one's inner size so that its items --
+    // (128-row weight tile, row group, split) -- cover the grid, every split
+    // at least one k-block; a split product is followed by the reduce op
+    // that joins its partials.  Returns the partials' size in bytes.
+    size_t split_products(std::vector<StepOp>& ops, const StepParams& p, int grid) const {
+        std::vector<StepOp> out;
+        size_t partial_bytes = 0;
+        const int groups = (p.rows + p.umma_rows - 1) / p.umma_rows;
+        for (StepOp op : ops) {
+            if (op.kind != kOpProduct || !p.umma) {
+                out.push_back(op);
+                continue;
+            }
+            const int m_tiles = (op.n + 127) / 128, kblocks = op.kp / 64;
+            const int base = m_tiles * groups;
+            int ks = std::max(1, std::min(kblocks, (grid + base / 2) / base));
+            const int per = (kblocks + ks - 1) / ks;
+            ks = (kblocks + per - 1) / per;
+            op.ksplit = ks;
+            out.push_back(op);
+            if (ks > 1) {
+                StepOp reduce = op;
+                reduce.kind = kOpReduce;
+                out.push_back(reduce);
+                partial_bytes = std::max(partial_bytes, (size_t)ks * m_tiles * 128 * groups * p.umma_rows * 4);
+            }
+        }
+        ops.swap(out);
+        return partial_bytes;
+    }
+
     // The weight-stream schedule of every CTA (schedule.h), into device memory.
     void upload_schedule(StepParams& p, const std::vector<StepOp>& ops, int grid) {
         build_schedule(p, ops, grid, decode_tile_rows(p), schedule_host_, offsets_host_);
@@ -918,6 +975,9 @@ private:
         };
         add(token_table_);
         add(cross_kv_);
+        add(normalised_);
+        add(attended_);
+        add(feed_forward_);
         for (int l = 0; l < shape_.layers; ++l) {
             const LayerBuffers& W = layers_[l];
             add(W.qkv_w); add(W.o_w); add(W.qc_w); add(W.oc_w); add(W.fc1_w); add(W.fc2_w);
@@ -926,10 +986,11 @@ private:
         for (size_t i = 0; i < schedule_host_.size(); ++i) {
             const ScheduleEntry& e = schedule_host_[i];
             if (e.source == 0 && e.bytes == 0) continue;  // the placeholder of an empty schedule
-            const size_t lo = (size_t)e.source, hi = lo + (size_t)e.bytes;
+            const size_t bytes = (size_t)(e.bytes & 0xFFFFFFFFull);
+            const size_t lo = (size_t)e.source, hi = lo + bytes;
             auto it = std::upper_bound(ranges.begin(), ranges.end(), std::make_pair(lo, (size_t)-1));
             const bool inside = it != ranges.begin() && lo >= std::prev(it)->first && hi <= std::prev(it)->second;
-            if (!inside || lo % 16 != 0 || e.bytes % 16 != 0 || e.bytes == 0 || e.bytes > (size_t)stage_bytes)
+            if (!inside || lo % 16 != 0 || bytes % 16 != 0 || bytes == 0 || bytes > (size_t)stage_bytes)
                 throw LogicError("weight-stream unit " + std::to_string(i) + " lies outside the weights");
         }
     }
@@ -958,6 +1019,8 @@ private:
         p.ffn = shape_.feed_forward_width;
         p.vocabulary = shape_.vocabulary_size;
         p.kpd = padded(shape_.width);
+        p.umma = umma_ ? 1 : 0;
+        p.act_rows = act_rows();
         p.max_positions = shape_.max_positions;
         p.ring_stride = ring_stride();
         p.scale = 1.f / std::sqrt((float)p.head_width);
@@ -1004,12 +1067,18 @@ private:
         p.profile = profile;
         const bool half = storage_ == Storage::f16;
         configure_stream(half, p);
+        // A tensor-core item's rows: as many as a stage holds (128 bytes a
+        // row), at most 256, a multiple of 16.
+        p.umma_rows = std::min(256, p.stage_bytes / 128 / 16 * 16);
         const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk);
         if (blocks <= 0) throw CudaFailure("the decode kernel does not fit on an SM", false);
         const int grid = sm_count_ * std::min(blocks, kMaxBlocksPerSm);
         std::vector<StepOp>& ops = sample ? (T == 1 ? ops_step_ : ops_prompt_) : ops_teacher_;
         DeviceBuffer& ops_dev = sample ? (T == 1 ? ops_step_dev_ : ops_prompt_dev_) : ops_teacher_dev_;
         ops = build_ops(R, grid, p.stage_bytes, p);
+        const size_t partial_bytes = split_products(ops, p, grid);
+        if (partial_d_.bytes() < partial_bytes) partial_d_.allocate(partial_bytes);
+        p.partial_d = partial_d_.get<float>();
         if (ops_dev.bytes() < ops.size() * sizeof(StepOp)) ops_dev.allocate(ops.size() * sizeof(StepOp));
         CUDA_CHECK(cudaMemcpyAsync(ops_dev.get(), ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice,
                                    stream_));
@@ -1076,7 +1145,8 @@ private:
     // q_proj (0), k_proj (1) or v_proj (2) into the head-grouped q/k/v matrix.
     void patch_qkv(DeviceBuffer& dst, int which, wsp_dtype dtype, const void* data) {
         const int d = shape_.width, chunks = padded(d) / 32;
-        patch16(dst, d, d, dtype, data, [&](int r, int c) { return packed_offset(qkv_row(which, r), c, chunks); });
+        (void)chunks;
+        patch16(dst, d, d, dtype, data, [&](int r, int c) { return weight_offset(qkv_row(which, r), c, padded(d)); });
     }
 
     void upload_floats(DeviceBuffer& dst, size_t offset, size_t count, wsp_dtype dtype, const void* data) {
@@ -1085,8 +1155,6 @@ private:
         CUDA_CHECK(cudaMemcpy(dst.get<float>() + offset, v.data(), count * 4, cudaMemcpyHostToDevice));
     }
 
-    // rows x cols of a row-major [rows, cols] tensor into dst rows
-    // [row_offset, row_offset+rows) of pitch ld, narrowed to the storage type.
     // Cross k_proj (kv 0) or v_proj (kv 1) of a layer into the projection
     // that writes the cross caches: per layer and head, the head's D key rows
     // then its D value rows, [L][H][2D][d], so the product of a window's
@@ -1143,7 +1211,7 @@ private:
 
     DeviceBuffer self_keys_, self_values_, cross_kv_, encoder_staging_, encoder16_;
     DeviceBuffer ring_, ring_prompt_, state_, masks_;
-    DeviceBuffer hidden_, queries_, normalised_, attended_, feed_forward_, partial_;
+    DeviceBuffer hidden_, queries_, normalised_, attended_, feed_forward_, partial_, partial_d_;
     DeviceBuffer candidate_values_, candidate_indices_, row_tokens_, counters_;
     DeviceBuffer barrier_, ended_, profile_;
     DeviceBuffer logits_staging_, hidden_staging_;
@@ -1154,6 +1222,7 @@ private:
     std::vector<StepOp> ops_prompt_, ops_step_, ops_teacher_;
 
     int token_capacity_ = 0;
+    bool umma_ = false;
     int active_cross_ = 0;
     int position_ = 0;
     bool started_ = false;

@@ -89,6 +89,31 @@ inline void append_cross_units(const StepParams& p, const StepOp& op, int cta, i
     }
 }
 
+// Tensor-core product: item (m tile of 128 weight rows, group of umma_rows
+// rows), CTA c taking items c, c + grid, ...; per k-block of 64 columns, the
+// weight block (16 KB) then the rows' activation block (rows rounded to 16,
+// 128 bytes each), as product_umma reads them.
+inline int umma_items(const StepParams& p, const StepOp& op) {
+    return ((op.n + 127) / 128) * ((p.rows + p.umma_rows - 1) / p.umma_rows) * (op.ksplit > 1 ? op.ksplit : 1);
+}
+inline void append_umma_units(const StepParams& p, const StepOp& op, int op_index, int cta, int grid,
+                              std::vector<ScheduleEntry>& out) {
+    const int kblocks = op.kp / 64;
+    for (int item = cta; item < umma_items(p, op); item += grid) {
+        const UmmaItem u = umma_item(p, op, item);
+        const int m = u.m, r0 = u.r0;
+        const unsigned n16 = (unsigned)(u.rows + 15) / 16 * 16;
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
+            out.push_back(schedule_entry(static_cast<const unsigned char*>(op.weight) + ((size_t)m * kblocks + kb) * 16384,
+                                         16384u));
+            // The rows the ops before this one wrote: gated on this op's start.
+            out.push_back(schedule_entry(static_cast<const unsigned char*>(op.input16) +
+                                             ((size_t)kb * p.act_rows + r0) * 128,
+                                         n16 * 128u, (unsigned)op_index + 1));
+        }
+    }
+}
+
 // The per-CTA schedules of a launch, concatenated, and their offsets.
 inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, int grid, int rt,
                            std::vector<ScheduleEntry>& units, std::vector<unsigned>& offsets) {
@@ -96,9 +121,14 @@ inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, 
     units.clear();
     offsets.assign(1, 0u);
     for (int cta = 0; cta < grid; ++cta) {
-        for (const StepOp& op : ops) {
+        for (size_t op_index = 0; op_index < ops.size(); ++op_index) {
+            const StepOp& op = ops[op_index];
             if (op.kind == kOpCrossAttention) {
                 append_cross_units(p, op, cta, grid, units);
+                continue;
+            }
+            if (op.kind == kOpProduct && p.umma) {
+                append_umma_units(p, op, (int)op_index, cta, grid, units);
                 continue;
             }
             const int items = op_items(p, op, rt);

@@ -12,6 +12,8 @@
 // Data written by one CTA and read by another inside the launch is read with
 // ld.global.cg (L2, never a stale L1 line); the grid barrier orders it.
 #include "step.cuh"
+
+#include <type_traits>
 #include "step_launch.h"
 
 #include <algorithm>
@@ -76,6 +78,12 @@ __device__ __forceinline__ float consumer_max(float v, float* scratch) {
 }
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+// Element (row r, column c) of a 16-bit activation matrix with row pitch ld:
+// row-major, or the tensor-core block layout (act_offset) when p.umma.
+__device__ __forceinline__ size_t act_index(const StepParams& p, int r, int c, int ld) {
+    return p.umma ? act_offset(r, c, p.act_rows) : (size_t)r * ld + c;
+}
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
@@ -90,7 +98,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // Section timers for measurement: CTA 0, thread 0 accumulates clock64
 // cycles per section of a launch into profile[kTraceBase + section] when a
 // profile buffer is given.
-enum TraceSection : int { kTrWait = 0, kTrCompute, kTrRelease, kTrEpilogue, kTrNorm, kTrAttention, kTrIssue,
+enum TraceSection : int { kTrWait = 0, kTrCompute, kTrBarrier, kTrEpilogue, kTrNorm, kTrAttention, kTrOther,
                           kTrSections };
 constexpr int kTraceBase = 512;
 __shared__ unsigned long long trace_cycles[kTrSections];
@@ -177,6 +185,7 @@ __device__ __forceinline__ uint32_t smem_address(const void* p) {
 
 struct Stream {
     unsigned char* ring;          // stages x stage_bytes
+    volatile unsigned* op_clock;  // the op the consumers have entered: step * n_ops + op
     uint64_t* full;               // per stage: the unit landed (tx bytes)
     uint64_t* empty;              // per stage: the 8 consumer warps released it
     int stages;
@@ -204,8 +213,12 @@ __device__ bool wait_parity(const StepParams& p, uint64_t* bar, uint32_t parity,
                             unsigned long long index) {
     if (try_parity(bar, parity)) return true;
     const unsigned long long start = global_ns();
-    while (!try_parity(bar, parity)) {
+    for (unsigned spin = 1; !try_parity(bar, parity); ++spin) {
         if (stop && *stop) return false;
+        if ((spin & 15) != 0) continue;
+        // Another wait gave up: this one will not be answered either.  (The
+        // producer's final drain still waits for its copies in flight.)
+        if (kind != kWaitDrain && ld_volatile(p.state + kAbort)) return false;
         if (global_ns() - start > kWaitTimeoutNs) {
             record_timeout(p.state, kind, (long long)index);
             return false;
@@ -285,6 +298,31 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
                 break;
             }
             const ulonglong2 e = __ldg(schedule + i);
+            const unsigned gate = (unsigned)(e.y >> 32);
+            if (gate != 0) {
+                // Activations an earlier op wrote: wait until the consumers
+                // have entered the unit's op (its grid barrier passed), then
+                // order those generic writes before this bulk (async) read.
+                const unsigned target = (unsigned)step * (unsigned)p.n_ops + gate - 1;
+                if (*s.op_clock < target) {
+                    const unsigned long long start = global_ns();
+                    for (unsigned spin = 1; *s.op_clock < target; ++spin) {
+                        if (*stop) break;
+                        if ((spin & 15) != 0) continue;
+                        if (ld_volatile(p.state + kAbort)) break;
+                        if (global_ns() - start > kWaitTimeoutNs) {
+                            record_timeout(p.state, kWaitGate, (long long)target);
+                            break;
+                        }
+                    }
+                    if (*s.op_clock < target) {
+                        go = false;
+                        break;
+                    }
+                }
+                __threadfence_block();
+                asm volatile("fence.proxy.async.global;\n" ::: "memory");
+            }
             const uint32_t bar = smem_address(s.full + stage);
             const uint32_t dst = smem_address(s.ring + (size_t)stage * s.stage_bytes);
             const unsigned bytes = (unsigned)e.y;
@@ -438,12 +476,21 @@ __device__ void stage_rows(const WT* X, int ld, int r0, int rows, int kp, WT* xs
 // LayerNorm of op.norm_rows rows into 16-bit rows, a row per CTA at a time
 // with the whole CTA on it.
 template <typename WT>
-__device__ void op_norm(const StepParams& p, const StepOp& op) {
+__device__ void op_norm(const StepParams& p, const StepOp& op, unsigned char* work) {
     WT* out = static_cast<WT*>(op.out);
+    WT* row16 = reinterpret_cast<WT*>(work);  // the block layout: a row first, then its pieces
     for (int row = blockIdx.x; row < op.norm_rows; row += gridDim.x) {
         consumer_sync();
-        layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, row, 1, op.norm_step, op.norm_offset,
-                            out + (size_t)row * op.ld_out, op.ld_out, op.norm_hidden);
+        if (!op.norm_umma) {
+            layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, row, 1, op.norm_step, op.norm_offset,
+                                out + (size_t)row * op.ld_out, op.ld_out, op.norm_hidden);
+            continue;
+        }
+        layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, row, 1, op.norm_step, op.norm_offset, row16, op.ld_out,
+                            op.norm_hidden);
+        consumer_sync();
+        for (int c = 8 * threadIdx.x; c < op.ld_out; c += 8 * kThreads)
+            *reinterpret_cast<uint4*>(out + act_offset(row, c, p.act_rows)) = *reinterpret_cast<const uint4*>(row16 + c);
     }
 }
 
@@ -598,6 +645,50 @@ __device__ __forceinline__ float product_sum(const float* red, int RT, int nl, i
     return v;
 }
 
+// One output of a product, v = the row of x times weight row n plus the
+// bias, written the way op.epilogue says (row r, at position + t of its
+// window for the self caches).
+template <typename WT>
+__device__ __forceinline__ void emit_output(const StepParams& p, const StepOp& op, int position, int n, int r, float v) {
+    switch (op.epilogue) {
+    case kEpStore: {
+        // Rows grouped by head, each head's rows padded to a whole tile.
+        int col = n;
+        if (op.slice > 0) {
+            const int within = n % round16(op.slice);
+            if (within >= op.slice) return;
+            col = (n / round16(op.slice)) * op.slice + within;
+        }
+        static_cast<float*>(op.out)[(size_t)r * op.ld_out + col] = v;
+        return;
+    }
+    case kEpResidual:
+        // The one writer of this element in the op: a reduction
+        // adds exactly what a read-add-write would, without waiting.
+        atomicAdd(static_cast<float*>(op.out) + (size_t)r * op.ld_out + n, v);
+        return;
+    case kEpGelu:
+        static_cast<WT*>(op.out)[act_index(p, r, n, op.ld_out)] = Half16<WT>::from_float(gelu_exact(v));
+        return;
+    case kEpQkv: {
+        // Head h's rows: its q, k and v rows, padded to a whole tile.
+        const int D = p.head_width, group = round16(3 * D);
+        const int within = n % group;
+        if (within >= 3 * D) return;
+        const int col = (n / group) * D + within % D;
+        const int which = within / D;
+        if (which == 0) {
+            static_cast<float*>(op.out)[(size_t)r * op.ld_out + col] = v;
+        } else {
+            const int b = r / p.tokens, t = r % p.tokens;
+            WT* cache = static_cast<WT*>(which == 1 ? op.self_keys : op.self_values);
+            cache[((size_t)b * p.max_positions + position + t) * p.width + col] = Half16<WT>::from_float(v);
+        }
+        return;
+    }
+    }
+}
+
 // Work area of a product: [xs: RT x pitch 16-bit][red: 8 x 16 x RT][tile: 16 x RT]
 //                         [best values: out_rows][best indices: out_rows]
 template <typename WT, int NT>
@@ -638,6 +729,8 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
             ok = product_tile<WT, NT, false>(p, s, op.kp, X, op.ld_input, rows_valid, acc);
         }
         if (!ok) return;
+        Trace tre = trace_of(p.profile);
+        tre.begin();
         product_reduce<NT>(red, acc);
         for (int o = threadIdx.x; o < 16 * RT; o += kThreads) {
             const int nl = o / RT, rl = o % RT;
@@ -645,45 +738,157 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
             if (n >= op.n || rl >= rows_valid) continue;
             float v = product_sum(red, RT, nl, rl);
             if (op.bias) v += op.bias[n];
-            switch (op.epilogue) {
-            case kEpStore: {
-                // Rows grouped by head, each head's rows padded to a whole tile.
-                int col = n;
-                if (op.slice > 0) {
-                    const int within = n % round16(op.slice);
-                    if (within >= op.slice) break;
-                    col = (n / round16(op.slice)) * op.slice + within;
-                }
-                static_cast<float*>(op.out)[(size_t)r * op.ld_out + col] = v;
-                break;
-            }
-            case kEpResidual: {
-                float* at = static_cast<float*>(op.out) + (size_t)r * op.ld_out + n;
-                *at = ld_cg(at) + v;
-                break;
-            }
-            case kEpGelu:
-                static_cast<WT*>(op.out)[(size_t)r * op.ld_out + n] = Half16<WT>::from_float(gelu_exact(v));
-                break;
-            case kEpQkv: {
-                // Head h's rows: its q, k and v rows, padded to a whole tile.
-                const int D = p.head_width, group = round16(3 * D);
-                const int within = n % group;
-                if (within >= 3 * D) break;
-                const int col = (n / group) * D + within % D;
-                const int which = within / D;
-                if (which == 0) {
-                    static_cast<float*>(op.out)[(size_t)r * op.ld_out + col] = v;
-                } else {
-                    const int b = r / p.tokens, t = r % p.tokens;
-                    WT* cache = static_cast<WT*>(which == 1 ? op.self_keys : op.self_values);
-                    cache[((size_t)b * p.max_positions + position + t) * p.width + col] = Half16<WT>::from_float(v);
-                }
-                break;
-            }
-            }
+            emit_output<WT>(p, op, position, n, r, v);
         }
         consumer_sync();
+        tre.end(kTrEpilogue);
+    }
+}
+
+// ------------------------------------------------------- tcgen05 products
+
+// With many rows a product runs on the 5th-generation tensor cores: item
+// (128 weight rows, up to umma_rows rows) accumulates D[128 x N] in tensor
+// memory over the k-blocks of its weight tile and of the rows' activations,
+// both streamed through the ring in the 128-byte-swizzled K-major layout
+// (umma_offset / act_offset).  Lane 0 of warp kIssueWarp issues tcgen05.mma
+// (M = 128, N = the rows rounded to 16, K = 16 per instruction, four per
+// k-block); warps 0..3, whole warps since tcgen05.ld is warp-collective,
+// read D back (lane = weight row) for the epilogue.
+struct TensorMemory {
+    uint32_t base;    // allocated columns (kTmemColumns), lanes 0..127
+    uint64_t* done;   // the item's products completed (tcgen05.commit)
+    uint32_t phase;
+};
+constexpr uint32_t kTmemColumns = 256;
+constexpr int kIssueWarp = 4;  // not one of the epilogue warps 0..3
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (version 1 for sm_100).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t address) {
+    return (uint64_t)((address >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor of kind::f16: fp32 accumulation, both operands
+// 16-bit (f16 or bf16 alike) and K-major, M = 128, N = n.
+template <typename WT>
+__device__ __forceinline__ uint32_t umma_idesc(int n) {
+    const uint32_t ab = std::is_same<WT, __nv_bfloat16>::value ? 1u : 0u;
+    return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+__device__ __forceinline__ void umma_mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+// The mbarrier receives one arrival once every product this thread issued
+// so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_address(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void stage_arrive(const Stream& s, unsigned long long index, unsigned count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_address(s.empty + index % s.stages)),
+                 "r"(count)
+                 : "memory");
+}
+// 32 columns of this warp's 32 lanes; the load and its wait are one asm
+// statement, so no use of the registers can be scheduled before the wait.
+__device__ __forceinline__ void tmem_load32(uint32_t address, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(address)
+        : "memory");
+}
+
+template <typename WT>
+__device__ void product_umma(const StepParams& p, const StepOp& op, int position, Stream& s, TensorMemory& tm) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m_tiles = (op.n + 127) / 128, groups = (p.rows + p.umma_rows - 1) / p.umma_rows;
+    const int ks = op.ksplit > 1 ? op.ksplit : 1;
+    const int items = m_tiles * groups * ks;
+    const int row_stride = groups * p.umma_rows;  // of the partials
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const UmmaItem u = umma_item(p, op, item);
+        const int m = u.m, r0 = u.r0, rows = u.rows;
+        const int kblocks = u.kb1 - u.kb0;
+        const int n16 = (rows + 15) & ~15;
+        if (threadIdx.x == 32 * kIssueWarp) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t idesc = umma_idesc<WT>(n16);
+            for (int kb = 0; kb < kblocks; ++kb) {
+                const unsigned long long iw = s.next + 2 * (unsigned long long)kb, ix = iw + 1;
+                const uint32_t w = smem_address(unit_at(p, s, iw));
+                const uint32_t x = smem_address(unit_at(p, s, ix));
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    umma_mma(tm.base, umma_desc(w + 32 * kk), umma_desc(x + 32 * kk), idesc, (kb | kk) != 0);
+                // A stage is free after kWarps arrivals: kWarps - 1 now, the
+                // last once the products above have read it.
+                stage_arrive(s, iw, kWarps - 1);
+                umma_commit(s.empty + iw % s.stages);
+                stage_arrive(s, ix, kWarps - 1);
+                umma_commit(s.empty + ix % s.stages);
+            }
+            umma_commit(tm.done);
+        }
+        s.next += 2 * (unsigned long long)kblocks;
+        float* partial = ks > 1 ? p.partial_d + (size_t)u.split * m_tiles * 128 * row_stride : nullptr;
+        if (warp < 4) {
+            Trace tr = trace_of(p.profile);
+            tr.begin();
+            wait_parity(p, tm.done, tm.phase, nullptr, kWaitUnit, (unsigned long long)item);
+            __syncwarp();
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int n = m * 128 + 32 * warp + lane;
+            const float bias = op.bias && n < op.n ? __ldg(op.bias + n) : 0.f;
+            for (int c0 = 0; c0 < n16; c0 += 32) {
+                uint32_t v[32];
+                tmem_load32(tm.base + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+                if (partial) {
+                    // This split's sums over its k-blocks; the reduce op adds
+                    // the splits, the bias and the epilogue.
+                    float* row = partial + (size_t)n * row_stride + r0 + c0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (c0 + j < rows) row[j] = __uint_as_float(v[j]);
+                } else if (n < op.n) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (c0 + j < rows) emit_output<WT>(p, op, position, n, r0 + c0 + j, __uint_as_float(v[j]) + bias);
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            tr.end(kTrEpilogue);
+        }
+        tm.phase ^= 1u;
+        consumer_sync();
+    }
+}
+
+// The splits of a tensor-core product summed in split order, the bias added
+// and the epilogue applied: element (n, r) per thread, row-contiguous reads.
+template <typename WT>
+__device__ void op_reduce(const StepParams& p, const StepOp& op, int position) {
+    const int m_tiles = (op.n + 127) / 128, groups = (p.rows + p.umma_rows - 1) / p.umma_rows;
+    const int row_stride = groups * p.umma_rows;
+    const size_t split_stride = (size_t)m_tiles * 128 * row_stride;
+    const long long total = (long long)op.n * p.rows;
+    for (long long e = (long long)blockIdx.x * kThreads + threadIdx.x; e < total; e += (long long)gridDim.x * kThreads) {
+        const int n = (int)(e / p.rows), r = (int)(e % p.rows);
+        const float* at = p.partial_d + (size_t)n * row_stride + r;
+        float v = op.bias ? __ldg(op.bias + n) : 0.f;
+        float sum = 0.f;
+#pragma unroll 8
+        for (int sp = 0; sp < op.ksplit; ++sp) sum += ld_cg(at + sp * split_stride);
+        emit_output<WT>(p, op, position, n, r, sum + v);
     }
 }
 
@@ -1022,8 +1227,9 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
         }
         const float l = consumer_sum(local, scratch);
         attention_values<WT, false>(scores, V, op.key_stride, D, 0, keys, fold, result);
-        WT* out = static_cast<WT*>(p.attn16) + (size_t)r * p.kpd + head * D;
-        for (int c = threadIdx.x; c < D; c += kThreads) out[c] = Half16<WT>::from_float(result[c] / l);
+        WT* out = static_cast<WT*>(p.attn16);
+        for (int c = threadIdx.x; c < D; c += kThreads)
+            out[act_index(p, r, head * D + c, p.kpd)] = Half16<WT>::from_float(result[c] / l);
     }
 }
 
@@ -1122,9 +1328,13 @@ __device__ void cross_join(const StepParams& p, const StepOp& op, int r, int hea
         if (c0 < D) o[0] += ld_cg(ps + c0) * f;
         if (c1 < D) o[1] += ld_cg(ps + c1) * f;
     }
-    WT* out = static_cast<WT*>(p.attn16) + (size_t)r * p.kpd + head * D;
-    if (c0 < D) out[c0] = Half16<WT>::from_float(o[0] / l + (op.value_bias ? __ldg(op.value_bias + head * D + c0) : 0.f));
-    if (c1 < D) out[c1] = Half16<WT>::from_float(o[1] / l + (op.value_bias ? __ldg(op.value_bias + head * D + c1) : 0.f));
+    WT* out = static_cast<WT*>(p.attn16);
+    if (c0 < D)
+        out[act_index(p, r, head * D + c0, p.kpd)] =
+            Half16<WT>::from_float(o[0] / l + (op.value_bias ? __ldg(op.value_bias + head * D + c0) : 0.f));
+    if (c1 < D)
+        out[act_index(p, r, head * D + c1, p.kpd)] =
+            Half16<WT>::from_float(o[1] / l + (op.value_bias ? __ldg(op.value_bias + head * D + c1) : 0.f));
 }
 
 // Shared memory: [q: 64][max: 2 x 8][sum: 2 x 8][fold: 2 x kWarps x 64][scores: kMaxCrossUnitKeys]
@@ -1185,7 +1395,7 @@ __device__ void cross_attention_cores(const StepParams& p, const StepOp& op, Str
         }
         if (S == 1) {
             if (threadIdx.x < D)
-                static_cast<WT*>(p.attn16)[(size_t)r * p.kpd + head * D + threadIdx.x] = Half16<WT>::from_float(
+                static_cast<WT*>(p.attn16)[act_index(p, r, head * D + threadIdx.x, p.kpd)] = Half16<WT>::from_float(
                     o_run / l_run + (op.value_bias ? __ldg(op.value_bias + head * D + threadIdx.x) : 0.f));
             continue;
         }
@@ -1369,7 +1579,7 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
         }
         if (S == 1) {
             if (threadIdx.x < 64)
-                static_cast<WT*>(p.attn16)[(size_t)r * p.kpd + head * 64 + threadIdx.x] = Half16<WT>::from_float(
+                static_cast<WT*>(p.attn16)[act_index(p, r, head * 64 + threadIdx.x, p.kpd)] = Half16<WT>::from_float(
                     O / L + (op.value_bias ? __ldg(op.value_bias + head * 64 + threadIdx.x) : 0.f));
             continue;
         }
@@ -1404,11 +1614,28 @@ __device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream
 
 constexpr int kMaxStages = 8;
 
+// Consumers leave together; warp 0 frees the tensor memory (every product
+// that wrote it has completed: each item waited for its commit).
+__device__ __forceinline__ void release_tensor_memory(const StepParams& p, const TensorMemory& tm) {
+    if (!p.umma) return;
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    consumer_sync();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (threadIdx.x < 32)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm.base), "r"(kTmemColumns));
+}
+
 template <typename WT, int NT>
 __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) {
-    extern __shared__ __align__(128) unsigned char smem[];
+    extern __shared__ __align__(1024) unsigned char dynamic_smem[];
     __shared__ int stop_flag;
     __shared__ unsigned long long armed_units;
+    __shared__ unsigned op_clock;
+    __shared__ uint32_t tmem_slot;
+    __shared__ __align__(8) uint64_t tmem_done;
+    // The ring starts on a 1024-byte boundary (the 128-byte swizzle's period).
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(dynamic_smem) + 1023) & ~static_cast<uintptr_t>(1023));
     Stream s;
     s.stages = p.stages;
     s.stage_bytes = p.stage_bytes;
@@ -1418,18 +1645,30 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
     unsigned char* work = smem + (size_t)s.stages * s.stage_bytes + 16 * kMaxStages;
     s.next = 0;
     s.armed = &armed_units;
+    s.op_clock = &op_clock;
     if (threadIdx.x == 0) {
         stop_flag = 0;
         armed_units = 0;
+        op_clock = 0;
         for (int i = 0; i < kTrSections; ++i) trace_cycles[i] = 0;
         for (int i = 0; i < s.stages; ++i) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(s.full + i)) : "memory");
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_address(s.empty + i)), "r"(kWarps)
                          : "memory");
         }
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(&tmem_done)) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
+    if (p.umma && threadIdx.x < 32) {
+        __syncwarp();  // tcgen05.alloc is warp-collective; lane 0 has just set up the barriers
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_address(&tmem_slot)),
+                     "r"(kTmemColumns));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    TensorMemory tm{p.umma ? tmem_slot : 0u, &tmem_done, 0u};
     volatile int* stop = &stop_flag;
     if (threadIdx.x >= kConsumers) {
         if (threadIdx.x == kConsumers) produce(p, s, stop);
@@ -1443,17 +1682,35 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
         if (stamp && step == 0) p.profile[0] = global_ns();
         for (int i = 0; i < p.n_ops; ++i) {
             const StepOp& op = p.ops[i];
+            // Publish the op entered (the barrier before it has passed) to the
+            // producer, which holds back units of activations until then.
+            if (threadIdx.x == 0) {
+                __threadfence_block();
+                *s.op_clock = (unsigned)step * (unsigned)p.n_ops + (unsigned)i;
+            }
+            Trace tro = trace_of(p.profile);
+            tro.begin();
             switch (op.kind) {
             case kOpEmbed: op_embed<WT>(p, position); break;
-            case kOpProduct: op_product<WT, NT>(p, op, position, s, work); break;
+            case kOpProduct:
+                if (p.umma) product_umma<WT>(p, op, position, s, tm);
+                else op_product<WT, NT>(p, op, position, s, work);
+                break;
             case kOpSelfAttention: op_self_attention<WT>(p, op, position, work); break;
             case kOpCrossAttention: op_cross_attention<WT>(p, op, s, work); break;
             case kOpLogits: op_logits<WT, NT>(p, op, position, s, work); break;
-            case kOpNorm: op_norm<WT>(p, op); break;
+            case kOpNorm: op_norm<WT>(p, op, work); break;
+            case kOpReduce: op_reduce<WT>(p, op, position); break;
             }
-            if (!grid_barrier(p.barrier, epoch, p.state)) {
+            tro.end(kTrOther);
+            Trace trb = trace_of(p.profile);
+            trb.begin();
+            const bool passed = grid_barrier(p.barrier, epoch, p.state);
+            trb.end(kTrBarrier);
+            if (!passed) {
                 trace_flush(p);
                 if (threadIdx.x == 0) *stop = 1;
+                release_tensor_memory(p, tm);
                 return;
             }
             if (stamp && step == 0) p.profile[i + 1] = global_ns();
@@ -1462,6 +1719,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
     }
     trace_flush(p);
     if (threadIdx.x == 0) *stop = 1;
+    release_tensor_memory(p, tm);
 }
 
 // Shared memory past the ring: the largest work area any op of the launch uses.
@@ -1479,7 +1737,7 @@ size_t work_bytes(const StepParams& p, int max_chunk) {
 
 template <typename WT, int NT>
 size_t shared_bytes(const StepParams& p, int max_chunk) {
-    return (size_t)p.stages * p.stage_bytes + 16 * kMaxStages + work_bytes<WT, NT>(p, max_chunk);
+    return 1024 + (size_t)p.stages * p.stage_bytes + 16 * kMaxStages + work_bytes<WT, NT>(p, max_chunk);
 }
 
 template <typename WT, int NT>
@@ -1548,8 +1806,8 @@ size_t work_rows(const StepParams& p, int max_chunk) {
 int decode_tile_rows(const StepParams& p) { return 8 * tile_columns(p); }
 
 size_t decode_work_bytes(bool half, const StepParams& p, int max_chunk) {
-    return (half ? work_rows<__half>(p, max_chunk) : work_rows<__nv_bfloat16>(p, max_chunk)) +
-           16 * kMaxStages;
+    return (half ? work_rows<__half>(p, max_chunk) : work_rows<__nv_bfloat16>(p, max_chunk)) + 16 * kMaxStages +
+           1024;
 }
 
 int decode_blocks_per_sm(bool half, const StepParams& p, int max_chunk) {

@@ -50,6 +50,7 @@ enum OpKind : int {
     kOpLogits = 4,
     kOpNone = 5,
     kOpNorm = 6,
+    kOpReduce = 7,
 };
 enum EpilogueKind : int { kEpQkv = 0, kEpStore = 1, kEpResidual = 2, kEpGelu = 3 };
 
@@ -60,7 +61,7 @@ enum StateWord : int {
     kPosition = 0, kError = 1, kAbort = 2, kStepsDone = 3, kAllEnded = 4,
     kFailKind = 5, kFailCta = 6, kFailWhere = 7, kStateWords = 8
 };
-enum WaitKind : int { kWaitGrid = 1, kWaitUnit = 2, kWaitEmpty = 3, kWaitDrain = 4, kWaitArmed = 5 };
+enum WaitKind : int { kWaitGrid = 1, kWaitUnit = 2, kWaitEmpty = 3, kWaitDrain = 4, kWaitArmed = 5, kWaitGate = 6 };
 enum ErrorBit : int { kErrToken = 1, kErrBarrierTimeout = 2 };
 
 // Weight matrices are stored fragment-packed: the 16-row tiles of an [n, kp]
@@ -73,6 +74,19 @@ __host__ __device__ inline size_t packed_offset(int n, int k, int chunks) {
     const int tile = n >> 4, row = n & 15, chunk = k >> 5, kk = k & 31;
     const int lane = (row & 7) * 4 + (kk >> 3);
     return (((size_t)tile * chunks + chunk) * 32 + lane) * 16 + (row >> 3) * 8 + (kk & 7);
+}
+
+// With many rows (the tensor-core products), weights and 16-bit activations
+// are laid out for tcgen05: K-major blocks of 64 columns (128 bytes a row)
+// in 8-row atoms whose 16-byte pieces rotate by row % 8 (the 128-byte
+// swizzle).  A weight matrix is 128-row tiles of kp/64 such blocks (16 KB
+// each); an activation matrix is kp/64 blocks of act_rows rows.
+__host__ __device__ inline size_t umma_offset(int n, int k, int kblocks) {
+    const int tile = n >> 7, r = n & 127, kb = k >> 6, c = (k >> 3) & 7;
+    return (((size_t)tile * kblocks + kb) * 128 + r) * 64 + ((c ^ (r & 7)) << 3) + (k & 7);
+}
+__host__ __device__ inline size_t act_offset(int r, int c, int act_rows) {
+    return ((size_t)(c >> 6) * act_rows + r) * 64 + ((((c >> 3) & 7) ^ (r & 7)) << 3) + (c & 7);
 }
 
 struct StepOp {
@@ -112,12 +126,23 @@ struct StepOp {
     // A product or the logits with input16 set and no gamma read such rows.
     int norm_rows, norm_step, norm_offset;
     float* norm_hidden;
+    int norm_umma;          // norm: write the tensor-core activation layout
+    // Tensor-core products: K splits of each tile's inner size.  With more
+    // than one, each item writes fp32 partials to p.partial_d [split][n_pad]
+    // [rows_pad] and the reduce op after the product sums them in split order
+    // and applies the epilogue.
+    int ksplit;
 };
 
 struct StepParams {
     int windows, tokens, rows;          // B, T, R
     int width, heads, head_width, ffn, vocabulary, kpd;
     int max_positions, ring_stride;
+    // Tensor-core products: weights and activations in the umma layouts
+    // above; act_rows rows an activation block; a product item covers
+    // umma_rows rows (<= 256) of 128 weight rows.
+    int umma, act_rows, umma_rows;
+    float* partial_d;                   // fp32 split-K partials of a tensor-core product
     float scale;                        // 1/sqrt(D), on the scores (DecoderShape.cpp:19-26)
     int out_rows, row_step, row_offset; // logits rows: row i reads h row i*row_step + row_offset
 
@@ -157,14 +182,37 @@ struct StepParams {
     const unsigned* schedule_offsets;
 };
 
-// One weight-stream unit: a 16-byte aligned source and its size in bytes.
+// Item (m tile of 128 weight rows, row group, K split) of a tensor-core
+// product: CTA c takes items c, c + grid, ...; split `split` covers k-blocks
+// [kb0, kb1) of the kp/64.
+struct UmmaItem {
+    int m, r0, rows, split, kb0, kb1;
+};
+__host__ __device__ inline UmmaItem umma_item(const StepParams& p, const StepOp& op, int item) {
+    const int m_tiles = (op.n + 127) / 128, groups = (p.rows + p.umma_rows - 1) / p.umma_rows;
+    const int kblocks = op.kp / 64, ks = op.ksplit > 1 ? op.ksplit : 1, per = (kblocks + ks - 1) / ks;
+    UmmaItem u;
+    u.m = item % m_tiles;
+    const int rest = item / m_tiles;
+    u.r0 = (rest % groups) * p.umma_rows;
+    u.rows = p.rows - u.r0 < p.umma_rows ? p.rows - u.r0 : p.umma_rows;
+    u.split = rest / groups;
+    u.kb0 = u.split * per;
+    u.kb1 = u.kb0 + per < kblocks ? u.kb0 + per : kblocks;
+    return u;
+}
+
+// One weight-stream unit: a 16-byte aligned source, its size in bytes (low
+// 32 bits of `bytes`) and a gate (high 32 bits): 0, or 1 + the index of the
+// op whose start it waits for -- a unit of activations an earlier op of the
+// same step writes may not be fetched before that op has finished.
 struct __align__(16) ScheduleEntry {
     unsigned long long source;
     unsigned long long bytes;
 };
 
-__host__ __device__ inline ScheduleEntry schedule_entry(const void* src, unsigned bytes) {
-    return ScheduleEntry{(unsigned long long)(size_t)src, (unsigned long long)bytes};
+__host__ __device__ inline ScheduleEntry schedule_entry(const void* src, unsigned bytes, unsigned gate = 0) {
+    return ScheduleEntry{(unsigned long long)(size_t)src, (unsigned long long)bytes | ((unsigned long long)gate << 32)};
 }
 
 }  // namespace wsp

@@ -8,7 +8,7 @@ namespace wsp {
 // Input rows of a general product's tile in a launch with these parameters.
 int decode_tile_rows(const StepParams& p);
 
-// Shared memory the kernel needs past its weight-stream ring (bytes).
+// Shared memory the kernel needs besides its weight-stream ring (bytes).
 size_t decode_work_bytes(bool half, const StepParams& p, int max_chunk);
 
 // CTAs of the decode kernel one SM holds for these parameters (0: none fit).
