@@ -78,6 +78,19 @@ int wsp_device_count(int* count);
  */
 int wsp_decoder_create(const wsp_decoder_shape* shape, int device, int windows,
                        wsp_dtype storage, wsp_decoder** out);
+
+/*
+ * The same with the form of the products chosen: WSP_PRODUCTS_MMA (mma.sync
+ * tiles of 16 weight rows), WSP_PRODUCTS_TCGEN05 (tcgen05 tiles of 128
+ * weight rows against every window's row, accumulated in tensor memory;
+ * widths in 64-column blocks, 64-wide heads and 16+ windows, else
+ * WSP_MODEL_ERROR), or WSP_PRODUCTS_AUTO (what wsp_decoder_create does: the
+ * faster for the window count, as measured on B200).  No counterpart in the
+ * reference.
+ */
+enum { WSP_PRODUCTS_AUTO = 0, WSP_PRODUCTS_MMA = 1, WSP_PRODUCTS_TCGEN05 = 2 };
+int wsp_decoder_create_products(const wsp_decoder_shape* shape, int device, int windows,
+                                wsp_dtype storage, int products, wsp_decoder** out);
 void wsp_decoder_destroy(wsp_decoder* decoder);
 
 /*

@@ -31,9 +31,10 @@ def shape_of(o: O.Shape):
     return DecoderShape(**o.__dict__)
 
 
-def make_decoder(oshape: O.Shape, tensors: dict, storage: str = "float16", windows: int = 1):
+def make_decoder(oshape: O.Shape, tensors: dict, storage: str = "float16", windows: int = 1,
+                 products: str = "auto"):
     from whispereacp_b200 import Decoder
-    decoder = Decoder(shape_of(oshape), windows=windows, storage=storage)
+    decoder = Decoder(shape_of(oshape), windows=windows, storage=storage, products=products)
     decoder.load_weights(tensors)
     return decoder
 

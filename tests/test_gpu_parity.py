@@ -132,10 +132,12 @@ def test_batched_windows_follow_the_oracle():
             check_tokens([together[b][k]], logits, later)
 
 
-def test_wide_batched_windows_follow_the_oracle():
+@pytest.mark.parametrize("products", ["mma", "tcgen05"])
+def test_wide_batched_windows_follow_the_oracle(products):
     """Forty windows of a 1024-wide decoder with the full vocabulary: 32 KB
     weight-stream stages leave room for fewer stages than warps, the logits
-    run as two row tiles with each warp owning every seventh vocabulary tile.
+    run as two row tiles with each warp owning every seventh vocabulary tile;
+    both product forms.
     Each window's
     transcript, replayed through the oracle, is its greedy choice wherever
     the margin decides it."""
@@ -147,7 +149,7 @@ def test_wide_batched_windows_follow_the_oracle():
     tensors = stored_tensors(S.normal_weights(shape, seed=51), "float16")
     encoders = S.encoder_output(windows, shape.cross_positions, shape.width, seed=52)
     first, later = S.suppression_masks(shape.vocabulary_size)
-    batched = make_decoder(oracle_shape(shape), tensors, windows=windows)
+    batched = make_decoder(oracle_shape(shape), tensors, windows=windows, products=products)
     batched.set_generation(prompt, first, later, maximum_tokens=steps, stop_at_end_of_text=False)
     together = batched.transcribe(encoders)
     decided = 0
@@ -164,8 +166,9 @@ def test_wide_batched_windows_follow_the_oracle():
 
 @pytest.mark.parametrize("storage", ["float16", "bfloat16"])
 def test_tensor_core_products_match_the_oracle(storage):
-    """Thirty-two windows: the products run as tcgen05 tiles (128 weight rows
-    against every window's row, accumulated in tensor memory).  Teacher-forced
+    """Thirty-two windows with the products as tcgen05 tiles (128 weight rows
+    against every window's row, accumulated in tensor memory, split along K
+    and joined).  Teacher-forced
     logits of every window match its own oracle sequence within max-abs 2e-2."""
     run = S.CONFIGS["tiny_en_b1"]
     shape = run.shape
@@ -175,7 +178,7 @@ def test_tensor_core_products_match_the_oracle(storage):
     rng = np.random.default_rng(63)
     ids = rng.integers(0, 50256, size=(windows, 5)).astype(np.uint32)
     ids[:, :2] = run.prompt
-    decoder = make_decoder(oracle_shape(shape), tensors, storage, windows=windows)
+    decoder = make_decoder(oracle_shape(shape), tensors, storage, windows=windows, products="tcgen05")
     decoder.begin_sequence(encoders)
     steps = [decoder.step(ids[:, :2])] + [decoder.step(ids[:, k:k + 1]) for k in range(2, 5)]
     worst = 0.0

@@ -64,6 +64,7 @@ SIGNATURES = {
     "wsp_abi_version": ([], _I),
     "wsp_device_count": ([ctypes.POINTER(_I)], _I),
     "wsp_decoder_create": ([ctypes.POINTER(CShape), _I, _I, _I, ctypes.POINTER(_P)], _I),
+    "wsp_decoder_create_products": ([ctypes.POINTER(CShape), _I, _I, _I, _I, ctypes.POINTER(_P)], _I),
     "wsp_decoder_destroy": ([_P], None),
     "wsp_decoder_set_tensor": ([_P, ctypes.c_char_p, _I, ctypes.POINTER(ctypes.c_int64), _I, _P], _I),
     "wsp_decoder_check_weights": ([_P], _I),

@@ -143,10 +143,10 @@ struct LayerBuffers {
 
 class Decoder {
 public:
-    Decoder(const wsp_decoder_shape& shape, int device, int windows, Storage storage)
+    Decoder(const wsp_decoder_shape& shape, int device, int windows, Storage storage, int products)
         : shape_(shape), device_(device), windows_(windows), storage_(storage) {
         validate_shape();
-        umma_ = choose_umma();
+        umma_ = choose_umma(products);
         CUDA_CHECK(cudaSetDevice(device_));
         CUDA_CHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
         CUDA_CHECK(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, device_));
@@ -617,12 +617,25 @@ private:
 
     static size_t round16(size_t n) { return (n + 15) / 16 * 16; }
 
-    // Tensor-core products (tcgen05) for batches of many windows: from this
-    // many windows, with widths and heads the umma layouts cover.
-    static constexpr int kUmmaWindows = 32;
-    bool choose_umma() const {
-        return windows_ >= kUmmaWindows && shape_.width % 64 == 0 && shape_.feed_forward_width % 64 == 0 &&
-               head_width() == 64;
+    // The products' form.  tcgen05 tiles (128 weight rows against every
+    // window's row, accumulated in tensor memory) need widths in 64-column
+    // blocks, 64-wide heads and at least 16 windows (an MMA's N >= 16).
+    // Measured on B200 they beat the mma.sync tiles once 128 windows share
+    // each weight tile (large-v3, 128 windows: 33 us a product against 37)
+    // and lose below (medium.en at 64 windows: 19 against 14), so AUTO picks
+    // them from kUmmaWindows windows.
+    static constexpr int kUmmaWindows = 128;
+    bool umma_possible() const {
+        return windows_ >= 16 && shape_.width % 64 == 0 && shape_.feed_forward_width % 64 == 0 && head_width() == 64;
+    }
+    bool choose_umma(int products) const {
+        if (products == WSP_PRODUCTS_MMA) return false;
+        if (products == WSP_PRODUCTS_TCGEN05) {
+            if (!umma_possible())
+                throw ModelError("tcgen05 products need widths in 64-column blocks, 64-wide heads and 16+ windows");
+            return true;
+        }
+        return umma_possible() && windows_ >= kUmmaWindows;
     }
     // Rows a product weight matrix is allocated with: whole 16-row tiles, or
     // whole 128-row tiles for the tensor-core products.
@@ -722,7 +735,7 @@ private:
             CUDA_CHECK(cudaMemset(state_.get<int>() + kError, 0, sizeof(int)));
             if (state[kError] & kErrBarrierTimeout) {
                 static const char* const kinds[] = {"?", "a grid barrier", "a weight unit", "a free stage",
-                                                    "a landing copy", "an armed stage", "an op to start"};
+                                                    "a landing copy", "an armed stage", "the splits of a product"};
                 const int kind = state[kFailKind] >= 1 && state[kFailKind] <= 6 ? state[kFailKind] : 0;
                 CUDA_CHECK(cudaMemset(state_.get<int>() + kFailKind, 0, 3 * sizeof(int)));
                 throw CudaFailure(std::string("the decode kernel gave up waiting for ") + kinds[kind] + " (CTA " +
@@ -742,7 +755,6 @@ private:
         case kOpCrossAttention: return WSP_KERNEL_CROSS_ATTENTION;
         case kOpLogits: return WSP_KERNEL_LOGITS_ARGMAX;
         case kOpNorm: return WSP_KERNEL_LAYER_NORM;
-        case kOpReduce: return WSP_KERNEL_PROJECTION;
         }
         return WSP_KERNEL_OTHER;
     }
@@ -917,34 +929,26 @@ private:
         return best;
     }
 
-    // Tensor-core products: split each one's inner size so that its items --
-    // (128-row weight tile, row group, split) -- cover the grid, every split
-    // at least one k-block; a split product is followed by the reduce op
-    // that joins its partials.  Returns the partials' size in bytes.
+    // Tensor-core products: a product whose (128-row weight tile, row
+    // group) items fill less than half the grid splits its inner size so
+    // that its items still fit one wave -- each split on its own CTA, which
+    // lets the tile's splits meet and join their partials.  Returns the
+    // partials' size in bytes.
     size_t split_products(std::vector<StepOp>& ops, const StepParams& p, int grid) const {
-        std::vector<StepOp> out;
         size_t partial_bytes = 0;
         const int groups = (p.rows + p.umma_rows - 1) / p.umma_rows;
-        for (StepOp op : ops) {
-            if (op.kind != kOpProduct || !p.umma) {
-                out.push_back(op);
-                continue;
-            }
+        for (StepOp& op : ops) {
+            if (op.kind != kOpProduct || !p.umma) continue;
             const int m_tiles = (op.n + 127) / 128, kblocks = op.kp / 64;
             const int base = m_tiles * groups;
-            int ks = std::max(1, std::min(kblocks, (grid + base / 2) / base));
-            const int per = (kblocks + ks - 1) / ks;
-            ks = (kblocks + per - 1) / per;
-            op.ksplit = ks;
-            out.push_back(op);
+            int ks = 2 * base > grid ? 1 : std::min(kblocks, grid / base);
             if (ks > 1) {
-                StepOp reduce = op;
-                reduce.kind = kOpReduce;
-                out.push_back(reduce);
-                partial_bytes = std::max(partial_bytes, (size_t)ks * m_tiles * 128 * groups * p.umma_rows * 4);
+                const int per = (kblocks + ks - 1) / ks;
+                ks = (kblocks + per - 1) / per;
             }
+            op.ksplit = ks;
+            if (ks > 1) partial_bytes = std::max(partial_bytes, (size_t)ks * m_tiles * 128 * groups * p.umma_rows * 4);
         }
-        ops.swap(out);
         return partial_bytes;
     }
 
@@ -986,7 +990,7 @@ private:
         for (size_t i = 0; i < schedule_host_.size(); ++i) {
             const ScheduleEntry& e = schedule_host_[i];
             if (e.source == 0 && e.bytes == 0) continue;  // the placeholder of an empty schedule
-            const size_t bytes = (size_t)(e.bytes & 0xFFFFFFFFull);
+            const size_t bytes = (size_t)e.bytes;
             const size_t lo = (size_t)e.source, hi = lo + bytes;
             auto it = std::upper_bound(ranges.begin(), ranges.end(), std::make_pair(lo, (size_t)-1));
             const bool inside = it != ranges.begin() && lo >= std::prev(it)->first && hi <= std::prev(it)->second;
@@ -997,9 +1001,13 @@ private:
 
     // Stage size: one 16-row tile over kpd (at least 16 KB); as many stages
     // (2..8) as the shared memory left by the work area holds.
-    void configure_stream(bool half, StepParams& p) const {
+    int stage_bytes_for_width() const {
         const int tile = 16 * padded(shape_.width) * 2;
-        p.stage_bytes = std::max(16384, (tile + 1023) / 1024 * 1024);
+        return std::max(16384, (tile + 1023) / 1024 * 1024);
+    }
+
+    void configure_stream(bool half, StepParams& p) const {
+        p.stage_bytes = stage_bytes_for_width();
         const size_t work = decode_work_bytes(half, p, kMaxCrossChunk);
         const long long room = (long long)max_shared_ - (long long)work;
         p.stages = (int)std::min<long long>(8, room / p.stage_bytes);
@@ -1066,10 +1074,17 @@ private:
         StepParams p = base_params(T, sample, mask, logits, hidden, row_tokens, steps, stop);
         p.profile = profile;
         const bool half = storage_ == Storage::f16;
-        configure_stream(half, p);
-        // A tensor-core item's rows: as many as a stage holds (128 bytes a
-        // row), at most 256, a multiple of 16.
+        // A tensor-core item's rows: as many as a weight stage holds (128
+        // bytes a row), at most 256, a multiple of 16; the activation ring
+        // holds kMaxXStages blocks of that many rows.
+        p.stage_bytes = stage_bytes_for_width();
         p.umma_rows = std::min(256, p.stage_bytes / 128 / 16 * 16);
+        if (umma_) {
+            p.umma_x_stage_bytes = std::min(p.umma_rows, (R + 15) / 16 * 16) * 128;
+            p.umma_x_stages = 4;
+            p.umma_blocks = std::max(1, p.stage_bytes / 16384);
+        }
+        configure_stream(half, p);
         const int blocks = decode_blocks_per_sm(half, p, kMaxCrossChunk);
         if (blocks <= 0) throw CudaFailure("the decode kernel does not fit on an SM", false);
         const int grid = sm_count_ * std::min(blocks, kMaxBlocksPerSm);
@@ -1079,6 +1094,12 @@ private:
         const size_t partial_bytes = split_products(ops, p, grid);
         if (partial_d_.bytes() < partial_bytes) partial_d_.allocate(partial_bytes);
         p.partial_d = partial_d_.get<float>();
+        if (umma_) {
+            const size_t counter_bytes = ops.size() * kSplitSlots * sizeof(unsigned);
+            if (split_counters_.bytes() < counter_bytes) split_counters_.allocate(counter_bytes);
+            CUDA_CHECK(cudaMemsetAsync(split_counters_.get(), 0, counter_bytes, stream_));
+            p.split_counters = split_counters_.get<unsigned>();
+        }
         if (ops_dev.bytes() < ops.size() * sizeof(StepOp)) ops_dev.allocate(ops.size() * sizeof(StepOp));
         CUDA_CHECK(cudaMemcpyAsync(ops_dev.get(), ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice,
                                    stream_));
@@ -1211,7 +1232,7 @@ private:
 
     DeviceBuffer self_keys_, self_values_, cross_kv_, encoder_staging_, encoder16_;
     DeviceBuffer ring_, ring_prompt_, state_, masks_;
-    DeviceBuffer hidden_, queries_, normalised_, attended_, feed_forward_, partial_, partial_d_;
+    DeviceBuffer hidden_, queries_, normalised_, attended_, feed_forward_, partial_, partial_d_, split_counters_;
     DeviceBuffer candidate_values_, candidate_indices_, row_tokens_, counters_;
     DeviceBuffer barrier_, ended_, profile_;
     DeviceBuffer logits_staging_, hidden_staging_;
@@ -1289,18 +1310,25 @@ int wsp_device_count(int* count) {
     });
 }
 
-int wsp_decoder_create(const wsp_decoder_shape* shape, int device, int windows, wsp_dtype storage,
-                       wsp_decoder** out) {
+int wsp_decoder_create_products(const wsp_decoder_shape* shape, int device, int windows, wsp_dtype storage,
+                                int products, wsp_decoder** out) {
     return guarded([&] {
         if (!shape || !out) throw wsp::InvalidArgument("shape and out must not be NULL");
         *out = nullptr;
         if (storage != WSP_FLOAT16 && storage != WSP_BFLOAT16)
             throw wsp::InvalidArgument("storage must be WSP_FLOAT16 or WSP_BFLOAT16");
+        if (products != WSP_PRODUCTS_AUTO && products != WSP_PRODUCTS_MMA && products != WSP_PRODUCTS_TCGEN05)
+            throw wsp::InvalidArgument("products must be WSP_PRODUCTS_AUTO, WSP_PRODUCTS_MMA or WSP_PRODUCTS_TCGEN05");
         auto holder = std::make_unique<wsp_decoder>();
         holder->impl = std::make_unique<wsp::Decoder>(
-            *shape, device, windows, storage == WSP_FLOAT16 ? wsp::Storage::f16 : wsp::Storage::bf16);
+            *shape, device, windows, storage == WSP_FLOAT16 ? wsp::Storage::f16 : wsp::Storage::bf16, products);
         *out = holder.release();
     });
+}
+
+int wsp_decoder_create(const wsp_decoder_shape* shape, int device, int windows, wsp_dtype storage,
+                       wsp_decoder** out) {
+    return wsp_decoder_create_products(shape, device, windows, storage, WSP_PRODUCTS_AUTO, out);
 }
 
 void wsp_decoder_destroy(wsp_decoder* decoder) { delete decoder; }

@@ -90,26 +90,22 @@ inline void append_cross_units(const StepParams& p, const StepOp& op, int cta, i
 }
 
 // Tensor-core product: item (m tile of 128 weight rows, group of umma_rows
-// rows), CTA c taking items c, c + grid, ...; per k-block of 64 columns, the
-// weight block (16 KB) then the rows' activation block (rows rounded to 16,
-// 128 bytes each), as product_umma reads them.
+// rows, K split), CTA c taking items c, c + grid, ...; the split's weight
+// blocks (16 KB per 64 columns), umma_blocks to a unit, as product_umma
+// reads them.
+// (The rows' activations come through the product's own ring.)
 inline int umma_items(const StepParams& p, const StepOp& op) {
     return ((op.n + 127) / 128) * ((p.rows + p.umma_rows - 1) / p.umma_rows) * (op.ksplit > 1 ? op.ksplit : 1);
 }
-inline void append_umma_units(const StepParams& p, const StepOp& op, int op_index, int cta, int grid,
+inline void append_umma_units(const StepParams& p, const StepOp& op, int cta, int grid,
                               std::vector<ScheduleEntry>& out) {
     const int kblocks = op.kp / 64;
     for (int item = cta; item < umma_items(p, op); item += grid) {
         const UmmaItem u = umma_item(p, op, item);
-        const int m = u.m, r0 = u.r0;
-        const unsigned n16 = (unsigned)(u.rows + 15) / 16 * 16;
-        for (int kb = u.kb0; kb < u.kb1; ++kb) {
-            out.push_back(schedule_entry(static_cast<const unsigned char*>(op.weight) + ((size_t)m * kblocks + kb) * 16384,
-                                         16384u));
-            // The rows the ops before this one wrote: gated on this op's start.
-            out.push_back(schedule_entry(static_cast<const unsigned char*>(op.input16) +
-                                             ((size_t)kb * p.act_rows + r0) * 128,
-                                         n16 * 128u, (unsigned)op_index + 1));
+        for (int kb = u.kb0; kb < u.kb1; kb += p.umma_blocks) {
+            const int n = std::min(p.umma_blocks, u.kb1 - kb);
+            out.push_back(schedule_entry(static_cast<const unsigned char*>(op.weight) + ((size_t)u.m * kblocks + kb) * 16384,
+                                         16384u * (unsigned)n));
         }
     }
 }
@@ -121,14 +117,13 @@ inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, 
     units.clear();
     offsets.assign(1, 0u);
     for (int cta = 0; cta < grid; ++cta) {
-        for (size_t op_index = 0; op_index < ops.size(); ++op_index) {
-            const StepOp& op = ops[op_index];
+        for (const StepOp& op : ops) {
             if (op.kind == kOpCrossAttention) {
                 append_cross_units(p, op, cta, grid, units);
                 continue;
             }
             if (op.kind == kOpProduct && p.umma) {
-                append_umma_units(p, op, (int)op_index, cta, grid, units);
+                append_umma_units(p, op, cta, grid, units);
                 continue;
             }
             const int items = op_items(p, op, rt);

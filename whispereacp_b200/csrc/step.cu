@@ -132,6 +132,7 @@ __device__ __forceinline__ float bits_to_float(unsigned short b) {
 // -------------------------------------------------------------- grid barrier
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
+constexpr unsigned long long kAbortLookNs = 50000ull;          // 50 us
 
 // A monotonic arrival counter: each CTA adds one with release semantics and
 // waits, with acquire loads, until every CTA has arrived `epoch` times.  The
@@ -185,7 +186,6 @@ __device__ __forceinline__ uint32_t smem_address(const void* p) {
 
 struct Stream {
     unsigned char* ring;          // stages x stage_bytes
-    volatile unsigned* op_clock;  // the op the consumers have entered: step * n_ops + op
     uint64_t* full;               // per stage: the unit landed (tx bytes)
     uint64_t* empty;              // per stage: the 8 consumer warps released it
     int stages;
@@ -216,13 +216,15 @@ __device__ bool wait_parity(const StepParams& p, uint64_t* bar, uint32_t parity,
     for (unsigned spin = 1; !try_parity(bar, parity); ++spin) {
         if (stop && *stop) return false;
         if ((spin & 15) != 0) continue;
-        // Another wait gave up: this one will not be answered either.  (The
-        // producer's final drain still waits for its copies in flight.)
-        if (kind != kWaitDrain && ld_volatile(p.state + kAbort)) return false;
-        if (global_ns() - start > kWaitTimeoutNs) {
+        const unsigned long long waited = global_ns() - start;
+        if (waited > kWaitTimeoutNs) {
             record_timeout(p.state, kind, (long long)index);
             return false;
         }
+        // A wait this long may be one another wait's failure left
+        // unanswered: look at the abort word (a global load, so never in a
+        // short wait).  The producer's final drain still waits for its copies.
+        if (waited > kAbortLookNs && kind != kWaitDrain && ld_volatile(p.state + kAbort)) return false;
     }
     return true;
 }
@@ -298,34 +300,9 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
                 break;
             }
             const ulonglong2 e = __ldg(schedule + i);
-            const unsigned gate = (unsigned)(e.y >> 32);
-            if (gate != 0) {
-                // Activations an earlier op wrote: wait until the consumers
-                // have entered the unit's op (its grid barrier passed), then
-                // order those generic writes before this bulk (async) read.
-                const unsigned target = (unsigned)step * (unsigned)p.n_ops + gate - 1;
-                if (*s.op_clock < target) {
-                    const unsigned long long start = global_ns();
-                    for (unsigned spin = 1; *s.op_clock < target; ++spin) {
-                        if (*stop) break;
-                        if ((spin & 15) != 0) continue;
-                        if (ld_volatile(p.state + kAbort)) break;
-                        if (global_ns() - start > kWaitTimeoutNs) {
-                            record_timeout(p.state, kWaitGate, (long long)target);
-                            break;
-                        }
-                    }
-                    if (*s.op_clock < target) {
-                        go = false;
-                        break;
-                    }
-                }
-                __threadfence_block();
-                asm volatile("fence.proxy.async.global;\n" ::: "memory");
-            }
             const uint32_t bar = smem_address(s.full + stage);
             const uint32_t dst = smem_address(s.ring + (size_t)stage * s.stage_bytes);
-            const unsigned bytes = (unsigned)e.y;
+            const unsigned bytes = (unsigned)e.y;  // (the high half is unused)
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
             asm volatile(
                 "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
@@ -756,11 +733,21 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
 // k-block); warps 0..3, whole warps since tcgen05.ld is warp-collective,
 // read D back (lane = weight row) for the epilogue.
 struct TensorMemory {
-    uint32_t base;    // allocated columns (kTmemColumns), lanes 0..127
-    uint64_t* done;   // the item's products completed (tcgen05.commit)
+    uint32_t base;           // allocated columns (kTmemColumns), lanes 0..127
+    uint64_t* done;          // the item's products completed (tcgen05.commit)
     uint32_t phase;
+    // The activations' own ring in the work area: blocks of the rows an op
+    // reads, fetched once the op has started (the weights' ring runs ahead
+    // across ops).
+    unsigned char* x_ring;
+    uint64_t* x_full;        // [x_stages] the block landed
+    uint64_t* x_empty;       // [x_stages] the products that read it completed
+    int x_stages, x_stage_bytes;
+    unsigned long long x_next;
 };
 constexpr uint32_t kTmemColumns = 256;
+constexpr int kLoadWarp = 5;      // lane 0 fetches the activation blocks
+constexpr int kMaxXStages = 4;
 constexpr int kIssueWarp = 4;  // not one of the epilogue warps 0..3
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
@@ -809,37 +796,69 @@ __device__ __forceinline__ void tmem_load32(uint32_t address, uint32_t (&r)[32])
 }
 
 template <typename WT>
-__device__ void product_umma(const StepParams& p, const StepOp& op, int position, Stream& s, TensorMemory& tm) {
+__device__ void product_umma(const StepParams& p, const StepOp& op, int position, int step, int op_index, Stream& s,
+                             TensorMemory& tm) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m_tiles = (op.n + 127) / 128, groups = (p.rows + p.umma_rows - 1) / p.umma_rows;
     const int ks = op.ksplit > 1 ? op.ksplit : 1;
     const int items = m_tiles * groups * ks;
     const int row_stride = groups * p.umma_rows;  // of the partials
+    __shared__ int join_ok;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const UmmaItem u = umma_item(p, op, item);
         const int m = u.m, r0 = u.r0, rows = u.rows;
-        const int kblocks = u.kb1 - u.kb0;
+        const int nkb = u.kb1 - u.kb0;
         const int n16 = (rows + 15) & ~15;
+        const unsigned long long x0 = tm.x_next;
+        if (threadIdx.x == 32 * kLoadWarp) {
+            // The rows' activation blocks, written by the ops before this one
+            // (whose grid barrier has passed): generic writes ordered before
+            // these bulk reads, then one copy a block into the X stages.
+            asm volatile("fence.proxy.async.global;\n" ::: "memory");
+            const unsigned char* src = static_cast<const unsigned char*>(op.input16) +
+                                       ((size_t)u.kb0 * p.act_rows + r0) * 128;
+            const unsigned bytes = (unsigned)n16 * 128u;
+            for (int j = 0; j < nkb; ++j) {
+                const unsigned long long q = x0 + j;
+                const int st = (int)(q % tm.x_stages);
+                if (q >= (unsigned long long)tm.x_stages &&
+                    !wait_parity(p, tm.x_empty + st, (uint32_t)((q / tm.x_stages - 1) & 1), nullptr, kWaitEmpty, q))
+                    break;
+                const uint32_t bar = smem_address(tm.x_full + st);
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                        smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes)),
+                    "l"(src + (size_t)j * p.act_rows * 128), "r"(bytes), "r"(bar)
+                    : "memory");
+            }
+        }
         if (threadIdx.x == 32 * kIssueWarp) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t idesc = umma_idesc<WT>(n16);
-            for (int kb = 0; kb < kblocks; ++kb) {
-                const unsigned long long iw = s.next + 2 * (unsigned long long)kb, ix = iw + 1;
+            for (int j0 = 0; j0 < nkb; j0 += p.umma_blocks) {
+                const unsigned long long iw = s.next + j0 / p.umma_blocks;
                 const uint32_t w = smem_address(unit_at(p, s, iw));
-                const uint32_t x = smem_address(unit_at(p, s, ix));
+                for (int j = j0; j < nkb && j < j0 + p.umma_blocks; ++j) {
+                    const unsigned long long q = x0 + j;
+                    const int st = (int)(q % tm.x_stages);
+                    wait_parity(p, tm.x_full + st, (uint32_t)((q / tm.x_stages) & 1), nullptr, kWaitUnit, q);
+                    const uint32_t x = smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes);
+                    const uint32_t wb = w + (uint32_t)(j - j0) * 16384u;
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    umma_mma(tm.base, umma_desc(w + 32 * kk), umma_desc(x + 32 * kk), idesc, (kb | kk) != 0);
-                // A stage is free after kWarps arrivals: kWarps - 1 now, the
-                // last once the products above have read it.
+                    for (int kk = 0; kk < 4; ++kk)
+                        umma_mma(tm.base, umma_desc(wb + 32 * kk), umma_desc(x + 32 * kk), idesc, (j | kk) != 0);
+                    umma_commit(tm.x_empty + st);  // the X stage: free once these products have read it
+                }
+                // The weight stage is free after kWarps arrivals: kWarps - 1
+                // now, the last once the products above have read it.
                 stage_arrive(s, iw, kWarps - 1);
                 umma_commit(s.empty + iw % s.stages);
-                stage_arrive(s, ix, kWarps - 1);
-                umma_commit(s.empty + ix % s.stages);
             }
             umma_commit(tm.done);
         }
-        s.next += 2 * (unsigned long long)kblocks;
+        s.next += (unsigned long long)((nkb + p.umma_blocks - 1) / p.umma_blocks);
+        tm.x_next += (unsigned long long)nkb;
         float* partial = ks > 1 ? p.partial_d + (size_t)u.split * m_tiles * 128 * row_stride : nullptr;
         if (warp < 4) {
             Trace tr = trace_of(p.profile);
@@ -853,8 +872,6 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
                 uint32_t v[32];
                 tmem_load32(tm.base + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
                 if (partial) {
-                    // This split's sums over its k-blocks; the reduce op adds
-                    // the splits, the bias and the epilogue.
                     float* row = partial + (size_t)n * row_stride + r0 + c0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
@@ -869,26 +886,64 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
             tr.end(kTrEpilogue);
         }
         tm.phase ^= 1u;
+        if (ks > 1) {
+            // The tile's splits (each on its own CTA: a split product's items
+            // fit one wave) meet here; then each joins the rows n % ks ==
+            // split of the tile, summing the partials in split order.
+            __threadfence();
+            consumer_sync();
+            if (threadIdx.x == 0) {
+                unsigned* counter = p.split_counters + (size_t)op_index * kSplitSlots + (item % (m_tiles * groups));
+                asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(counter), "r"(1u) : "memory");
+                const unsigned target = (unsigned)(step + 1) * (unsigned)ks;
+                const unsigned long long start = global_ns();
+                int ok = 1;
+                for (unsigned spin = 1; ld_acquire(counter) < target; ++spin) {
+                    if ((spin & 15) != 0) continue;
+                    if (ld_volatile(p.state + kAbort)) { ok = 0; break; }
+                    if (global_ns() - start > kWaitTimeoutNs) {
+                        record_timeout(p.state, kWaitJoin, (long long)item);
+                        ok = 0;
+                        break;
+                    }
+                }
+                join_ok = ok;
+            }
+            consumer_sync();
+            if (join_ok) {
+                // Four elements a thread at a time, every split's load of all
+                // four issued before any sum, so the join costs a few L2
+                // round trips rather than one per element.
+                const int share = (128 - u.split + ks - 1) / ks;  // rows u.split, u.split + ks, ... of 128
+                const size_t split_stride = (size_t)m_tiles * 128 * row_stride;
+                const int total = share * rows;
+                for (int e0 = threadIdx.x; e0 < total; e0 += 4 * kThreads) {
+                    float sum[4] = {0.f, 0.f, 0.f, 0.f};
+                    const float* at[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int e = min(e0 + k * kThreads, total - 1);
+                        at[k] = p.partial_d + (size_t)(m * 128 + u.split + (e / rows) * ks) * row_stride + r0 + e % rows;
+                    }
+                    for (int sp = 0; sp < ks; ++sp) {
+                        float v[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) v[k] = ld_cg(at[k] + sp * split_stride);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) sum[k] += v[k];
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int e = e0 + k * kThreads;
+                        if (e >= total) break;
+                        const int n = m * 128 + u.split + (e / rows) * ks, t = e % rows;
+                        if (n < op.n)
+                            emit_output<WT>(p, op, position, n, r0 + t, sum[k] + (op.bias ? __ldg(op.bias + n) : 0.f));
+                    }
+                }
+            }
+        }
         consumer_sync();
-    }
-}
-
-// The splits of a tensor-core product summed in split order, the bias added
-// and the epilogue applied: element (n, r) per thread, row-contiguous reads.
-template <typename WT>
-__device__ void op_reduce(const StepParams& p, const StepOp& op, int position) {
-    const int m_tiles = (op.n + 127) / 128, groups = (p.rows + p.umma_rows - 1) / p.umma_rows;
-    const int row_stride = groups * p.umma_rows;
-    const size_t split_stride = (size_t)m_tiles * 128 * row_stride;
-    const long long total = (long long)op.n * p.rows;
-    for (long long e = (long long)blockIdx.x * kThreads + threadIdx.x; e < total; e += (long long)gridDim.x * kThreads) {
-        const int n = (int)(e / p.rows), r = (int)(e % p.rows);
-        const float* at = p.partial_d + (size_t)n * row_stride + r;
-        float v = op.bias ? __ldg(op.bias + n) : 0.f;
-        float sum = 0.f;
-#pragma unroll 8
-        for (int sp = 0; sp < op.ksplit; ++sp) sum += ld_cg(at + sp * split_stride);
-        emit_output<WT>(p, op, position, n, r, sum + v);
     }
 }
 
@@ -1625,17 +1680,23 @@ __device__ __forceinline__ void release_tensor_memory(const StepParams& p, const
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tm.base), "r"(kTmemColumns));
 }
 
-template <typename WT, int NT>
+// UMMA: the tensor-core product path (p.umma); a separate instantiation, so
+// the mma.sync kernel carries none of it.
+template <typename WT, int NT, bool UMMA>
 __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) {
-    extern __shared__ __align__(1024) unsigned char dynamic_smem[];
+    extern __shared__ __align__(128) unsigned char dynamic_smem[];
     __shared__ int stop_flag;
     __shared__ unsigned long long armed_units;
-    __shared__ unsigned op_clock;
     __shared__ uint32_t tmem_slot;
     __shared__ __align__(8) uint64_t tmem_done;
-    // The ring starts on a 1024-byte boundary (the 128-byte swizzle's period).
-    unsigned char* smem = reinterpret_cast<unsigned char*>(
-        (reinterpret_cast<uintptr_t>(dynamic_smem) + 1023) & ~static_cast<uintptr_t>(1023));
+    __shared__ __align__(8) uint64_t x_full[kMaxXStages];
+    __shared__ __align__(8) uint64_t x_empty[kMaxXStages];
+    // The tensor-core kernel's ring starts on a 1024-byte boundary (the
+    // 128-byte swizzle's period).  The mma.sync kernel keeps the 128-byte
+    // start: aligning it too measured 6 % slower at 32 windows.
+    unsigned char* smem = UMMA ? reinterpret_cast<unsigned char*>(
+                                     (reinterpret_cast<uintptr_t>(dynamic_smem) + 1023) & ~static_cast<uintptr_t>(1023))
+                               : dynamic_smem;
     Stream s;
     s.stages = p.stages;
     s.stage_bytes = p.stage_bytes;
@@ -1645,11 +1706,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
     unsigned char* work = smem + (size_t)s.stages * s.stage_bytes + 16 * kMaxStages;
     s.next = 0;
     s.armed = &armed_units;
-    s.op_clock = &op_clock;
     if (threadIdx.x == 0) {
         stop_flag = 0;
         armed_units = 0;
-        op_clock = 0;
         for (int i = 0; i < kTrSections; ++i) trace_cycles[i] = 0;
         for (int i = 0; i < s.stages; ++i) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(s.full + i)) : "memory");
@@ -1657,18 +1716,25 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
                          : "memory");
         }
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(&tmem_done)) : "memory");
+        for (int i = 0; i < kMaxXStages; ++i) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(x_full + i)) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_address(x_empty + i)) : "memory");
+        }
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
-    if (p.umma && threadIdx.x < 32) {
+    if (UMMA && threadIdx.x < 32) {
         __syncwarp();  // tcgen05.alloc is warp-collective; lane 0 has just set up the barriers
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_address(&tmem_slot)),
                      "r"(kTmemColumns));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    if (UMMA) asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    TensorMemory tm{p.umma ? tmem_slot : 0u, &tmem_done, 0u};
+    if (UMMA) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    TensorMemory tm{UMMA ? tmem_slot : 0u, &tmem_done, 0u,
+                    reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(work) + 1023) &
+                                                     ~static_cast<uintptr_t>(1023)),
+                    x_full, x_empty, p.umma_x_stages, p.umma_x_stage_bytes, 0ull};
     volatile int* stop = &stop_flag;
     if (threadIdx.x >= kConsumers) {
         if (threadIdx.x == kConsumers) produce(p, s, stop);
@@ -1682,25 +1748,18 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
         if (stamp && step == 0) p.profile[0] = global_ns();
         for (int i = 0; i < p.n_ops; ++i) {
             const StepOp& op = p.ops[i];
-            // Publish the op entered (the barrier before it has passed) to the
-            // producer, which holds back units of activations until then.
-            if (threadIdx.x == 0) {
-                __threadfence_block();
-                *s.op_clock = (unsigned)step * (unsigned)p.n_ops + (unsigned)i;
-            }
             Trace tro = trace_of(p.profile);
             tro.begin();
             switch (op.kind) {
             case kOpEmbed: op_embed<WT>(p, position); break;
             case kOpProduct:
-                if (p.umma) product_umma<WT>(p, op, position, s, tm);
+                if constexpr (UMMA) product_umma<WT>(p, op, position, step, i, s, tm);
                 else op_product<WT, NT>(p, op, position, s, work);
                 break;
             case kOpSelfAttention: op_self_attention<WT>(p, op, position, work); break;
             case kOpCrossAttention: op_cross_attention<WT>(p, op, s, work); break;
             case kOpLogits: op_logits<WT, NT>(p, op, position, s, work); break;
             case kOpNorm: op_norm<WT>(p, op, work); break;
-            case kOpReduce: op_reduce<WT>(p, op, position); break;
             }
             tro.end(kTrOther);
             Trace trb = trace_of(p.profile);
@@ -1710,7 +1769,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
             if (!passed) {
                 trace_flush(p);
                 if (threadIdx.x == 0) *stop = 1;
-                release_tensor_memory(p, tm);
+                if (UMMA) release_tensor_memory(p, tm);
                 return;
             }
             if (stamp && step == 0) p.profile[i + 1] = global_ns();
@@ -1719,7 +1778,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
     }
     trace_flush(p);
     if (threadIdx.x == 0) *stop = 1;
-    release_tensor_memory(p, tm);
+    if (UMMA) release_tensor_memory(p, tm);
 }
 
 // Shared memory past the ring: the largest work area any op of the launch uses.
@@ -1732,6 +1791,8 @@ size_t work_bytes(const StepParams& p, int max_chunk) {
     const size_t attention = sizeof(float) * std::max<size_t>(kAttentionFixed + std::max(max_chunk, p.max_positions),
                                                               64 + 32 + 2 * kWarps * 64 + kMaxCrossUnitKeys);
     size_t work = std::max(product, attention);
+    // The activation ring of the tensor-core products (1024-byte aligned).
+    if (p.umma) work = std::max(work, (size_t)1024 + (size_t)p.umma_x_stages * p.umma_x_stage_bytes);
     return (work + 127) / 128 * 128;
 }
 
@@ -1743,7 +1804,7 @@ size_t shared_bytes(const StepParams& p, int max_chunk) {
 template <typename WT, int NT>
 void launch_typed(const StepParams& p, int max_chunk, int grid, cudaStream_t stream) {
     const size_t smem = shared_bytes<WT, NT>(p, max_chunk);
-    auto kernel = decode_kernel<WT, NT>;
+    auto kernel = p.umma ? decode_kernel<WT, NT, true> : decode_kernel<WT, NT, false>;
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) throw std::runtime_error(std::string("decode kernel shared memory: ") + cudaGetErrorString(e));
     StepParams copy = p;
@@ -1755,7 +1816,7 @@ void launch_typed(const StepParams& p, int max_chunk, int grid, cudaStream_t str
 template <typename WT, int NT>
 int occupancy_typed(const StepParams& p, int max_chunk) {
     const size_t smem = shared_bytes<WT, NT>(p, max_chunk);
-    auto kernel = decode_kernel<WT, NT>;
+    auto kernel = p.umma ? decode_kernel<WT, NT, true> : decode_kernel<WT, NT, false>;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
         cudaGetLastError();
         return 0;

@@ -41,6 +41,8 @@ constexpr int kStepWarps = 7;
 // (row, head).
 constexpr int kMaxCrossUnitKeys = 256;
 constexpr int kMaxCrossSplits = 32;
+// Join counters per op of a split tensor-core product.
+constexpr int kSplitSlots = 128;
 
 enum OpKind : int {
     kOpEmbed = 0,
@@ -50,7 +52,6 @@ enum OpKind : int {
     kOpLogits = 4,
     kOpNone = 5,
     kOpNorm = 6,
-    kOpReduce = 7,
 };
 enum EpilogueKind : int { kEpQkv = 0, kEpStore = 1, kEpResidual = 2, kEpGelu = 3 };
 
@@ -61,7 +62,7 @@ enum StateWord : int {
     kPosition = 0, kError = 1, kAbort = 2, kStepsDone = 3, kAllEnded = 4,
     kFailKind = 5, kFailCta = 6, kFailWhere = 7, kStateWords = 8
 };
-enum WaitKind : int { kWaitGrid = 1, kWaitUnit = 2, kWaitEmpty = 3, kWaitDrain = 4, kWaitArmed = 5, kWaitGate = 6 };
+enum WaitKind : int { kWaitGrid = 1, kWaitUnit = 2, kWaitEmpty = 3, kWaitDrain = 4, kWaitArmed = 5, kWaitJoin = 6 };
 enum ErrorBit : int { kErrToken = 1, kErrBarrierTimeout = 2 };
 
 // Weight matrices are stored fragment-packed: the 16-row tiles of an [n, kp]
@@ -128,8 +129,9 @@ struct StepOp {
     float* norm_hidden;
     int norm_umma;          // norm: write the tensor-core activation layout
     // Tensor-core products: K splits of each tile's inner size.  With more
-    // than one, each item writes fp32 partials to p.partial_d [split][n_pad]
-    // [rows_pad] and the reduce op after the product sums them in split order
+    // than one (only when all the items fit one wave of CTAs), each item
+    // writes fp32 partials to p.partial_d [split][n_pad][rows_pad], the
+    // tile's splits meet, and each sums its share of the rows in split order
     // and applies the epilogue.
     int ksplit;
 };
@@ -143,6 +145,9 @@ struct StepParams {
     // umma_rows rows (<= 256) of 128 weight rows.
     int umma, act_rows, umma_rows;
     float* partial_d;                   // fp32 split-K partials of a tensor-core product
+    unsigned* split_counters;           // [n_ops][kSplitSlots] split arrivals (zero at launch)
+    int umma_x_stages, umma_x_stage_bytes;  // the activation ring in the work area
+    int umma_blocks;                    // 16 KB weight k-blocks a stream unit carries
     float scale;                        // 1/sqrt(D), on the scores (DecoderShape.cpp:19-26)
     int out_rows, row_step, row_offset; // logits rows: row i reads h row i*row_step + row_offset
 
@@ -202,17 +207,16 @@ __host__ __device__ inline UmmaItem umma_item(const StepParams& p, const StepOp&
     return u;
 }
 
-// One weight-stream unit: a 16-byte aligned source, its size in bytes (low
-// 32 bits of `bytes`) and a gate (high 32 bits): 0, or 1 + the index of the
-// op whose start it waits for -- a unit of activations an earlier op of the
-// same step writes may not be fetched before that op has finished.
+// One weight-stream unit: a 16-byte aligned source and its size in bytes.
+// Units hold what no op of the launch writes (weights, the token table, the
+// cross keys and values), so the producer may fetch them any time ahead.
 struct __align__(16) ScheduleEntry {
     unsigned long long source;
     unsigned long long bytes;
 };
 
-__host__ __device__ inline ScheduleEntry schedule_entry(const void* src, unsigned bytes, unsigned gate = 0) {
-    return ScheduleEntry{(unsigned long long)(size_t)src, (unsigned long long)bytes | ((unsigned long long)gate << 32)};
+__host__ __device__ inline ScheduleEntry schedule_entry(const void* src, unsigned bytes) {
+    return ScheduleEntry{(unsigned long long)(size_t)src, (unsigned long long)bytes};
 }
 
 }  // namespace wsp

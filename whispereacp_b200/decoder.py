@@ -76,10 +76,16 @@ _DTYPES = {np.dtype(np.float32): WSP_FLOAT32, np.dtype(np.float16): WSP_FLOAT16}
 class Decoder:
     """A CUDA decoder for `windows` windows on one device (Decoder.h:49-127)."""
 
+    PRODUCTS = {"auto": 0, "mma": 1, "tcgen05": 2}
+
     def __init__(self, shape: DecoderShape, windows: int = 1, device: int = 0,
-                 storage: str = "float16"):
+                 storage: str = "float16", products: str = "auto"):
+        """products: "auto" (the faster form for the window count), "mma"
+        (mma.sync tiles) or "tcgen05" (tensor-memory tiles)."""
         if storage not in STORAGE:
             raise ValueError(f"storage must be one of {sorted(STORAGE)}")
+        if products not in self.PRODUCTS:
+            raise ValueError(f"products must be one of {sorted(self.PRODUCTS)}")
         self.shape = shape
         self.windows = windows
         self.device = device
@@ -87,8 +93,9 @@ class Decoder:
         self._lib = library()
         handle = ctypes.c_void_p()
         self._shape_c = shape.c()
-        check(self._lib.wsp_decoder_create(ctypes.byref(self._shape_c), device, windows,
-                                           STORAGE[storage], ctypes.byref(handle)))
+        check(self._lib.wsp_decoder_create_products(ctypes.byref(self._shape_c), device, windows,
+                                                    STORAGE[storage], self.PRODUCTS[products],
+                                                    ctypes.byref(handle)))
         self._handle = handle
         self._generation = None
 
