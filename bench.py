@@ -50,6 +50,10 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--tokens", type=int, default=0,
                    help="tokens per window (default: the config's); smaller for profiler captures")
+    p.add_argument("--windows", type=int, default=0,
+                   help="windows per GPU (default: the config's); fewer for profiler captures")
+    p.add_argument("--products", default="auto", choices=["auto", "mma", "tcgen05"],
+                   help="the products' form (default: the decoder's choice for the window count)")
     return p.parse_args()
 
 
@@ -191,7 +195,7 @@ def run_ours(args, run):
     encoder = S.encoder_output(run.windows, shape.cross_positions, shape.width, seed=1 + rank)
     first, later = S.suppression_masks(shape.vocabulary_size)
 
-    decoder = Decoder(shape, windows=run.windows, device=local, storage=run.storage)
+    decoder = Decoder(shape, windows=run.windows, device=local, storage=run.storage, products=args.products)
     decoder.load_weights(tensors)
     decoder.set_generation(run.prompt, first, later, maximum_tokens=tokens_per_window,
                            end_of_text=S.END_OF_TEXT, stop_at_end_of_text=False)
@@ -285,7 +289,8 @@ def run_ours(args, run):
                        "decoder_layers": shape.layers, "vocabulary": shape.vocabulary_size,
                        "step": "sequence start + prompt step + greedy single-token steps (one persistent launch)",
                        "l2": "flushed (256 MiB write) between timed steps, outside the timed intervals",
-                       "parallelism": f"dp{world} (independent windows per GPU)"},
+                       "parallelism": f"dp{world} (independent windows per GPU)",
+                       "products": args.products},
             "batch1_ms_per_token_step": launch_ms / max(1, later_steps),
             "e2e": {"value": tokens / (e2e_step_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -373,8 +378,11 @@ def run_reference(args, run):
 
 def main():
     args = parse_args()
+    from dataclasses import replace
     from whispereacp_b200.synthetic import CONFIGS
     run = CONFIGS[args.config]
+    if args.windows:
+        run = replace(run, windows=args.windows, description=f"{run.description}, run with {args.windows} windows")
     result = run_reference(args, run) if args.impl == "reference" else run_ours(args, run)
     if result is not None:
         print(json.dumps(result), flush=True)
