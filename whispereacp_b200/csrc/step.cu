@@ -1288,6 +1288,120 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
     }
 }
 
+// Self attention with many rows: a warp per (row, head) item, so a CTA has
+// kWarps items' loads in flight instead of one.  64-wide heads.  Scores:
+// eight keys a pass, four lanes a key (32 bytes each, two shuffles to
+// join), four passes' loads issued together; the weights in the warp's
+// score row; values: four keys a pass, a 16-byte piece a lane, eight passes'
+// loads together, the four key slots joined at the end.  Keys and values
+// come through L2 (this launch's q/k/v op wrote the newest ones).
+constexpr int kSelfWarpKeys = 512;  // score row of a warp (>= max_positions)
+
+template <typename WT>
+__device__ void self_attention_warps(const StepParams& p, const StepOp& op, int position, unsigned char* work) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int H = p.heads;
+    float* sc = reinterpret_cast<float*>(work) + warp * kSelfWarpKeys;
+    const int items = p.rows * H;
+    for (int item = blockIdx.x * kWarps + warp; item < items; item += gridDim.x * kWarps) {
+        const int r = item / H, head = item % H;
+        const int b = r / p.tokens, t = r % p.tokens;
+        const int keys = position + t + 1;
+        const WT* K = static_cast<const WT*>(op.keys) + (size_t)b * op.window_stride + head * 64;
+        const WT* V = static_cast<const WT*>(op.values) + (size_t)b * op.window_stride + head * 64;
+        // This lane's quarter of q: dims 16*qd .. 16*qd + 15.
+        const int slot = lane >> 2, qd = lane & 3;
+        float q[16];
+        const float* qrow = p.q + (size_t)r * p.width + head * 64 + 16 * qd;
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(qrow + i));
+            q[i] = v.x * p.scale;
+            q[i + 1] = v.y * p.scale;
+            q[i + 2] = v.z * p.scale;
+            q[i + 3] = v.w * p.scale;
+        }
+        float mx = -INFINITY;
+        for (int j0 = 0; j0 < keys; j0 += 32) {
+            uint4 ka[4], kb[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = min(j0 + 8 * u + slot, keys - 1);
+                const WT* row = K + (size_t)j * op.key_stride + 16 * qd;
+                ka[u] = ld_cg4(row);
+                kb[u] = ld_cg4(row + 8);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = j0 + 8 * u + slot;
+                const float2 a0 = Half16<WT>::pair_to_float2(ka[u].x), a1 = Half16<WT>::pair_to_float2(ka[u].y);
+                const float2 a2 = Half16<WT>::pair_to_float2(ka[u].z), a3 = Half16<WT>::pair_to_float2(ka[u].w);
+                const float2 b0 = Half16<WT>::pair_to_float2(kb[u].x), b1 = Half16<WT>::pair_to_float2(kb[u].y);
+                const float2 b2 = Half16<WT>::pair_to_float2(kb[u].z), b3 = Half16<WT>::pair_to_float2(kb[u].w);
+                float part = q[0] * a0.x + q[1] * a0.y + q[2] * a1.x + q[3] * a1.y + q[4] * a2.x + q[5] * a2.y +
+                             q[6] * a3.x + q[7] * a3.y;
+                part += q[8] * b0.x + q[9] * b0.y + q[10] * b1.x + q[11] * b1.y + q[12] * b2.x + q[13] * b2.y +
+                        q[14] * b3.x + q[15] * b3.y;
+                part += __shfl_xor_sync(0xffffffffu, part, 1);
+                part += __shfl_xor_sync(0xffffffffu, part, 2);
+                if (j < keys) {
+                    if (qd == 0) sc[j] = part;
+                    mx = fmaxf(mx, part);
+                }
+            }
+        }
+        mx = warp_max(mx);
+        __syncwarp();
+        float l = 0.f;
+        for (int j = lane; j < keys; j += 32) {
+            const float e = __expf(sc[j] - mx);
+            sc[j] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        __syncwarp();
+        const int vslot = lane >> 3, piece = lane & 7;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int j0 = 0; j0 < keys; j0 += 32) {
+            uint4 v[8];
+            float w[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int j = j0 + 4 * u + vslot;
+                const int jj = min(j, keys - 1);
+                v[u] = ld_cg4(V + (size_t)jj * op.key_stride + 8 * piece);
+                w[u] = j < keys ? sc[jj] : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float2 f0 = Half16<WT>::pair_to_float2(v[u].x), f1 = Half16<WT>::pair_to_float2(v[u].y);
+                const float2 f2 = Half16<WT>::pair_to_float2(v[u].z), f3 = Half16<WT>::pair_to_float2(v[u].w);
+                acc[0] += w[u] * f0.x;
+                acc[1] += w[u] * f0.y;
+                acc[2] += w[u] * f1.x;
+                acc[3] += w[u] * f1.y;
+                acc[4] += w[u] * f2.x;
+                acc[5] += w[u] * f2.y;
+                acc[6] += w[u] * f3.x;
+                acc[7] += w[u] * f3.y;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 8);
+            acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], 16);
+        }
+        if (vslot == 0) {
+            WT* out = static_cast<WT*>(p.attn16);
+            const float inv = 1.f / l;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                out[act_index(p, r, head * 64 + 8 * piece + i, p.kpd)] = Half16<WT>::from_float(acc[i] * inv);
+        }
+        __syncwarp();
+    }
+}
+
 // ------------------------------------------------------- cross attention
 
 // The keys and values of one (window, layer, head) are one contiguous block
@@ -1756,7 +1870,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
                 if constexpr (UMMA) product_umma<WT>(p, op, position, step, i, s, tm);
                 else op_product<WT, NT>(p, op, position, s, work);
                 break;
-            case kOpSelfAttention: op_self_attention<WT>(p, op, position, work); break;
+            case kOpSelfAttention:
+                // As many items as CTAs or more: a warp per item; fewer: the
+                // whole CTA on each.
+                if (p.head_width == 64 && p.max_positions <= kSelfWarpKeys && p.rows * p.heads >= (int)gridDim.x)
+                    self_attention_warps<WT>(p, op, position, work);
+                else
+                    op_self_attention<WT>(p, op, position, work);
+                break;
             case kOpCrossAttention: op_cross_attention<WT>(p, op, s, work); break;
             case kOpLogits: op_logits<WT, NT>(p, op, position, s, work); break;
             case kOpNorm: op_norm<WT>(p, op, work); break;
@@ -1788,8 +1909,10 @@ size_t work_bytes(const StepParams& p, int max_chunk) {
     const size_t product = (size_t)RT * tile_pitch(p.kpd) * sizeof(WT) +
                            sizeof(float) * (kWarps * 16 * RT + 16 * RT) + (size_t)p.out_rows * 8 +
                            sizeof(float) * 2 * kWarps * RT;
-    const size_t attention = sizeof(float) * std::max<size_t>(kAttentionFixed + std::max(max_chunk, p.max_positions),
-                                                              64 + 32 + 2 * kWarps * 64 + kMaxCrossUnitKeys);
+    const size_t attention =
+        sizeof(float) * std::max<size_t>({(size_t)kAttentionFixed + std::max(max_chunk, p.max_positions),
+                                          (size_t)(64 + 32 + 2 * kWarps * 64 + kMaxCrossUnitKeys),
+                                          (size_t)kWarps * kSelfWarpKeys});
     size_t work = std::max(product, attention);
     // The activation ring of the tensor-core products (1024-byte aligned).
     if (p.umma) work = std::max(work, (size_t)1024 + (size_t)p.umma_x_stages * p.umma_x_stage_bytes);
