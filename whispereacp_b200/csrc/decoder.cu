@@ -910,6 +910,22 @@ private:
     CrossSplit cross_split(int R, int grid, int stage_bytes) const {
         const int D = head_width();
         int chunk = std::max(1, std::min({kMaxCrossUnitKeys, stage_bytes / (4 * D), active_cross_}));
+        // 64-wide heads run 16-key groups, dealt to the kStepWarps warps: a
+        // unit takes as long as its busiest warp, so take the multiple of 16
+        // that best trades the warps' balance against the stage it fills.
+        if (D == 64 && chunk >= 16) {
+            int best = chunk;
+            double best_score = -1.0;
+            for (int c = chunk / 16 * 16; c >= 16; c -= 16) {
+                const int groups = c / 16, rounds = (groups + kStepWarps - 1) / kStepWarps;
+                const double score = (double)groups / (kStepWarps * rounds) * c / chunk;
+                if (score > best_score + 1e-9) {
+                    best_score = score;
+                    best = c;
+                }
+            }
+            chunk = best;
+        }
         // Units start on a multiple of 8 keys: the period of the rotated layout.
         if (chunk < active_cross_) chunk = std::max(8, chunk / 8 * 8);
         const int units = (active_cross_ + chunk - 1) / chunk;
