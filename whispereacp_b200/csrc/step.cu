@@ -749,6 +749,7 @@ constexpr uint32_t kTmemColumns = 256;
 constexpr int kLoadWarp = 5;      // lane 0 fetches the activation blocks
 constexpr int kMaxXStages = 4;
 constexpr int kIssueWarp = 4;  // not one of the epilogue warps 0..3
+constexpr int kJoinBatch = 8;  // split partials a thread loads before summing
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (version 1 for sm_100).
@@ -859,7 +860,10 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
         }
         s.next += (unsigned long long)((nkb + p.umma_blocks - 1) / p.umma_blocks);
         tm.x_next += (unsigned long long)nkb;
-        float* partial = ks > 1 ? p.partial_d + (size_t)u.split * m_tiles * 128 * row_stride : nullptr;
+        // Partials are [split][row][weight row]: a warp's lanes (consecutive
+        // weight rows) store one row's 128 contiguous bytes at a time.
+        const int ncols = m_tiles * 128;
+        float* partial = ks > 1 ? p.partial_d + (size_t)u.split * row_stride * ncols : nullptr;
         if (warp < 4) {
             Trace tr = trace_of(p.profile);
             tr.begin();
@@ -872,10 +876,10 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
                 uint32_t v[32];
                 tmem_load32(tm.base + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
                 if (partial) {
-                    float* row = partial + (size_t)n * row_stride + r0 + c0;
+                    float* col = partial + (size_t)(r0 + c0) * ncols + n;
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        if (c0 + j < rows) row[j] = __uint_as_float(v[j]);
+                        if (c0 + j < rows) col[(size_t)j * ncols] = __uint_as_float(v[j]);
                 } else if (n < op.n) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
@@ -888,8 +892,9 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
         tm.phase ^= 1u;
         if (ks > 1) {
             // The tile's splits (each on its own CTA: a split product's items
-            // fit one wave) meet here; then each joins the rows n % ks ==
-            // split of the tile, summing the partials in split order.
+            // fit one wave) meet here; then each joins a contiguous share of
+            // the tile's (row, weight row) elements, summing the partials in
+            // split order.
             __threadfence();
             consumer_sync();
             if (threadIdx.x == 0) {
@@ -911,34 +916,36 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
             }
             consumer_sync();
             if (join_ok) {
-                // Four elements a thread at a time, every split's load of all
-                // four issued before any sum, so the join costs a few L2
-                // round trips rather than one per element.
-                const int share = (128 - u.split + ks - 1) / ks;  // rows u.split, u.split + ks, ... of 128
-                const size_t split_stride = (size_t)m_tiles * 128 * row_stride;
-                const int total = share * rows;
-                for (int e0 = threadIdx.x; e0 < total; e0 += 4 * kThreads) {
+                // Four adjacent weight rows a thread, and up to kJoinBatch
+                // splits' loads in flight before any sum: a few L2 round trips
+                // per element rather than one per split.
+                const int elems = rows * 128;
+                const int per = ((elems + ks - 1) / ks + 3) & ~3;
+                const int f1 = min((u.split + 1) * per, elems);
+                const size_t split_stride = (size_t)row_stride * ncols;
+                for (int f = u.split * per + 4 * threadIdx.x; f < f1; f += 4 * kThreads) {
+                    const int t = f >> 7, nl = f & 127;
+                    const float* at = p.partial_d + (size_t)(r0 + t) * ncols + m * 128 + nl;
                     float sum[4] = {0.f, 0.f, 0.f, 0.f};
-                    const float* at[4];
+                    for (int sp0 = 0; sp0 < ks; sp0 += kJoinBatch) {
+                        float4 v[kJoinBatch];
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int e = min(e0 + k * kThreads, total - 1);
-                        at[k] = p.partial_d + (size_t)(m * 128 + u.split + (e / rows) * ks) * row_stride + r0 + e % rows;
+                        for (int k = 0; k < kJoinBatch; ++k)
+                            if (sp0 + k < ks) v[k] = __ldcg(reinterpret_cast<const float4*>(at + (sp0 + k) * split_stride));
+#pragma unroll
+                        for (int k = 0; k < kJoinBatch; ++k)
+                            if (sp0 + k < ks) {
+                                sum[0] += v[k].x;
+                                sum[1] += v[k].y;
+                                sum[2] += v[k].z;
+                                sum[3] += v[k].w;
+                            }
                     }
-                    for (int sp = 0; sp < ks; ++sp) {
-                        float v[4];
 #pragma unroll
-                        for (int k = 0; k < 4; ++k) v[k] = ld_cg(at[k] + sp * split_stride);
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) sum[k] += v[k];
-                    }
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int e = e0 + k * kThreads;
-                        if (e >= total) break;
-                        const int n = m * 128 + u.split + (e / rows) * ks, t = e % rows;
+                    for (int e = 0; e < 4; ++e) {
+                        const int n = m * 128 + nl + e;
                         if (n < op.n)
-                            emit_output<WT>(p, op, position, n, r0 + t, sum[k] + (op.bias ? __ldg(op.bias + n) : 0.f));
+                            emit_output<WT>(p, op, position, n, r0 + t, sum[e] + (op.bias ? __ldg(op.bias + n) : 0.f));
                     }
                 }
             }
@@ -1617,7 +1624,7 @@ template <typename WT>
 __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t4 = lane & 3;
-    const bool row0 = lane < 4;
+    const bool row0 = lane < 4, pair = lane < 8;
     const int H = p.heads, S = op.splits;
     const int units = cross_units(op);
     const int items = p.rows * H * S;
@@ -1632,14 +1639,19 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
         consumer_sync();
         if (threadIdx.x < 64) q[threadIdx.x] = ld_cg(p.q + (size_t)r * p.width + head * 64 + threadIdx.x) * p.scale;
         consumer_sync();
-        uint32_t qh[4][2], ql[4][2];
+        // Row 0 of A is q's hi half, row 1 its lo half (lanes 4..7), so one
+        // product gives both, and the two rows add after the chain.
+        uint32_t qa[4][2];
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-            if (row0) {
-                split_pair<WT>(q[16 * kk + 2 * t4], q[16 * kk + 2 * t4 + 1], qh[kk][0], ql[kk][0]);
-                split_pair<WT>(q[16 * kk + 2 * t4 + 8], q[16 * kk + 2 * t4 + 9], qh[kk][1], ql[kk][1]);
+            if (pair) {
+                uint32_t h0, l0, h1, l1;
+                split_pair<WT>(q[16 * kk + 2 * t4], q[16 * kk + 2 * t4 + 1], h0, l0);
+                split_pair<WT>(q[16 * kk + 2 * t4 + 8], q[16 * kk + 2 * t4 + 9], h1, l1);
+                qa[kk][0] = row0 ? h0 : l0;
+                qa[kk][1] = row0 ? h1 : l1;
             } else {
-                qh[kk][0] = qh[kk][1] = ql[kk][0] = ql[kk][1] = 0u;
+                qa[kk][0] = qa[kk][1] = 0u;
             }
         }
         float m_w = -INFINITY, l_w = 0.f;
@@ -1655,31 +1667,41 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
             Trace tr = trace_of(p.profile);
             tr.begin();
             for (int n0 = 16 * warp; n0 < n; n0 += 16 * kWarps) {
+                // Even and odd key pieces accumulate apart: four chains of two
+                // products, summed after.
                 float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+                float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
                 {
                     // Keys n0 + 8*(mi/2) + rr, key pieces 2kk + mi%2 (rows past
                     // the unit's keys read its last key; their scores are dropped).
                     const int key = min(n0 + 8 * (mi >> 1) + rr, n - 1);
+                    uint32_t b[4][4];
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        ldmatrix_x4(b[kk], rows + (size_t)key * 128 + cross_piece(2 * kk + (mi & 1), key) * 8);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        uint32_t b[4];
-                        ldmatrix_x4(b, rows + (size_t)key * 128 + cross_piece(2 * kk + (mi & 1), key) * 8);
-                        const uint32_t ah[4] = {qh[kk][0], 0u, qh[kk][1], 0u};
-                        const uint32_t al[4] = {ql[kk][0], 0u, ql[kk][1], 0u};
-                        const uint32_t b0[2] = {b[0], b[1]}, b1[2] = {b[2], b[3]};
-                        mma_16816<WT>(s0, ah, b0);
-                        mma_16816<WT>(s1, ah, b1);
-                        mma_16816<WT>(s0, al, b0);
-                        mma_16816<WT>(s1, al, b1);
+                        const uint32_t a[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
+                        const uint32_t b0[2] = {b[kk][0], b[kk][1]}, b1[2] = {b[kk][2], b[kk][3]};
+                        mma_16816<WT>(kk & 1 ? t0 : s0, a, b0);
+                        mma_16816<WT>(kk & 1 ? t1 : s1, a, b1);
                     }
                 }
-                // Row 0: keys n0+2t, n0+2t+1 (s0) and n0+8+2t, n0+9+2t (s1).
+                // Rows 0 (hi, lanes 0..3) and 1 (lo, lanes 4..7): keys n0+2t,
+                // n0+2t+1 (s0) and n0+8+2t, n0+9+2t (s1).  Their sum reaches
+                // lanes 0..7 alike.
+                float sc[4] = {s0[0] + t0[0], s0[1] + t0[1], s1[0] + t1[0], s1[1] + t1[1]};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float other = __shfl_xor_sync(0xffffffffu, sc[i], 4);
+                    sc[i] = row0 ? sc[i] + other : other + sc[i];
+                }
                 const int ka = n0 + 2 * t4;
                 float v[4];
-                v[0] = row0 && ka < n ? s0[0] : -INFINITY;
-                v[1] = row0 && ka + 1 < n ? s0[1] : -INFINITY;
-                v[2] = row0 && ka + 8 < n ? s1[0] : -INFINITY;
-                v[3] = row0 && ka + 9 < n ? s1[1] : -INFINITY;
+                v[0] = pair && ka < n ? sc[0] : -INFINITY;
+                v[1] = pair && ka + 1 < n ? sc[1] : -INFINITY;
+                v[2] = pair && ka + 8 < n ? sc[2] : -INFINITY;
+                v[3] = pair && ka + 9 < n ? sc[3] : -INFINITY;
                 float gm = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
                 gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
                 gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 2));
@@ -1700,30 +1722,37 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
                     o[i][0] *= keep;
                     o[i][1] *= keep;
                 }
+                // P likewise: its hi half as row 0, its lo half as row 1; the
+                // two output rows add once per item.
                 uint32_t ph0, pl0, ph2, pl2;
                 split_pair<WT>(e[0], e[1], ph0, pl0);
                 split_pair<WT>(e[2], e[3], ph2, pl2);
-                const uint32_t ah[4] = {row0 ? ph0 : 0u, 0u, row0 ? ph2 : 0u, 0u};
-                const uint32_t al[4] = {row0 ? pl0 : 0u, 0u, row0 ? pl2 : 0u, 0u};
+                const uint32_t a[4] = {pair ? (row0 ? ph0 : pl0) : 0u, 0u, pair ? (row0 ? ph2 : pl2) : 0u, 0u};
                 {
                     // Keys n0 + 8*(mi%2) + rr, value pieces 8 + 2cc + mi/2.
                     const int key = min(n0 + 8 * (mi & 1) + rr, n - 1);
+                    uint32_t b[4][4];
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc)
+                        ldmatrix_x4_trans(b[cc], rows + (size_t)key * 128 + cross_piece(8 + 2 * cc + (mi >> 1), key) * 8);
 #pragma unroll
                     for (int cc = 0; cc < 4; ++cc) {
-                        uint32_t b[4];
-                        ldmatrix_x4_trans(b, rows + (size_t)key * 128 + cross_piece(8 + 2 * cc + (mi >> 1), key) * 8);
-                        const uint32_t b0[2] = {b[0], b[1]}, b1[2] = {b[2], b[3]};
-                        mma_16816<WT>(o[2 * cc], ah, b0);
-                        mma_16816<WT>(o[2 * cc], al, b0);
-                        mma_16816<WT>(o[2 * cc + 1], ah, b1);
-                        mma_16816<WT>(o[2 * cc + 1], al, b1);
+                        const uint32_t b0[2] = {b[cc][0], b[cc][1]}, b1[2] = {b[cc][2], b[cc][3]};
+                        mma_16816<WT>(o[2 * cc], a, b0);
+                        mma_16816<WT>(o[2 * cc + 1], a, b1);
                     }
                 }
             }
             tr.end(kTrAttention);
             release_unit(s);
         }
-        // Join the warps' softmaxes.
+        // Rows 0 and 1 of the output (P's hi and lo halves) add; then the
+        // warps' softmaxes join.
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            o[i][0] += __shfl_xor_sync(0xffffffffu, o[i][0], 4);
+            o[i][1] += __shfl_xor_sync(0xffffffffu, o[i][1], 4);
+        }
         if (lane == 0) {
             wmax[warp] = m_w;
             wsum[warp] = l_w;
