@@ -223,6 +223,16 @@ int wsp_decoder_time_barriers(wsp_decoder* decoder, int count, float* microsecon
 int wsp_decoder_trace_cycles(const wsp_decoder* decoder, double* cycles, int count);
 
 /*
+ * Microseconds of each op of the decode step's op list (its work and the
+ * grid barrier after it, from CTA 0's clock) and the op's kind (0 embed,
+ * 1 product, 2 self attention, 3 cross attention, 4 logits, 6 layer norm),
+ * averaged over the last wsp_decoder_time_kernels run.  Fills up to
+ * `capacity` entries of each array (either may be NULL) and sets *count to
+ * the ops in the list.  Measurement only; no counterpart in the reference.
+ */
+int wsp_decoder_op_times(const wsp_decoder* decoder, float* microseconds, int* kinds, int capacity, int* count);
+
+/*
  * Milliseconds of the last transcription's three phases, from CUDA events on
  * the decoder's stream: ms[0] the sequence start (encoder-row narrowing and
  * the cross K/V product), ms[1] the prompt step's launch, ms[2] the launch

@@ -81,6 +81,7 @@ SIGNATURES = {
     "wsp_decoder_time_kernels": ([_P, _I, _P, _P], _I),
     "wsp_decoder_time_barriers": ([_P, _I, ctypes.POINTER(ctypes.c_float)], _I),
     "wsp_decoder_trace_cycles": ([_P, ctypes.POINTER(ctypes.c_double), _I], _I),
+    "wsp_decoder_op_times": ([_P, _P, _P, _I, _P], _I),
     "wsp_decoder_step_launches": ([_P, ctypes.POINTER(_I)], _I),
     "wsp_decoder_phase_ms": ([_P, ctypes.POINTER(ctypes.c_float)], _I),
     "wsp_argmax": ([_P, _P, _P, _I, _I, _P], _I),

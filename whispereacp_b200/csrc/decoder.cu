@@ -534,10 +534,14 @@ public:
                                        kTraceSections * sizeof(unsigned long long), cudaMemcpyDeviceToHost, stream_));
             CUDA_CHECK(cudaStreamSynchronize(stream_));
             for (int t = 0; t < kTraceSections; ++t) trace_cycles_[t] += (double)sections[t] / steps;
+            if (i == 0) op_us_.assign(ops.size(), 0.0);
+            op_kinds_.resize(ops.size());
             for (size_t o = 0; o < ops.size(); ++o) {
                 const int cls = op_class(ops[o].kind);
                 total[cls] += (stamps[o + 1] - stamps[o]) * 1e-6;
                 count[cls] += 1;
+                op_kinds_[o] = ops[o].kind;
+                if (o < op_us_.size()) op_us_[o] += (stamps[o + 1] - stamps[o]) * 1e-3 / steps;
             }
             ++position_;
         }
@@ -576,6 +580,16 @@ public:
         check_device_errors();
         // The first barrier also absorbs the launch's start-up skew.
         return count > 1 ? (float)((stamps[count] - stamps[1]) * 1e-3 / (count - 1)) : 0.f;
+    }
+
+    // Microseconds of each op of the step (its work and the grid barrier
+    // after it) and its kind, averaged over the last time_kernels run.
+    int op_times(float* us, int* kinds, int capacity) const {
+        for (int i = 0; i < capacity && i < (int)op_us_.size(); ++i) {
+            if (us) us[i] = (float)op_us_[i];
+            if (kinds) kinds[i] = op_kinds_[i];
+        }
+        return (int)op_us_.size();
     }
 
     // Section cycles of CTA 0 per step, from the last time_kernels run.
@@ -717,6 +731,11 @@ private:
         attended_.allocate(A * padded(d) * 2);
         feed_forward_.allocate(A * padded(f) * 2);
         partial_.allocate(R * H * kMaxCrossSplits * (D + 2) * 4);
+        // Fused out-projections (a few rows): the heads' partial rows of the
+        // self and the cross attention, and the residual rows between them.
+        const size_t Rf = std::min<size_t>(R, kInlineNormRows);
+        out_partials_.allocate(2 * H * Rf * d * 4);
+        hidden_mid_.allocate(Rf * d * 4);
         const size_t grid = (size_t)kMaxBlocksPerSm * sm_count_;
         candidate_values_.allocate(R * grid * 4);
         candidate_indices_.allocate(R * grid * 4);
@@ -763,6 +782,7 @@ private:
     // capacity (the self attention holds max_positions scores).
     static constexpr int kMaxCrossChunk = 0;
     static constexpr int kMaxBlocksPerSm = 2;
+    static constexpr int kStaticSharedBytes = 2048;
 
     // The step: recordDecoderStep (Decoder.cpp:151-177) with decoderLayer
     // (Decoder.cpp:73-115), lowered onto the ops of step.cuh.
@@ -801,6 +821,16 @@ private:
         const size_t elem = 2;
         const size_t self_layer = (size_t)windows_ * shape_.max_positions * d * elem;
         const CrossSplit cs = cross_split(R, grid, stage_bytes);
+        // A few rows, 64-wide heads, mma.sync products, every (row, head) on a
+        // CTA of its own: each attention op applies its heads' out-projection
+        // shares itself, and the LayerNorm prologue of the op after it adds
+        // them to h (in head order, with the bias); the cross attention
+        // computes its own queries -- three grid-wide phases fewer per layer.
+        // h holds a layer's input and output rows, hidden_mid_ the rows
+        // between its self and cross attention.
+        const bool fuse_out = !umma_ && R <= kInlineNormRows && d == 64 * H && (long long)R * H < grid;
+        float* self_partials = out_partials_.get<float>();
+        float* cross_partials = self_partials + (size_t)H * std::min(R, kInlineNormRows) * d;
         std::vector<StepOp> ops;
         StepOp e{};
         e.kind = kOpEmbed;
@@ -832,21 +862,41 @@ private:
             self.values = qkv.self_values;
             self.key_stride = d;
             self.window_stride = (long long)shape_.max_positions * d;
+            if (fuse_out) {
+                self.out_weight = W.o_w.get();
+                self.out_partial = self_partials;
+            }
             ops.push_back(self);
-            StepOp out = product(kEpResidual, W.o_w, d, kpd, W.o_b);
-            out.input16 = attended_.get();
-            out.ld_input = kpd;
-            out.out = hidden_.get();
-            out.ld_out = d;
-            ops.push_back(out);
+            if (!fuse_out) {
+                StepOp out = product(kEpResidual, W.o_w, d, kpd, W.o_b);
+                out.input16 = attended_.get();
+                out.ld_input = kpd;
+                out.out = hidden_.get();
+                out.ld_out = d;
+                ops.push_back(out);
+            }
             // h += out_proj(cross_attention(encoder_attn_layer_norm(h)))  (Decoder.cpp:93-104)
-            StepOp cq = product(kEpStore, W.qc_w, H * (int)round16(D), kpd, W.qc_b);
-            cq.slice = D;
-            normalised_input(ops, cq, W.ln2_w, W.ln2_b, R);
-            cq.out = queries_.get();
-            cq.ld_out = d;
-            ops.push_back(cq);
             StepOp cross{};
+            if (fuse_out) {
+                // The cross attention computes its own queries: LN2 of h plus
+                // the self attention's partials (the residual, kept in
+                // hidden_mid_), then the head's q rows of W_q.
+                cross = product(kEpStore, W.qc_w, H * (int)round16(D), kpd, W.qc_b);
+                cross.gamma = W.ln2_w.get<float>();
+                cross.beta = W.ln2_b.get<float>();
+                cross.addends = self_partials;
+                cross.addend_count = H;
+                cross.addend_stride = (long long)R * d;
+                cross.addend_bias = W.o_b.get<float>();
+                cross.sum_out = hidden_mid_.get<float>();
+            } else {
+                StepOp cq = product(kEpStore, W.qc_w, H * (int)round16(D), kpd, W.qc_b);
+                cq.slice = D;
+                normalised_input(ops, cq, W.ln2_w, W.ln2_b, R);
+                cq.out = queries_.get();
+                cq.ld_out = d;
+                ops.push_back(cq);
+            }
             cross.kind = kOpCrossAttention;
             const long long head_block = (long long)shape_.cross_positions * 2 * D;
             cross.keys = cross_kv_.get<char>() + (size_t)l * H * head_block * elem;
@@ -858,16 +908,30 @@ private:
             cross.span = cs.span;
             cross.splits = cs.splits;
             cross.value_bias = W.vc_b.get<float>();
+            if (fuse_out) {
+                cross.out_weight = W.oc_w.get();
+                cross.out_partial = cross_partials;
+            }
             ops.push_back(cross);
-            StepOp cout = product(kEpResidual, W.oc_w, d, kpd, W.oc_b);
-            cout.input16 = attended_.get();
-            cout.ld_input = kpd;
-            cout.out = hidden_.get();
-            cout.ld_out = d;
-            ops.push_back(cout);
+            if (!fuse_out) {
+                StepOp cout = product(kEpResidual, W.oc_w, d, kpd, W.oc_b);
+                cout.input16 = attended_.get();
+                cout.ld_input = kpd;
+                cout.out = hidden_.get();
+                cout.ld_out = d;
+                ops.push_back(cout);
+            }
             // h += fc2(gelu(fc1(final_layer_norm(h))))  (Decoder.cpp:106-114)
             StepOp up = product(kEpGelu, W.fc1_w, f, kpd, W.fc1_b);
             normalised_input(ops, up, W.ln3_w, W.ln3_b, R);
+            if (fuse_out) {
+                up.norm_input = hidden_mid_.get<float>();
+                up.addends = cross_partials;
+                up.addend_count = H;
+                up.addend_stride = (long long)R * d;
+                up.addend_bias = W.oc_b.get<float>();
+                up.sum_out = hidden_.get<float>();
+            }
             up.out = feed_forward_.get();
             up.ld_out = kpf;
             ops.push_back(up);
@@ -1025,7 +1089,9 @@ private:
     void configure_stream(bool half, StepParams& p) const {
         p.stage_bytes = stage_bytes_for_width();
         const size_t work = decode_work_bytes(half, p, kMaxCrossChunk);
-        const long long room = (long long)max_shared_ - (long long)work;
+        // (The kernel's static shared memory -- barriers, flags, a fused
+        // out-projection's input row -- comes out of the same budget.)
+        const long long room = (long long)max_shared_ - kStaticSharedBytes - (long long)work;
         p.stages = (int)std::min<long long>(8, room / p.stage_bytes);
         if (p.stages < 2) throw CudaFailure("the decode kernel's shared memory does not fit", false);
     }
@@ -1249,6 +1315,7 @@ private:
     DeviceBuffer self_keys_, self_values_, cross_kv_, encoder_staging_, encoder16_;
     DeviceBuffer ring_, ring_prompt_, state_, masks_;
     DeviceBuffer hidden_, queries_, normalised_, attended_, feed_forward_, partial_, partial_d_, split_counters_;
+    DeviceBuffer out_partials_, hidden_mid_;
     DeviceBuffer candidate_values_, candidate_indices_, row_tokens_, counters_;
     DeviceBuffer barrier_, ended_, profile_;
     DeviceBuffer logits_staging_, hidden_staging_;
@@ -1272,6 +1339,8 @@ private:
     bool generation_set_ = false;
     int sampled_steps_ = 0;
     std::vector<double> trace_cycles_;
+    std::vector<double> op_us_;
+    std::vector<int> op_kinds_;
     static constexpr int kTraceOffset = 512;   // kTraceBase of step.cu
     static constexpr int kTraceSections = 7;
     int queued_steps_ = 0;
@@ -1460,6 +1529,14 @@ int wsp_decoder_trace_cycles(const wsp_decoder* decoder, double* cycles, int cou
         WSP_NEED(decoder);
         if (!cycles || count < 0) throw wsp::InvalidArgument("cycles is NULL");
         decoder->impl->trace_cycles(cycles, count);
+    });
+}
+
+int wsp_decoder_op_times(const wsp_decoder* decoder, float* microseconds, int* kinds, int capacity, int* count) {
+    return guarded([&] {
+        WSP_NEED(decoder);
+        if (capacity < 0 || !count) throw wsp::InvalidArgument("count is NULL or capacity negative");
+        *count = decoder->impl->op_times(microseconds, kinds, capacity);
     });
 }
 

@@ -68,8 +68,9 @@ inline void append_region(const Region& r, int stage_chunks, std::vector<Schedul
 }
 
 // Cross attention: the CTA's items (cta, cta + grid, ...), each item's
-// units (one per `chunk` keys) in order, as op_cross_attention reads them.
-inline void append_cross_units(const StepParams& p, const StepOp& op, int cta, int grid,
+// units (one per `chunk` keys) in order, as op_cross_attention reads them;
+// with a fused query, the head's q weight tiles before them.
+inline void append_cross_units(const StepParams& p, const StepOp& op, int cta, int grid, int stage_chunks,
                                std::vector<ScheduleEntry>& out) {
     const int S = op.splits, H = p.heads;
     const int items = p.rows * H * S;
@@ -78,6 +79,14 @@ inline void append_cross_units(const StepParams& p, const StepOp& op, int cta, i
     for (int it = cta; it < items; it += grid) {
         const int split = it % S, head = (it / S) % H, r = it / (S * H), b = r / p.tokens;
         const int count = std::max(0, std::min(op.span, units - split * op.span));
+        if (op.weight) {
+            // A fused query: the head's 16-row q tiles first (cross_query).
+            const int head_tiles = schedule_round16(p.head_width) / 16;
+            append_region(Region{static_cast<const unsigned char*>(op.weight) +
+                                     (size_t)head * head_tiles * (op.kp / 32) * 1024,
+                                 head_tiles, op.kp / 32, 1},
+                          stage_chunks, out);
+        }
         for (int t = 0; t < count; ++t) {
             const int k0 = (split * op.span + t) * op.chunk;
             const int n = std::min(op.chunk, op.key_count - k0);
@@ -119,7 +128,7 @@ inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, 
     for (int cta = 0; cta < grid; ++cta) {
         for (const StepOp& op : ops) {
             if (op.kind == kOpCrossAttention) {
-                append_cross_units(p, op, cta, grid, units);
+                append_cross_units(p, op, cta, grid, stage_chunks, units);
                 continue;
             }
             if (op.kind == kOpProduct && p.umma) {

@@ -135,35 +135,47 @@ constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
 constexpr unsigned long long kAbortLookNs = 50000ull;          // 50 us
 
 // A monotonic arrival counter: each CTA adds one with release semantics and
-// waits, with acquire loads, until every CTA has arrived `epoch` times.  The
-// wait gives up after kWaitTimeoutNs (or as soon as another CTA gave up): it
-// records kErrBarrierTimeout, raises the abort word and the kernel returns.
-// Records the first wait that gave up: its kind, CTA and op/unit index.
-__device__ __forceinline__ void record_timeout(int* state, int kind, long long where) {
-    atomicOr(state + kError, kErrBarrierTimeout);
-    if (atomicCAS(state + kFailKind, 0, kind) == 0) {
-        state[kFailCta] = (int)blockIdx.x;
-        state[kFailWhere] = (int)where;
+// polls with acquire loads, nothing else in flight, until every CTA has
+// arrived `epoch` times.  A wait that gives up anywhere in the kernel
+// (record_timeout) also adds kAbortBias to the counter, so every CTA polling
+// it sees the failure on the same load that would have seen the barrier
+// complete -- no second word to read per poll or per barrier.  The poll
+// reads the clock every 32 loads and gives up after kWaitTimeoutNs: it
+// records kErrBarrierTimeout and the kernel returns.  (Arrivals per launch
+// stay far below the bias: steps x ops x CTAs < 2^30.)
+constexpr unsigned kAbortBias = 1u << 30;
+
+// Records the first wait that gave up: its kind, CTA and op/unit index; then
+// raises the abort word (read by long ring waits) and the barrier's bias.
+__device__ __forceinline__ void record_timeout(const StepParams& p, int kind, long long where) {
+    atomicOr(p.state + kError, kErrBarrierTimeout);
+    if (atomicCAS(p.state + kFailKind, 0, kind) == 0) {
+        p.state[kFailCta] = (int)blockIdx.x;
+        p.state[kFailWhere] = (int)where;
     }
-    atomicExch(state + kAbort, 1);
+    // The first to give up adds the bias, once: more would wrap the counter.
+    if (atomicExch(p.state + kAbort, 1) == 0) atomicAdd(p.barrier, kAbortBias);
 }
 
-__device__ bool grid_barrier(unsigned* count, unsigned& epoch, int* state) {
+__device__ bool grid_barrier(const StepParams& p, unsigned& epoch) {
     __shared__ int aborted;
     consumer_sync();
     ++epoch;
     if (threadIdx.x == 0) {
-        asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(count), "r"(1u) : "memory");
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p.barrier), "r"(1u) : "memory");
         const unsigned target = epoch * gridDim.x;
-        const unsigned long long start = global_ns();
-        while (ld_acquire(count) < target) {
-            if (ld_volatile(state + kAbort)) break;
-            if (global_ns() - start > kWaitTimeoutNs) {
-                record_timeout(state, kWaitGrid, (long long)epoch);
-                break;
+        unsigned seen = ld_acquire(p.barrier);
+        if (seen < target) {
+            const unsigned long long start = global_ns();
+            for (unsigned spin = 1; (seen = ld_acquire(p.barrier)) < target; ++spin) {
+                if ((spin & 31) == 0 && global_ns() - start > kWaitTimeoutNs) {
+                    record_timeout(p, kWaitGrid, (long long)epoch);
+                    seen = kAbortBias;
+                    break;
+                }
             }
         }
-        aborted = ld_volatile(state + kAbort);
+        aborted = seen >= kAbortBias;
     }
     consumer_sync();
     return aborted == 0;
@@ -218,7 +230,7 @@ __device__ bool wait_parity(const StepParams& p, uint64_t* bar, uint32_t parity,
         if ((spin & 15) != 0) continue;
         const unsigned long long waited = global_ns() - start;
         if (waited > kWaitTimeoutNs) {
-            record_timeout(p.state, kind, (long long)index);
+            record_timeout(p, kind, (long long)index);
             return false;
         }
         // A wait this long may be one another wait's failure left
@@ -254,7 +266,7 @@ __device__ __forceinline__ const unsigned char* owned_unit_at(const StepParams& 
         const unsigned long long start = global_ns();
         while (*s.armed <= index) {
             if (global_ns() - start > kWaitTimeoutNs) {
-                record_timeout(p.state, kWaitArmed, (long long)index);
+                record_timeout(p, kWaitArmed, (long long)index);
                 break;
             }
         }
@@ -342,14 +354,56 @@ __device__ void op_embed(const StepParams& p, int position) {
 
 constexpr int kNormMaxPerLane = 48;  // widths up to 1536
 
+// Terms added to a LayerNorm's input rows before normalising: the bias and
+// count partial rows (stride floats apart, row-major [R][d] each), summed in
+// order; sum_out, when given, receives the sums (the new residual rows).
+struct Addends {
+    const float* base = nullptr;
+    int count = 0;
+    long long stride = 0;
+    const float* bias = nullptr;
+    float* sum_out = nullptr;
+};
+
+// v[i] (element c0 + i*step of row `row`, i < N, columns below d) plus the
+// addends, every load of a batch of four partial rows in flight at once.
+template <int N>
+__device__ __forceinline__ void add_addends(const Addends& a, size_t row, int d, int c0, int step, float (&v)[N]) {
+    const float* rowp = a.base + row * d;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const int c = c0 + i * step;
+        if (c < d) v[i] += __ldg(a.bias + c);
+    }
+    // Four partial rows a batch for a few values a thread; one for many (a
+    // row's own loads are then plenty in flight).
+    constexpr int kBatch = N <= 8 ? 4 : 1;
+    for (int j0 = 0; j0 < a.count; j0 += kBatch) {
+        float t[kBatch][N];
+#pragma unroll
+        for (int jj = 0; jj < kBatch; ++jj)
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+                const int c = c0 + i * step;
+                t[jj][i] = j0 + jj < a.count && c < d ? ld_cg(rowp + (size_t)(j0 + jj) * a.stride + c) : 0.f;
+            }
+#pragma unroll
+        for (int jj = 0; jj < kBatch; ++jj)
+#pragma unroll
+            for (int i = 0; i < N; ++i) v[i] += t[jj][i];
+    }
+}
+
 // LayerNorm of rows_in_tile rows of h into the 16-bit tile xs [rows][ldx]:
 // output row rl reads h row (r0 + rl)*row_step + row_offset.  One warp a row,
 // the row in registers: the mean, then the centred variance, as
 // LayerNorm.h:19-98 does.  hidden_out, when given, receives the fp32 rows.
+// With addends, each row is first input + bias + the partial rows (the
+// residual additions of a fused out-projection, Decoder.cpp:80-104).
 template <typename WT>
 __device__ void layer_norm_tile(const StepParams& p, const float* input, const float* gamma, const float* beta,
                                 int r0, int rows_in_tile, int row_step, int row_offset, WT* xs, int ldx,
-                                float* hidden_out) {
+                                float* hidden_out, const Addends& add = Addends()) {
     const int d = p.width;
     if (rows_in_tile <= 2) {
         // A row or two: the whole CTA on each row, every load of the row,
@@ -357,7 +411,8 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
         __shared__ float scratch[kWarps];
         constexpr int kPer = (1536 + kThreads - 1) / kThreads;
         for (int rl = 0; rl < rows_in_tile; ++rl) {
-            const float* x = input + ((size_t)(r0 + rl) * row_step + row_offset) * d;
+            const size_t row = (size_t)(r0 + rl) * row_step + row_offset;
+            const float* x = input + row * d;
             float v[kPer], g[kPer], b[kPer];
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
@@ -365,6 +420,16 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
                 v[i] = c < d ? ld_cg(x + c) : 0.f;
                 g[i] = c < d ? __ldg(gamma + c) : 0.f;
                 b[i] = c < d ? __ldg(beta + c) : 0.f;
+            }
+            if (add.count > 0) {
+                add_addends<kPer>(add, row, d, threadIdx.x, kThreads, v);
+                if (add.sum_out) {
+#pragma unroll
+                    for (int i = 0; i < kPer; ++i) {
+                        const int c = threadIdx.x + i * kThreads;
+                        if (c < d) add.sum_out[row * d + c] = v[i];
+                    }
+                }
             }
             float total = 0.f;
 #pragma unroll
@@ -395,12 +460,23 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
     // More rows: one warp a row, the row in registers.
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int rl = warp; rl < rows_in_tile; rl += kWarps) {
-        const float* x = input + ((size_t)(r0 + rl) * row_step + row_offset) * d;
+        const size_t row = (size_t)(r0 + rl) * row_step + row_offset;
+        const float* x = input + row * d;
         float v[kNormMaxPerLane];
 #pragma unroll
         for (int i = 0; i < kNormMaxPerLane; ++i) {
             const int c = lane + 32 * i;
             v[i] = c < d ? ld_cg(x + c) : 0.f;
+        }
+        if (add.count > 0) {
+            add_addends<kNormMaxPerLane>(add, row, d, lane, 32, v);
+            if (add.sum_out) {
+#pragma unroll
+                for (int i = 0; i < kNormMaxPerLane; ++i) {
+                    const int c = lane + 32 * i;
+                    if (c < d) add.sum_out[row * d + c] = v[i];
+                }
+            }
         }
         float total = 0.f;
 #pragma unroll
@@ -692,8 +768,17 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
                 consumer_sync();
                 Trace trn = trace_of(p.profile);
                 trn.begin();
-                if (normalise)
-                    layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, r0, rows_valid, 1, 0, xs, pitch, nullptr);
+                if (normalise) {
+                    // The residual additions of a fused out-projection; the
+                    // CTA holding the row tile's first weight tile keeps them.
+                    Addends add;
+                    if (op.addend_count > 0) {
+                        add = Addends{op.addends, op.addend_count, op.addend_stride, op.addend_bias,
+                                      blockIdx.x == (unsigned)((r_tile * n_tiles) % gridDim.x) ? op.sum_out : nullptr};
+                    }
+                    layer_norm_tile<WT>(p, op.norm_input ? op.norm_input : p.h, op.gamma, op.beta, r0, rows_valid,
+                                        1, 0, xs, pitch, nullptr, add);
+                }
                 else
                     stage_rows<WT>(static_cast<const WT*>(op.input16), op.ld_input, r0, rows_valid, op.kp, xs, pitch);
                 consumer_sync();
@@ -907,7 +992,7 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
                     if ((spin & 15) != 0) continue;
                     if (ld_volatile(p.state + kAbort)) { ok = 0; break; }
                     if (global_ns() - start > kWaitTimeoutNs) {
-                        record_timeout(p.state, kWaitJoin, (long long)item);
+                        record_timeout(p, kWaitJoin, (long long)item);
                         ok = 0;
                         break;
                     }
@@ -1145,6 +1230,69 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
     }
 }
 
+// ------------------------------------------------ fused out-projection
+
+// Head `head`'s share of the attention out-projection for row r: the d
+// outputs W[:, 64 head .. 64 head + 63] . a, with a the head's 64 attended
+// values (16-bit, shared memory, 16-byte aligned), written to op.out_partial
+// [head][r][:] (Decoder.cpp:80-104 adds out_proj(attention) to h; the op
+// after this one adds the heads' partials in head order, with the bias).
+// The head's columns are chunks 2 head and 2 head + 1 of every 16-row tile
+// of the fragment-packed weight, read straight from memory (which CTA joins
+// a (row, head) is known only at run time, so they are not on the stream):
+// each warp takes tiles warp, warp + 7, ..., six tiles' fragments in flight
+// at once, a as the one input row of swap-AB m16n8k16 products.
+template <typename WT>
+__device__ void head_out_projection(const StepParams& p, const StepOp& op, int r, int head, const WT* a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+    const int d = p.width, chunks = p.kpd / 32, tiles = (d + 15) / 16;
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    const uint4 x0 = gq == 0 ? *reinterpret_cast<const uint4*>(a + 8 * tq) : zero;
+    const uint4 x1 = gq == 0 ? *reinterpret_cast<const uint4*>(a + 32 + 8 * tq) : zero;
+    const unsigned char* wbase = static_cast<const unsigned char*>(op.out_weight);
+    float* out = op.out_partial + ((size_t)head * p.rows + r) * d;
+    constexpr int kBatch = 6;
+    for (int t0 = warp; t0 < tiles; t0 += kWarps * kBatch) {
+        uint4 w[kBatch][4];
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const int t = t0 + i * kWarps;
+            if (t < tiles) {
+                const uint4* src =
+                    reinterpret_cast<const uint4*>(wbase + (((size_t)t * chunks + 2 * head) * 32 + lane) * 32);
+                w[i][0] = ld_nc4(src);
+                w[i][1] = ld_nc4(src + 1);
+                w[i][2] = ld_nc4(src + 64);  // the next chunk: 32 lanes x 32 bytes on
+                w[i][3] = ld_nc4(src + 65);
+            } else {
+                w[i][0] = w[i][1] = w[i][2] = w[i][3] = zero;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+            const int t = t0 + i * kWarps;
+            if (t >= tiles) break;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t a0[4] = {w[i][0].x, w[i][1].x, w[i][0].y, w[i][1].y};
+            const uint32_t a1[4] = {w[i][0].z, w[i][1].z, w[i][0].w, w[i][1].w};
+            const uint32_t a2[4] = {w[i][2].x, w[i][3].x, w[i][2].y, w[i][3].y};
+            const uint32_t a3[4] = {w[i][2].z, w[i][3].z, w[i][2].w, w[i][3].w};
+            const uint32_t b0[2] = {x0.x, x0.y}, b1[2] = {x0.z, x0.w};
+            const uint32_t b2[2] = {x1.x, x1.y}, b3[2] = {x1.z, x1.w};
+            mma_16816<WT>(acc, a0, b0);
+            mma_16816<WT>(acc, a1, b1);
+            mma_16816<WT>(acc, a2, b2);
+            mma_16816<WT>(acc, a3, b3);
+            // Column 0 (the one input row) sits in lanes tq == 0: weight rows gq, gq + 8.
+            if (tq == 0) {
+                const int n = 16 * t + gq;
+                if (n < d) out[n] = acc[0];
+                if (n + 8 < d) out[n + 8] = acc[2];
+            }
+        }
+    }
+}
+
 // ----------------------------------------------------------------- attention
 
 template <typename WT, bool READ_ONLY>
@@ -1289,6 +1437,14 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
         }
         const float l = consumer_sum(local, scratch);
         attention_values<WT, false>(scores, V, op.key_stride, D, 0, keys, fold, result);
+        if (op.out_weight) {
+            // The head's out-projection share, from its 16-bit values.
+            __shared__ __align__(16) WT attended[64];
+            for (int c = threadIdx.x; c < 64; c += kThreads) attended[c] = Half16<WT>::from_float(result[c] / l);
+            consumer_sync();
+            head_out_projection<WT>(p, op, r, head, attended);
+            continue;
+        }
         WT* out = static_cast<WT*>(p.attn16);
         for (int c = threadIdx.x; c < D; c += kThreads)
             out[act_index(p, r, head * D + c, p.kpd)] = Half16<WT>::from_float(result[c] / l);
@@ -1486,7 +1642,7 @@ __device__ __forceinline__ void cross_values(const WT* rows, int n, int D, const
 // The last split of a (row, head), one warp: joins the splits' partials
 // [max, sum, D values] with every load of a lane in flight at once.
 template <typename WT>
-__device__ void cross_join(const StepParams& p, const StepOp& op, int r, int head) {
+__device__ void cross_join(const StepParams& p, const StepOp& op, int r, int head, WT* to_shared = nullptr) {
     const int lane = threadIdx.x & 31;
     const int D = p.head_width, S = op.splits;
     const float* part = p.partial + ((size_t)r * p.heads + head) * S * (D + 2);
@@ -1504,13 +1660,17 @@ __device__ void cross_join(const StepParams& p, const StepOp& op, int r, int hea
         if (c0 < D) o[0] += ld_cg(ps + c0) * f;
         if (c1 < D) o[1] += ld_cg(ps + c1) * f;
     }
+    const float a0 = o[0] / l + (op.value_bias && c0 < D ? __ldg(op.value_bias + head * D + c0) : 0.f);
+    const float a1 = o[1] / l + (op.value_bias && c1 < D ? __ldg(op.value_bias + head * D + c1) : 0.f);
+    if (to_shared) {
+        // A fused out-projection reads the 16-bit values from shared memory.
+        if (c0 < D) to_shared[c0] = Half16<WT>::from_float(a0);
+        if (c1 < D) to_shared[c1] = Half16<WT>::from_float(a1);
+        return;
+    }
     WT* out = static_cast<WT*>(p.attn16);
-    if (c0 < D)
-        out[act_index(p, r, head * D + c0, p.kpd)] =
-            Half16<WT>::from_float(o[0] / l + (op.value_bias ? __ldg(op.value_bias + head * D + c0) : 0.f));
-    if (c1 < D)
-        out[act_index(p, r, head * D + c1, p.kpd)] =
-            Half16<WT>::from_float(o[1] / l + (op.value_bias ? __ldg(op.value_bias + head * D + c1) : 0.f));
+    if (c0 < D) out[act_index(p, r, head * D + c0, p.kpd)] = Half16<WT>::from_float(a0);
+    if (c1 < D) out[act_index(p, r, head * D + c1, p.kpd)] = Half16<WT>::from_float(a1);
 }
 
 // Shared memory: [q: 64][max: 2 x 8][sum: 2 x 8][fold: 2 x kWarps x 64][scores: kMaxCrossUnitKeys]
@@ -1609,6 +1769,54 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&d)[4], const void* 
                  : "memory");
 }
 
+// Shared memory of cross_attention_mma before a fused query's tile:
+// [q: 64][warp max: 8][warp sum: 8][warp rows: kWarps x 64] floats.
+constexpr int kCrossQueryOffset = 2304;
+
+// A fused cross query (op.gamma set: a few rows): q of (row r, head) is
+// LN2(h_r) . Wq[64 head .. 64 head + 63]^T + bq, scaled by 1/sqrt(D)
+// (Decoder.cpp:93-100, DecoderShape.cpp:19-26), computed by the item itself
+// instead of by a product op of its own.  The LayerNorm prologue adds the
+// self attention's out-projection partials (its residual, Decoder.cpp:80-91);
+// keep_sum: this CTA stores the sums as the new residual rows.  The head's
+// four 16-row weight tiles come off the weight stream ahead of the item's
+// keys, one tile to each of the first four warps.  Work area at `area`:
+// [xs: 8 x pitch 16-bit].
+template <typename WT>
+__device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int head, bool keep_sum, Stream& s,
+                            unsigned char* area, float* q) {
+    const int pitch = tile_pitch(p.kpd), D = p.head_width;
+    WT* xs = reinterpret_cast<WT*>(area);
+    Addends add;
+    if (op.addend_count > 0)
+        add = Addends{op.addends, op.addend_count, op.addend_stride, op.addend_bias, keep_sum ? op.sum_out : nullptr};
+    layer_norm_tile<WT>(p, op.norm_input ? op.norm_input : p.h, op.gamma, op.beta, r, 1, 1, 0, xs, pitch, nullptr,
+                        add);
+    consumer_sync();
+    // Warp j < tiles owns q tile j (one unit: a stage holds a whole tile)
+    // over all of K, so no partial sums cross warps.
+    const int tiles = round16(D) / 16, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < tiles) {
+        const unsigned long long index = s.next + warp;
+        const unsigned char* unit = owned_unit_at(p, s, index);
+        float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+        const bool x_ok[1] = {(lane >> 2) == 0};
+        chunks_product<WT, 1, true>(unit, 0, 1, op.kp / 32, xs, pitch, 0, x_ok, acc);
+        release_at(s, index, kWarps);
+        // Column 0 (the one row) sits in lanes t == 0: q rows g and g + 8 of the tile.
+        if ((lane & 3) == 0) {
+            const int n = 16 * warp + (lane >> 2);
+            const float* bias = op.bias + head * round16(D);
+            if (n < D) q[n] = (acc[0][0] + __ldg(bias + n)) * p.scale;
+            if (n + 8 < D) q[n + 8] = (acc[0][2] + __ldg(bias + n + 8)) * p.scale;
+        }
+    }
+    s.next += tiles;
+    // (A wait that gave up hands back its stage all the same; the kernel
+    // leaves at the next grid barrier.)
+    return true;
+}
+
 // 64-wide heads on the tensor cores.  A warp takes the unit's 16-key groups
 // 16*warp, 16*(warp + kWarps), ...:
 //   scores  m16n8k16 with q as row 0 of A (split hi + lo, so the product
@@ -1633,11 +1841,17 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
     float* wsum = wmax + 8;
     float* wrows = wsum + 8;
     __shared__ int is_last;
+    __shared__ __align__(16) WT attended[64];  // a fused out-projection's input
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int split = item % S, head = (item / S) % H, r = item / (S * H);
         const int count = cross_item_units(op, item, units);
         consumer_sync();
-        if (threadIdx.x < 64) q[threadIdx.x] = ld_cg(p.q + (size_t)r * p.width + head * 64 + threadIdx.x) * p.scale;
+        if (op.gamma) {
+            // The item's own query; item (r, head 0, split 0) keeps row r's residual sums.
+            if (!cross_query<WT>(p, op, r, head, head == 0 && split == 0, s, work + kCrossQueryOffset, q)) return;
+        } else if (threadIdx.x < 64) {
+            q[threadIdx.x] = ld_cg(p.q + (size_t)r * p.width + head * 64 + threadIdx.x) * p.scale;
+        }
         consumer_sync();
         // Row 0 of A is q's hi half, row 1 its lo half (lanes 4..7), so one
         // product gives both, and the two rows add after the chain.
@@ -1776,9 +1990,15 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
             if (threadIdx.x < 64) O += wrows[w * 64 + threadIdx.x] * f;
         }
         if (S == 1) {
+            const float a = O / L + (op.value_bias ? __ldg(op.value_bias + head * 64 + (threadIdx.x & 63)) : 0.f);
+            if (op.out_weight) {
+                if (threadIdx.x < 64) attended[threadIdx.x] = Half16<WT>::from_float(a);
+                consumer_sync();
+                head_out_projection<WT>(p, op, r, head, attended);
+                continue;
+            }
             if (threadIdx.x < 64)
-                static_cast<WT*>(p.attn16)[act_index(p, r, head * 64 + threadIdx.x, p.kpd)] = Half16<WT>::from_float(
-                    O / L + (op.value_bias ? __ldg(op.value_bias + head * 64 + threadIdx.x) : 0.f));
+                static_cast<WT*>(p.attn16)[act_index(p, r, head * 64 + threadIdx.x, p.kpd)] = Half16<WT>::from_float(a);
             continue;
         }
         float* part = p.partial + (((size_t)r * H + head) * S + split) * 66;
@@ -1795,9 +2015,15 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
             if (is_last) atomicExch(counter, 0u);
         }
         consumer_sync();
-        if (is_last && warp == 0) {
-            __threadfence();
-            cross_join<WT>(p, op, r, head);
+        if (is_last) {
+            if (warp == 0) {
+                __threadfence();
+                cross_join<WT>(p, op, r, head, op.out_weight ? attended : nullptr);
+            }
+            if (op.out_weight) {
+                consumer_sync();
+                head_out_projection<WT>(p, op, r, head, attended);
+            }
         }
     }
 }
@@ -1806,6 +2032,84 @@ template <typename WT>
 __device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
     if (p.head_width == 64) cross_attention_mma<WT>(p, op, s, work);
     else cross_attention_cores<WT>(p, op, s, work);
+}
+
+// ----------------------------------------------------------- L2 prefetch
+
+// The weight stream moves ~100 MB or more a step through L2, so the small
+// per-layer parameters (LayerNorm gains and offsets, biases) and the columns
+// a fused out-projection reads straight from memory have left L2 by the
+// time the next step needs them: each would cost its op a DRAM round trip
+// on the critical path.  At the start of each op, thread 0 of every CTA asks
+// L2 for a share of what the op after it reads (a bulk prefetch: no data
+// comes back to the SM, nothing waits for it), so those loads find L2.
+__device__ __forceinline__ void prefetch_l2(const void* ptr, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(ptr), "r"(bytes) : "memory");
+}
+
+// Share of op `next`'s parameters for this CTA (all sizes are multiples of
+// 16 bytes and every array starts on a 256-byte boundary).
+__device__ void prefetch_op(const StepParams& p, const StepOp& next, int position) {
+    const unsigned row = (unsigned)p.width * 4u;
+    const unsigned cta = blockIdx.x, grid = gridDim.x;
+    auto take = [&](unsigned slot, const void* ptr, unsigned bytes) {
+        if (ptr && bytes && slot % grid == cta) prefetch_l2(ptr, bytes);
+    };
+    switch (next.kind) {
+    case kOpProduct:
+        take(0, next.gamma, row);
+        take(1, next.beta, row);
+        take(2, next.bias, (unsigned)next.n * 4u);
+        take(3, next.addend_bias, row);
+        break;
+    case kOpNorm:
+        take(0, next.gamma, row);
+        take(1, next.beta, row);
+        break;
+    case kOpLogits:
+        take(0, p.final_gamma, row);
+        take(1, p.final_beta, row);
+        if (p.mask) {
+            // The suppression mask, 4 KB a CTA.
+            const unsigned bytes = (unsigned)p.vocabulary * 4u / 16u * 16u;
+            for (unsigned o = (cta + 2) % grid * 4096u; o < bytes; o += grid * 4096u)
+                prefetch_l2(reinterpret_cast<const unsigned char*>(p.mask) + o, min(4096u, bytes - o));
+        }
+        break;
+    case kOpEmbed:
+        // The next step's position rows.
+        if (position + 2 * p.tokens <= p.max_positions)
+            take(0, p.position_table + (size_t)(position + p.tokens) * p.width, row * (unsigned)p.tokens);
+        break;
+    case kOpCrossAttention:
+        take(0, next.value_bias, row);
+        take(1, next.gamma, row);
+        take(2, next.beta, row);
+        take(3, next.bias, (unsigned)next.n * 4u);
+        take(4, next.addend_bias, row);
+        break;
+    }
+    if (next.kind == kOpSelfAttention && next.out_weight) {
+        // A few rows: each window's self keys and values 0 .. position + T - 1
+        // (last written steps ago, so out of L2 by now), 4 KB a CTA.
+        const unsigned bytes = (unsigned)(position + p.tokens) * (unsigned)p.width * 2u / 16u * 16u;
+        const unsigned per = (bytes + 4095u) / 4096u;
+        for (unsigned i = cta; i < 2u * (unsigned)p.windows * per; i += grid) {
+            const unsigned which = i / per, piece = i % per, b = which >> 1;
+            const void* base = (which & 1) ? next.values : next.keys;
+            const unsigned o = piece * 4096u;
+            prefetch_l2(static_cast<const unsigned char*>(base) + (size_t)b * next.window_stride * 2 + o,
+                        min(4096u, bytes - o));
+        }
+    }
+    if (next.out_weight) {
+        // Head h's columns: 2 KB (chunks 2h, 2h + 1) of every 16-row tile.
+        const int chunks = p.kpd / 32, tiles = (p.width + 15) / 16;
+        for (int i = (int)cta; i < p.heads * tiles; i += (int)grid) {
+            const int h = i / tiles, t = i % tiles;
+            prefetch_l2(static_cast<const unsigned char*>(next.out_weight) + ((size_t)t * chunks + 2 * h) * 1024, 2048u);
+        }
+    }
 }
 
 // -------------------------------------------------------------- the kernel
@@ -1891,6 +2195,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
         if (stamp && step == 0) p.profile[0] = global_ns();
         for (int i = 0; i < p.n_ops; ++i) {
             const StepOp& op = p.ops[i];
+            if (threadIdx.x == 0) prefetch_op(p, p.ops[i + 1 < p.n_ops ? i + 1 : 0], position);
             Trace tro = trace_of(p.profile);
             tro.begin();
             switch (op.kind) {
@@ -1902,7 +2207,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
             case kOpSelfAttention:
                 // As many items as CTAs or more: a warp per item; fewer: the
                 // whole CTA on each.
-                if (p.head_width == 64 && p.max_positions <= kSelfWarpKeys && p.rows * p.heads >= (int)gridDim.x)
+                if (!op.out_weight && p.head_width == 64 && p.max_positions <= kSelfWarpKeys &&
+                    p.rows * p.heads >= (int)gridDim.x)
                     self_attention_warps<WT>(p, op, position, work);
                 else
                     op_self_attention<WT>(p, op, position, work);
@@ -1914,7 +2220,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
             tro.end(kTrOther);
             Trace trb = trace_of(p.profile);
             trb.begin();
-            const bool passed = grid_barrier(p.barrier, epoch, p.state);
+            const bool passed = grid_barrier(p, epoch);
             trb.end(kTrBarrier);
             if (!passed) {
                 trace_flush(p);
@@ -1942,7 +2248,8 @@ size_t work_bytes(const StepParams& p, int max_chunk) {
         sizeof(float) * std::max<size_t>({(size_t)kAttentionFixed + std::max(max_chunk, p.max_positions),
                                           (size_t)(64 + 32 + 2 * kWarps * 64 + kMaxCrossUnitKeys),
                                           (size_t)kWarps * kSelfWarpKeys});
-    size_t work = std::max(product, attention);
+    // A fused cross query's tile sits past the cross attention's own area.
+    size_t work = std::max(product + kCrossQueryOffset, attention);
     // The activation ring of the tensor-core products (1024-byte aligned).
     if (p.umma) work = std::max(work, (size_t)1024 + (size_t)p.umma_x_stages * p.umma_x_stage_bytes);
     return (work + 127) / 128 * 128;

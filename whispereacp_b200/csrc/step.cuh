@@ -128,6 +128,24 @@ struct StepOp {
     int norm_rows, norm_step, norm_offset;
     float* norm_hidden;
     int norm_umma;          // norm: write the tensor-core activation layout
+    // Attention ops with out_weight set (a few rows, 64-wide heads): each
+    // (row, head) also applies its head's 64 columns of the attention
+    // out-projection (fragment-packed [d, kpd], bias left out) to the head's
+    // attended values and writes the d results to out_partial [H][R][d]; the
+    // op after it adds them, so the out-projection is no op of its own.
+    const void* out_weight;
+    float* out_partial;
+    // LayerNorm prologues: the rows normalised are norm_input (p.h when
+    // null) plus, with addend_count > 0, addend_bias and addends + j *
+    // addend_stride (row-major [R][d]) for j = 0 .. addend_count-1 in that
+    // order; the CTA that holds a row tile's first weight tile writes those
+    // sums, the new residual rows, to sum_out.
+    const float* norm_input;
+    const float* addends;
+    int addend_count;
+    long long addend_stride;
+    const float* addend_bias;
+    float* sum_out;
     // Tensor-core products: K splits of each tile's inner size.  With more
     // than one (only when all the items fit one wave of CTAs), each item
     // writes fp32 partials to p.partial_d [split][n_pad][rows_pad], the

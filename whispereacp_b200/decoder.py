@@ -254,6 +254,15 @@ class Decoder:
         check(self._lib.wsp_decoder_trace_cycles(self._handle, values, len(TRACE_SECTIONS)))
         return {name: values[i] for i, name in enumerate(TRACE_SECTIONS)}
 
+    def op_times(self) -> list[tuple[int, float]]:
+        """(kind, microseconds) of each op of the step, from the last time_kernels."""
+        count = ctypes.c_int()
+        check(self._lib.wsp_decoder_op_times(self._handle, None, None, 0, ctypes.byref(count)))
+        us = (ctypes.c_float * max(1, count.value))()
+        kinds = (ctypes.c_int * max(1, count.value))()
+        check(self._lib.wsp_decoder_op_times(self._handle, us, kinds, count.value, ctypes.byref(count)))
+        return [(kinds[i], us[i]) for i in range(count.value)]
+
     def time_kernels(self, steps: int) -> dict[str, tuple[float, int]]:
         """Mean ms per launch and launches per step of each kernel class."""
         ms = (ctypes.c_float * len(KERNEL_CLASSES))()
