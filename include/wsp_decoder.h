@@ -216,9 +216,10 @@ int wsp_decoder_time_barriers(wsp_decoder* decoder, int count, float* microsecon
 /*
  * Clock cycles per step that CTA 0 of the decode kernel spent in each section
  * (waiting for weights, products, grid barriers, reductions and epilogues,
- * layer norms and row staging, attention, and the ops as a whole, barriers
- * excluded), averaged over the last wsp_decoder_time_kernels run; `count`
- * entries (7 are defined).
+ * layer norms and row staging, attention, the ops as a whole with barriers
+ * excluded, a fused cross query, a cross split join, a fused out-projection,
+ * a self-attention item, and the logits), averaged over the last
+ * wsp_decoder_time_kernels run; `count` entries (12 are defined).
  */
 int wsp_decoder_trace_cycles(const wsp_decoder* decoder, double* cycles, int count);
 

@@ -22,7 +22,8 @@ WSP_FLOAT32 = 0
 WSP_FLOAT16 = 1
 WSP_BFLOAT16 = 2
 
-TRACE_SECTIONS = ("wait", "compute", "barrier", "epilogue", "norm", "attention", "ops")
+TRACE_SECTIONS = ("wait", "compute", "barrier", "epilogue", "norm", "attention", "ops", "query", "join",
+                  "out_projection", "self_item", "logits")
 
 KERNEL_CLASSES = ("embed", "layer_norm", "projection", "self_attention", "cross_attention",
                   "attention_combine", "logits_argmax", "argmax_final", "other")

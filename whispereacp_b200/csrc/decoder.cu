@@ -53,6 +53,16 @@ void cublas_check(cublasStatus_t s, const char* what) {
 
 // ------------------------------------------------------- device memory
 
+// Host-side memsets and pageable copies run on the legacy default stream,
+// and may still be in flight when the call returns (a pageable copy returns
+// once the data is staged; a memset of device memory once it is queued).
+// The decoder launches on a non-blocking stream, which does not wait for
+// the legacy one -- and a cooperative launch that holds every SM can keep
+// a queued memset from running until after it.  So every such call is
+// followed by this wait before anything the decoder launches can read the
+// memory.
+inline void settle_legacy_stream() { CUDA_CHECK(cudaStreamSynchronize(cudaStreamLegacy)); }
+
 class DeviceBuffer {
 public:
     DeviceBuffer() = default;
@@ -65,6 +75,7 @@ public:
         if (bytes == 0) bytes = 16;
         CUDA_CHECK(cudaMalloc(&ptr_, bytes));
         CUDA_CHECK(cudaMemset(ptr_, 0, bytes));
+        settle_legacy_stream();
         bytes_ = bytes;
     }
     void release() {
@@ -412,6 +423,7 @@ public:
         for (int b = 0; b < windows_; ++b)
             std::copy(prompt_.begin(), prompt_.end(), ring_prompt.begin() + (size_t)b * ring_stride());
         CUDA_CHECK(cudaMemcpy(ring_prompt_.get(), ring_prompt.data(), ring_prompt.size() * 4, cudaMemcpyHostToDevice));
+        settle_legacy_stream();
         ensure_row_capacity((int)prompt_.size());
         generation_set_ = true;
     }
@@ -561,6 +573,7 @@ public:
         for (auto& o : ops) o.kind = kOpNone;
         if (ops_probe_dev_.bytes() < ops.size() * sizeof(StepOp)) ops_probe_dev_.allocate(ops.size() * sizeof(StepOp));
         CUDA_CHECK(cudaMemcpy(ops_probe_dev_.get(), ops.data(), ops.size() * sizeof(StepOp), cudaMemcpyHostToDevice));
+        settle_legacy_stream();
         StepParams p = base_params(1, true, nullptr, nullptr, nullptr, nullptr, 1, false);
         p.profile = profile_.get<unsigned long long>();
         p.ops = ops_probe_dev_.get<StepOp>();
@@ -752,11 +765,13 @@ private:
         CUDA_CHECK(cudaMemcpy(state, state_.get(), sizeof state, cudaMemcpyDeviceToHost));
         if (state[kError] != 0) {
             CUDA_CHECK(cudaMemset(state_.get<int>() + kError, 0, sizeof(int)));
+            settle_legacy_stream();
             if (state[kError] & kErrBarrierTimeout) {
                 static const char* const kinds[] = {"?", "a grid barrier", "a weight unit", "a free stage",
                                                     "a landing copy", "an armed stage", "the splits of a product"};
                 const int kind = state[kFailKind] >= 1 && state[kFailKind] <= 6 ? state[kFailKind] : 0;
                 CUDA_CHECK(cudaMemset(state_.get<int>() + kFailKind, 0, 3 * sizeof(int)));
+                settle_legacy_stream();
                 throw CudaFailure(std::string("the decode kernel gave up waiting for ") + kinds[kind] + " (CTA " +
                                       std::to_string(state[kFailCta]) + ", index " +
                                       std::to_string(state[kFailWhere]) + ")",
@@ -1342,7 +1357,7 @@ private:
     std::vector<double> op_us_;
     std::vector<int> op_kinds_;
     static constexpr int kTraceOffset = 512;   // kTraceBase of step.cu
-    static constexpr int kTraceSections = 7;
+    static constexpr int kTraceSections = 12;
     int queued_steps_ = 0;
 };
 
@@ -1426,6 +1441,7 @@ int wsp_decoder_set_tensor(wsp_decoder* decoder, const char* name, wsp_dtype dty
     return guarded([&] {
         WSP_NEED(decoder);
         decoder->impl->set_tensor(name, dtype, extents, rank, data);
+        wsp::settle_legacy_stream();  // the uploads are pageable copies
     });
 }
 

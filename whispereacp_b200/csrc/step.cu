@@ -89,6 +89,15 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+// Adds one to a gpu-scope counter with acquire-release semantics and returns
+// the old value: after a CTA barrier, it releases everything the CTA wrote
+// before it and, for the arrival that sees the others', acquires what they
+// released -- one round trip, no separate fences.
+__device__ __forceinline__ unsigned arrive_acq_rel(unsigned* counter) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;\n" : "=r"(old) : "l"(counter) : "memory");
+    return old;
+}
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -99,7 +108,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // cycles per section of a launch into profile[kTraceBase + section] when a
 // profile buffer is given.
 enum TraceSection : int { kTrWait = 0, kTrCompute, kTrBarrier, kTrEpilogue, kTrNorm, kTrAttention, kTrOther,
-                          kTrSections };
+                          kTrQuery, kTrJoin, kTrOutProj, kTrSelf, kTrLogits, kTrSections };
 constexpr int kTraceBase = 512;
 __shared__ unsigned long long trace_cycles[kTrSections];
 
@@ -375,9 +384,10 @@ __device__ __forceinline__ void add_addends(const Addends& a, size_t row, int d,
         const int c = c0 + i * step;
         if (c < d) v[i] += __ldg(a.bias + c);
     }
-    // Four partial rows a batch for a few values a thread; one for many (a
-    // row's own loads are then plenty in flight).
-    constexpr int kBatch = N <= 8 ? 4 : 1;
+    // Eight partial rows a batch for a few values a thread (every load of a
+    // base.en-sized op in flight at once); one for many (a row's own loads
+    // are then plenty in flight).
+    constexpr int kBatch = N <= 8 ? 8 : 1;
     for (int j0 = 0; j0 < a.count; j0 += kBatch) {
         float t[kBatch][N];
 #pragma unroll
@@ -979,8 +989,8 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
             // The tile's splits (each on its own CTA: a split product's items
             // fit one wave) meet here; then each joins a contiguous share of
             // the tile's (row, weight row) elements, summing the partials in
-            // split order.
-            __threadfence();
+            // split order.  (The release below, after the CTA barrier,
+            // publishes every thread's partials.)
             consumer_sync();
             if (threadIdx.x == 0) {
                 unsigned* counter = p.split_counters + (size_t)op_index * kSplitSlots + (item % (m_tiles * groups));
@@ -1185,12 +1195,10 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
         p.candidate_values[(size_t)r * gridDim.x + blockIdx.x] = best_v[r];
         p.candidate_indices[(size_t)r * gridDim.x + blockIdx.x] = best_i[r];
     }
-    __threadfence();
     consumer_sync();
-    if (threadIdx.x == 0) is_last = atomicAdd(p.logits_counter, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) is_last = arrive_acq_rel(p.logits_counter) == gridDim.x - 1;
     consumer_sync();
     if (!is_last) return;
-    __threadfence();
     const int rows_per_window = p.out_rows / p.windows;
     for (int r = warp; r < p.out_rows; r += kWarps) {
         float bv = -INFINITY;
@@ -1226,7 +1234,7 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
         atomicAdd(p.state + kStepsDone, 1);
         atomicAdd(p.state + kPosition, p.tokens);
         atomicExch(p.logits_counter, 0u);
-        __threadfence();
+        // (The grid barrier after this op releases these writes.)
     }
 }
 
@@ -1244,6 +1252,8 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
 // at once, a as the one input row of swap-AB m16n8k16 products.
 template <typename WT>
 __device__ void head_out_projection(const StepParams& p, const StepOp& op, int r, int head, const WT* a) {
+    Trace tr = trace_of(p.profile);
+    tr.begin();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
     const int d = p.width, chunks = p.kpd / 32, tiles = (d + 15) / 16;
     const uint4 zero = make_uint4(0, 0, 0, 0);
@@ -1291,6 +1301,7 @@ __device__ void head_out_projection(const StepParams& p, const StepOp& op, int r
             }
         }
     }
+    tr.end(kTrOutProj);
 }
 
 // ----------------------------------------------------------------- attention
@@ -1411,6 +1422,71 @@ constexpr int kFold = 2048;
 constexpr int kAttentionFixed = 64 + 8 + kFold + 64;
 
 // Self-attention of row (b, t) and head h over keys 0..position+t: one item.
+// A self-attention item of at most kThreads keys and 64-wide heads: thread
+// j loads key row j, and thread (g, piece) the value pieces of keys g, g +
+// 28, ..., all before q arrives, so the item waits on memory once.  Scores
+// (scaled q . k), the maximum, the weights exp(s - max) and their sum, and
+// the weighted values as the general path computes them
+// (SingleQueryAttention.h:62-373); returns the sum, result[0..63] holds the
+// unnormalised output.
+template <typename WT>
+__device__ float self_item_in_registers(const StepParams& p, int r, int head, int keys, const WT* K, const WT* V,
+                                        long long key_stride, float* q, float* scratch, float* fold, float* result,
+                                        float* scores) {
+    const int j = threadIdx.x;
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    uint4 kr[8], vr[8];
+    const WT* krow = K + (size_t)(j < keys ? j : 0) * key_stride;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) kr[i] = j < keys ? load_kv4<WT, false>(krow + 8 * i) : zero;
+    constexpr int kGroups = kThreads / 8;
+    const int piece = threadIdx.x & 7, g = threadIdx.x >> 3;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int key = g + kGroups * i;
+        vr[i] = key < keys ? load_kv4<WT, false>(V + (size_t)key * key_stride + piece * 8) : zero;
+    }
+    if (threadIdx.x < 64) q[threadIdx.x] = ld_cg(p.q + (size_t)r * p.width + head * 64 + threadIdx.x) * p.scale;
+    consumer_sync();
+    float sc = -INFINITY;
+    if (j < keys) {
+        sc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float2 f0 = Half16<WT>::pair_to_float2(kr[i].x), f1 = Half16<WT>::pair_to_float2(kr[i].y);
+            const float2 f2 = Half16<WT>::pair_to_float2(kr[i].z), f3 = Half16<WT>::pair_to_float2(kr[i].w);
+            const float* qq = q + 8 * i;
+            sc += qq[0] * f0.x + qq[1] * f0.y + qq[2] * f1.x + qq[3] * f1.y + qq[4] * f2.x + qq[5] * f2.y +
+                  qq[6] * f3.x + qq[7] * f3.y;
+        }
+    }
+    const float m = consumer_max(sc, scratch);
+    const float e = j < keys ? __expf(sc - m) : 0.f;
+    if (j < keys) scores[j] = e;
+    const float l = consumer_sum(e, scratch);  // (its barriers also publish scores[])
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int key = g + kGroups * i;
+        if (key >= keys) break;
+        const float w = scores[key];
+        const float2 f0 = Half16<WT>::pair_to_float2(vr[i].x), f1 = Half16<WT>::pair_to_float2(vr[i].y);
+        const float2 f2 = Half16<WT>::pair_to_float2(vr[i].z), f3 = Half16<WT>::pair_to_float2(vr[i].w);
+        acc[0] += w * f0.x; acc[1] += w * f0.y; acc[2] += w * f1.x; acc[3] += w * f1.y;
+        acc[4] += w * f2.x; acc[5] += w * f2.y; acc[6] += w * f3.x; acc[7] += w * f3.y;
+    }
+#pragma unroll
+    for (int e8 = 0; e8 < 8; ++e8) fold[g * 64 + piece * 8 + e8] = acc[e8];
+    consumer_sync();
+    if (threadIdx.x < 64) {
+        float o = 0.f;
+        for (int gg = 0; gg < kGroups; ++gg) o += fold[gg * 64 + threadIdx.x];
+        result[threadIdx.x] = o;
+    }
+    consumer_sync();
+    return l;
+}
+
 template <typename WT>
 __device__ void op_self_attention(const StepParams& p, const StepOp& op, int position, unsigned char* smem) {
     float* q = reinterpret_cast<float*>(smem);
@@ -1423,20 +1499,31 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
         const int r = item / p.heads, head = item % p.heads;
         const int b = r / p.tokens, t = r % p.tokens;
         const int keys = position + t + 1;
-        consumer_sync();
-        for (int c = threadIdx.x; c < D; c += kThreads) q[c] = ld_cg(p.q + (size_t)r * p.width + head * D + c) * p.scale;
+        Trace trs = trace_of(p.profile);
+        trs.begin();
         consumer_sync();
         const WT* K = static_cast<const WT*>(op.keys) + (size_t)b * op.window_stride + (size_t)head * D;
         const WT* V = static_cast<const WT*>(op.values) + (size_t)b * op.window_stride + (size_t)head * D;
-        const float m = consumer_max(attention_scores<WT, false>(q, K, op.key_stride, D, 0, keys, scores), scratch);
-        float local = 0.f;
-        for (int j = threadIdx.x; j < keys; j += kThreads) {
-            const float e = __expf(scores[j] - m);
-            scores[j] = e;
-            local += e;
+        float l;
+        if (D == 64 && keys <= kThreads) {
+            // Up to one key a thread: every key row and value piece of the item
+            // is loaded with q, one round trip in all.
+            l = self_item_in_registers<WT>(p, r, head, keys, K, V, op.key_stride, q, scratch, fold, result, scores);
+        } else {
+            for (int c = threadIdx.x; c < D; c += kThreads)
+                q[c] = ld_cg(p.q + (size_t)r * p.width + head * D + c) * p.scale;
+            consumer_sync();
+            const float m = consumer_max(attention_scores<WT, false>(q, K, op.key_stride, D, 0, keys, scores), scratch);
+            float local = 0.f;
+            for (int j = threadIdx.x; j < keys; j += kThreads) {
+                const float e = __expf(scores[j] - m);
+                scores[j] = e;
+                local += e;
+            }
+            l = consumer_sum(local, scratch);
+            attention_values<WT, false>(scores, V, op.key_stride, D, 0, keys, fold, result);
         }
-        const float l = consumer_sum(local, scratch);
-        attention_values<WT, false>(scores, V, op.key_stride, D, 0, keys, fold, result);
+        trs.end(kTrSelf);
         if (op.out_weight) {
             // The head's out-projection share, from its 16-bit values.
             __shared__ __align__(16) WT attended[64];
@@ -1741,18 +1828,14 @@ __device__ void cross_attention_cores(const StepParams& p, const StepOp& op, Str
             part[0] = m_run;
             part[1] = l_run;
         }
-        __threadfence();
         consumer_sync();
         if (threadIdx.x == 0) {
             unsigned* counter = p.combine_counters + (size_t)r * H + head;
-            is_last = atomicAdd(counter, 1u) == (unsigned)(S - 1);
+            is_last = arrive_acq_rel(counter) == (unsigned)(S - 1);
             if (is_last) atomicExch(counter, 0u);
         }
         consumer_sync();
-        if (is_last && warp == 0) {
-            __threadfence();
-            cross_join<WT>(p, op, r, head);
-        }
+        if (is_last && warp == 0) cross_join<WT>(p, op, r, head);
     }
 }
 
@@ -1848,7 +1931,10 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
         consumer_sync();
         if (op.gamma) {
             // The item's own query; item (r, head 0, split 0) keeps row r's residual sums.
+            Trace trq = trace_of(p.profile);
+            trq.begin();
             if (!cross_query<WT>(p, op, r, head, head == 0 && split == 0, s, work + kCrossQueryOffset, q)) return;
+            trq.end(kTrQuery);
         } else if (threadIdx.x < 64) {
             q[threadIdx.x] = ld_cg(p.q + (size_t)r * p.width + head * 64 + threadIdx.x) * p.scale;
         }
@@ -2001,29 +2087,30 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
                 static_cast<WT*>(p.attn16)[act_index(p, r, head * 64 + threadIdx.x, p.kpd)] = Half16<WT>::from_float(a);
             continue;
         }
+        Trace trj = trace_of(p.profile);
+        trj.begin();
         float* part = p.partial + (((size_t)r * H + head) * S + split) * 66;
         if (threadIdx.x < 64) part[2 + threadIdx.x] = O;
         if (threadIdx.x == 0) {
             part[0] = M;
             part[1] = L;
         }
-        __threadfence();
         consumer_sync();
         if (threadIdx.x == 0) {
             unsigned* counter = p.combine_counters + (size_t)r * H + head;
-            is_last = atomicAdd(counter, 1u) == (unsigned)(S - 1);
+            is_last = arrive_acq_rel(counter) == (unsigned)(S - 1);
             if (is_last) atomicExch(counter, 0u);
         }
         consumer_sync();
         if (is_last) {
-            if (warp == 0) {
-                __threadfence();
-                cross_join<WT>(p, op, r, head, op.out_weight ? attended : nullptr);
-            }
+            if (warp == 0) cross_join<WT>(p, op, r, head, op.out_weight ? attended : nullptr);
             if (op.out_weight) {
                 consumer_sync();
+                trj.end(kTrJoin);
                 head_out_projection<WT>(p, op, r, head, attended);
             }
+        } else {
+            trj.end(kTrJoin);
         }
     }
 }
@@ -2214,7 +2301,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
                     op_self_attention<WT>(p, op, position, work);
                 break;
             case kOpCrossAttention: op_cross_attention<WT>(p, op, s, work); break;
-            case kOpLogits: op_logits<WT, NT>(p, op, position, s, work); break;
+            case kOpLogits: {
+                Trace trl = trace_of(p.profile);
+                trl.begin();
+                op_logits<WT, NT>(p, op, position, s, work);
+                trl.end(kTrLogits);
+                break;
+            }
             case kOpNorm: op_norm<WT>(p, op, work); break;
             }
             tro.end(kTrOther);
