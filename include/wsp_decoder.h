@@ -218,8 +218,10 @@ int wsp_decoder_time_barriers(wsp_decoder* decoder, int count, float* microsecon
  * (waiting for weights, products, grid barriers, reductions and epilogues,
  * layer norms and row staging, attention, the ops as a whole with barriers
  * excluded, a fused cross query, a cross split join, a fused out-projection,
- * a self-attention item, and the logits), averaged over the last
- * wsp_decoder_time_kernels run; `count` entries (12 are defined).
+ * a self-attention item, the logits, a one- or two-row layer norm's loads
+ * and the rest of it, the logits' vocabulary tiles and their fold), averaged
+ * over the last wsp_decoder_time_kernels run; `count` entries (16 are
+ * defined).
  */
 int wsp_decoder_trace_cycles(const wsp_decoder* decoder, double* cycles, int count);
 

@@ -23,7 +23,8 @@ WSP_FLOAT16 = 1
 WSP_BFLOAT16 = 2
 
 TRACE_SECTIONS = ("wait", "compute", "barrier", "epilogue", "norm", "attention", "ops", "query", "join",
-                  "out_projection", "self_item", "logits")
+                  "out_projection", "self_item", "logits", "norm_load", "norm_rest", "logits_tiles",
+                  "logits_fold")
 
 KERNEL_CLASSES = ("embed", "layer_norm", "projection", "self_attention", "cross_attention",
                   "attention_combine", "logits_argmax", "argmax_final", "other")

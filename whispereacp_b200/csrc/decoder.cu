@@ -1357,7 +1357,7 @@ private:
     std::vector<double> op_us_;
     std::vector<int> op_kinds_;
     static constexpr int kTraceOffset = 512;   // kTraceBase of step.cu
-    static constexpr int kTraceSections = 12;
+    static constexpr int kTraceSections = 16;
     int queued_steps_ = 0;
 };
 

@@ -65,6 +65,19 @@ __device__ __forceinline__ float consumer_sum(float v, float* scratch) {
     return total;
 }
 
+// consumer_sum for a scratch array no thread can still be reading (the
+// caller alternates arrays between barriers): one CTA barrier instead of two.
+__device__ __forceinline__ float consumer_sum_fresh(float v, float* scratch) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) scratch[warp] = v;
+    consumer_sync();
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) total += scratch[w];
+    return total;
+}
+
 __device__ __forceinline__ float consumer_max(float v, float* scratch) {
     v = warp_max(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -108,7 +121,8 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // cycles per section of a launch into profile[kTraceBase + section] when a
 // profile buffer is given.
 enum TraceSection : int { kTrWait = 0, kTrCompute, kTrBarrier, kTrEpilogue, kTrNorm, kTrAttention, kTrOther,
-                          kTrQuery, kTrJoin, kTrOutProj, kTrSelf, kTrLogits, kTrSections };
+                          kTrQuery, kTrJoin, kTrOutProj, kTrSelf, kTrLogits, kTrNormLoad, kTrNormRest, kTrLogitsTiles,
+                          kTrLogitsFold, kTrSections };
 constexpr int kTraceBase = 512;
 __shared__ unsigned long long trace_cycles[kTrSections];
 
@@ -417,10 +431,15 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
     const int d = p.width;
     if (rows_in_tile <= 2) {
         // A row or two: the whole CTA on each row, every load of the row,
-        // the gains and the offsets in flight at once.
-        __shared__ float scratch[kWarps];
+        // the gains and the offsets in flight at once.  The mean and the
+        // centred sum reduce through two scratch arrays, one barrier each:
+        // a thread that passes one reduction's barrier knows every thread
+        // has finished reading the other array (callers sync between calls).
+        __shared__ float scratch[2][kWarps];
         constexpr int kPer = (1536 + kThreads - 1) / kThreads;
         for (int rl = 0; rl < rows_in_tile; ++rl) {
+            Trace trl = trace_of(p.profile);
+            trl.begin();
             const size_t row = (size_t)(r0 + rl) * row_step + row_offset;
             const float* x = input + row * d;
             float v[kPer], g[kPer], b[kPer];
@@ -444,7 +463,9 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
             float total = 0.f;
 #pragma unroll
             for (int i = 0; i < kPer; ++i) total += v[i];
-            const float mean = consumer_sum(total, scratch) / (float)d;
+            trl.end(kTrNormLoad);
+            trl.begin();
+            const float mean = consumer_sum_fresh(total, scratch[0]) / (float)d;
             float centred = 0.f;
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
@@ -452,7 +473,7 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
                 const float dv = c < d ? v[i] - mean : 0.f;
                 centred += dv * dv;
             }
-            const float scale = rsqrtf(consumer_sum(centred, scratch) / (float)d + 1e-5f);
+            const float scale = rsqrtf(consumer_sum_fresh(centred, scratch[1]) / (float)d + 1e-5f);
             WT* out = xs + (size_t)rl * ldx;
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
@@ -464,6 +485,7 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
                 }
             }
             for (int c = d + threadIdx.x; c < ldx; c += kThreads) out[c] = Half16<WT>::from_float(0.f);
+            trl.end(kTrNormRest);
         }
         return;
     }
@@ -1103,6 +1125,8 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
         consumer_sync();
         trn.end(kTrNorm);
 
+        Trace trt = trace_of(p.profile);
+        trt.begin();
         bool x_ok[NT];
 #pragma unroll
         for (int j = 0; j < NT; ++j) x_ok[j] = 8 * j + gq < rows_valid;
@@ -1115,6 +1139,11 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
         }
         for (int k = warp; k < count; k += kWarps) {
             const int n0 = (first - lo + k * (int)gridDim.x) * 16;
+            // Lane (g, t) holds rows n0+g and n0+g+8 of input rows 8j+2t, 8j+2t+1;
+            // their mask entries load now, under the tile's products.
+            const int na = n0 + gq, nb = n0 + gq + 8;
+            const bool a_ok = na < p.vocabulary && (p.mask == nullptr || __ldg(p.mask + na) == 0.f);
+            const bool b_ok = nb < p.vocabulary && (p.mask == nullptr || __ldg(p.mask + nb) == 0.f);
             float acc[NT][4];
 #pragma unroll
             for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -1128,10 +1157,6 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
                 tr.end(kTrCompute);
                 release_at(s, index, kWarps);
             }
-            // Lane (g, t) holds rows n0+g and n0+g+8 of input rows 8j+2t, 8j+2t+1.
-            const int na = n0 + gq, nb = n0 + gq + 8;
-            const bool a_ok = na < p.vocabulary && (p.mask == nullptr || __ldg(p.mask + na) == 0.f);
-            const bool b_ok = nb < p.vocabulary && (p.mask == nullptr || __ldg(p.mask + nb) == 0.f);
 #pragma unroll
             for (int j = 0; j < NT; ++j) {
 #pragma unroll
@@ -1186,11 +1211,14 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
             best_i[r0 + rl] = bi;
         }
         mine += count;
+        trt.end(kTrLogitsTiles);
     }
     s.next = base + (unsigned long long)mine * blocks;
     consumer_sync();
 
     // This CTA's candidates, then the fold by whichever CTA finishes last.
+    Trace trf = trace_of(p.profile);
+    trf.begin();
     for (int r = threadIdx.x; r < p.out_rows; r += kThreads) {
         p.candidate_values[(size_t)r * gridDim.x + blockIdx.x] = best_v[r];
         p.candidate_indices[(size_t)r * gridDim.x + blockIdx.x] = best_i[r];
@@ -1198,7 +1226,10 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
     consumer_sync();
     if (threadIdx.x == 0) is_last = arrive_acq_rel(p.logits_counter) == gridDim.x - 1;
     consumer_sync();
-    if (!is_last) return;
+    if (!is_last) {
+        trf.end(kTrLogitsFold);
+        return;
+    }
     const int rows_per_window = p.out_rows / p.windows;
     for (int r = warp; r < p.out_rows; r += kWarps) {
         float bv = -INFINITY;
@@ -1236,6 +1267,7 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
         atomicExch(p.logits_counter, 0u);
         // (The grid barrier after this op releases these writes.)
     }
+    trf.end(kTrLogitsFold);
 }
 
 // ------------------------------------------------ fused out-projection
