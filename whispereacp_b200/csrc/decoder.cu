@@ -870,6 +870,7 @@ private:
             qkv.ld_out = d;
             qkv.self_keys = self_keys_.get<char>() + l * self_layer;
             qkv.self_values = self_values_.get<char>() + l * self_layer;
+            qkv.prefetch_keys = fuse_out ? 1 : 0;
             ops.push_back(qkv);
             StepOp self{};
             self.kind = kOpSelfAttention;
@@ -1085,6 +1086,7 @@ private:
         for (size_t i = 0; i < schedule_host_.size(); ++i) {
             const ScheduleEntry& e = schedule_host_[i];
             if (e.source == 0 && e.bytes == 0) continue;  // the placeholder of an empty schedule
+            if (e.bytes & kPrefetchOnly) continue;          // an L2 prefetch, not a unit
             const size_t bytes = (size_t)e.bytes;
             const size_t lo = (size_t)e.source, hi = lo + bytes;
             auto it = std::upper_bound(ranges.begin(), ranges.end(), std::make_pair(lo, (size_t)-1));

@@ -7,6 +7,7 @@
 #include "step.cuh"
 
 #include <algorithm>
+#include <utility>
 #include <vector>
 
 namespace wsp {
@@ -119,14 +120,66 @@ inline void append_umma_units(const StepParams& p, const StepOp& op, int cta, in
     }
 }
 
-// The per-CTA schedules of a launch, concatenated, and their offsets.
+// What an op reads straight from memory that no op writes, for the
+// producers to prefetch into L2 just ahead of it: LayerNorm gains and
+// offsets, biases, the mask, a fused out-projection's head columns (2 KB of
+// every 16-row tile).
+inline void op_prefetches(const StepParams& p, const StepOp& op,
+                          std::vector<std::pair<const void*, unsigned long long>>& out) {
+    const unsigned long long row = (unsigned long long)p.width * 4;
+    auto add = [&](const void* ptr, unsigned long long bytes) {
+        if (ptr && bytes) out.push_back({ptr, bytes});
+    };
+    switch (op.kind) {
+    case kOpProduct:
+        add(op.gamma, row);
+        add(op.beta, row);
+        add(op.bias, 4ull * op.n);
+        add(op.addend_bias, row);
+        break;
+    case kOpNorm:
+        add(op.gamma, row);
+        add(op.beta, row);
+        break;
+    case kOpLogits:
+        add(p.final_gamma, row);
+        add(p.final_beta, row);
+        if (p.mask)
+            for (unsigned long long o = 0, all = 4ull * p.vocabulary; o < all; o += 4096)
+                add(reinterpret_cast<const unsigned char*>(p.mask) + o, std::min(4096ull, all - o));
+        break;
+    case kOpCrossAttention:
+        add(op.value_bias, row);
+        add(op.gamma, row);
+        add(op.beta, row);
+        add(op.bias, 4ull * op.n);
+        add(op.addend_bias, row);
+        break;
+    }
+    if (op.out_weight) {
+        const int chunks = p.kpd / 32, tiles = (p.width + 15) / 16;
+        for (int h = 0; h < p.heads; ++h)
+            for (int t = 0; t < tiles; ++t)
+                add(static_cast<const unsigned char*>(op.out_weight) + ((size_t)t * chunks + 2 * h) * 1024, 2048);
+    }
+}
+
+// The per-CTA schedules of a launch, concatenated, and their offsets.  Ahead
+// of each op's units, a CTA's schedule carries its share of that op's
+// prefetches (entry j of op k goes to CTA (j + 7k) mod grid).
 inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, int grid, int rt,
                            std::vector<ScheduleEntry>& units, std::vector<unsigned>& offsets) {
     const int stage_chunks = p.stage_bytes / 1024;
     units.clear();
     offsets.assign(1, 0u);
+    std::vector<std::vector<std::pair<const void*, unsigned long long>>> prefetches(ops.size());
+    for (size_t k = 0; k < ops.size(); ++k) op_prefetches(p, ops[k], prefetches[k]);
     for (int cta = 0; cta < grid; ++cta) {
-        for (const StepOp& op : ops) {
+        for (size_t k = 0; k < ops.size(); ++k) {
+            const StepOp& op = ops[k];
+            const auto& pf = prefetches[k];
+            for (size_t j = (size_t)((cta - (long long)(7 * k) % grid + grid) % grid); j < pf.size(); j += grid)
+                units.push_back(ScheduleEntry{(unsigned long long)(size_t)pf[j].first, pf[j].second | kPrefetchOnly});
             if (op.kind == kOpCrossAttention) {
                 append_cross_units(p, op, cta, grid, stage_chunks, units);
                 continue;

@@ -318,6 +318,18 @@ __device__ __forceinline__ void release_unit(Stream& s) {
     ++s.next;
 }
 
+// An L2 prefetch of [ptr, ptr + bytes): a bulk prefetch (no data comes back
+// to the SM, nothing waits for it), which wants 16-byte alignment: the start
+// is rounded down to 16 bytes (never below its allocation, whose start is
+// aligned) and the end down as well.
+__device__ __forceinline__ void prefetch_l2(const void* ptr, unsigned long long bytes) {
+    const unsigned long long start = reinterpret_cast<unsigned long long>(ptr) & ~15ull;
+    const unsigned long long end = (reinterpret_cast<unsigned long long>(ptr) + bytes) & ~15ull;
+    if (end > start)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(start), "r"((unsigned)(end - start))
+                     : "memory");
+}
+
 // The producer warp's lane 0: the CTA's schedule for every step, then a
 // wait for every copy still landing, so none outlives the CTA.
 __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop) {
@@ -327,17 +339,23 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
     unsigned long long u = 0;
     bool go = count > 0;
     for (int step = 0; go && step < p.steps; ++step) {
-        for (unsigned i = 0; i < count; ++i, ++u) {
+        for (unsigned i = 0; i < count; ++i) {
+            const ulonglong2 e = __ldg(schedule + i);
+            if (e.y & kPrefetchOnly) {
+                // Not a unit: an L2 prefetch of data an op ahead reads straight
+                // from memory (its parameters, a fused out-projection's columns).
+                prefetch_l2(reinterpret_cast<const void*>(e.x), (unsigned)e.y);
+                continue;
+            }
             const int stage = (int)(u % s.stages);
             if (u >= (unsigned long long)s.stages &&
                 !wait_parity(p, s.empty + stage, (uint32_t)((u / s.stages - 1) & 1), stop, kWaitEmpty, u)) {
                 go = false;
                 break;
             }
-            const ulonglong2 e = __ldg(schedule + i);
             const uint32_t bar = smem_address(s.full + stage);
             const uint32_t dst = smem_address(s.ring + (size_t)stage * s.stage_bytes);
-            const unsigned bytes = (unsigned)e.y;  // (the high half is unused)
+            const unsigned bytes = (unsigned)e.y;
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
             asm volatile(
                 "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
@@ -345,6 +363,7 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
                 : "memory");
             __threadfence_block();
             *s.armed = u + 1;
+            ++u;
         }
     }
     const unsigned long long stages = (unsigned long long)s.stages;
@@ -2155,79 +2174,31 @@ __device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream
 
 // ----------------------------------------------------------- L2 prefetch
 
-// The weight stream moves ~100 MB or more a step through L2, so the small
-// per-layer parameters (LayerNorm gains and offsets, biases) and the columns
-// a fused out-projection reads straight from memory have left L2 by the
-// time the next step needs them: each would cost its op a DRAM round trip
-// on the critical path.  At the start of each op, thread 0 of every CTA asks
-// L2 for a share of what the op after it reads (a bulk prefetch: no data
-// comes back to the SM, nothing waits for it), so those loads find L2.
-__device__ __forceinline__ void prefetch_l2(const void* ptr, unsigned bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(ptr), "r"(bytes) : "memory");
-}
-
-// Share of op `next`'s parameters for this CTA (all sizes are multiples of
-// 16 bytes and every array starts on a 256-byte boundary).
-__device__ void prefetch_op(const StepParams& p, const StepOp& next, int position) {
-    const unsigned row = (unsigned)p.width * 4u;
+// The weight stream moves ~100 MB or more a step through L2, so data read
+// straight from memory a step after it was last touched has left L2 by
+// then, and each such read would cost its op a DRAM round trip on the
+// critical path.  Static data (parameters, a fused out-projection's columns,
+// the mask) is prefetched by the producer warp from the schedule; what
+// depends on the position is prefetched here by thread 0, from fields of the
+// op it is already running: during the logits, the next step's position
+// rows; during a q/k/v product that asks for it (a few rows), the self keys
+// and values 0 .. position + T - 1 its self attention will read, 4 KB a CTA.
+__device__ void prefetch_rows(const StepParams& p, const StepOp& op, int position) {
     const unsigned cta = blockIdx.x, grid = gridDim.x;
-    auto take = [&](unsigned slot, const void* ptr, unsigned bytes) {
-        if (ptr && bytes && slot % grid == cta) prefetch_l2(ptr, bytes);
-    };
-    switch (next.kind) {
-    case kOpProduct:
-        take(0, next.gamma, row);
-        take(1, next.beta, row);
-        take(2, next.bias, (unsigned)next.n * 4u);
-        take(3, next.addend_bias, row);
-        break;
-    case kOpNorm:
-        take(0, next.gamma, row);
-        take(1, next.beta, row);
-        break;
-    case kOpLogits:
-        take(0, p.final_gamma, row);
-        take(1, p.final_beta, row);
-        if (p.mask) {
-            // The suppression mask, 4 KB a CTA.
-            const unsigned bytes = (unsigned)p.vocabulary * 4u / 16u * 16u;
-            for (unsigned o = (cta + 2) % grid * 4096u; o < bytes; o += grid * 4096u)
-                prefetch_l2(reinterpret_cast<const unsigned char*>(p.mask) + o, min(4096u, bytes - o));
-        }
-        break;
-    case kOpEmbed:
-        // The next step's position rows.
-        if (position + 2 * p.tokens <= p.max_positions)
-            take(0, p.position_table + (size_t)(position + p.tokens) * p.width, row * (unsigned)p.tokens);
-        break;
-    case kOpCrossAttention:
-        take(0, next.value_bias, row);
-        take(1, next.gamma, row);
-        take(2, next.beta, row);
-        take(3, next.bias, (unsigned)next.n * 4u);
-        take(4, next.addend_bias, row);
-        break;
+    if (op.kind == kOpLogits) {
+        if (cta == 0 && position + 2 * p.tokens <= p.max_positions)
+            prefetch_l2(p.position_table + (size_t)(position + p.tokens) * p.width,
+                        (unsigned long long)p.tokens * p.width * 4);
+        return;
     }
-    if (next.kind == kOpSelfAttention && next.out_weight) {
-        // A few rows: each window's self keys and values 0 .. position + T - 1
-        // (last written steps ago, so out of L2 by now), 4 KB a CTA.
-        const unsigned bytes = (unsigned)(position + p.tokens) * (unsigned)p.width * 2u / 16u * 16u;
-        const unsigned per = (bytes + 4095u) / 4096u;
-        for (unsigned i = cta; i < 2u * (unsigned)p.windows * per; i += grid) {
-            const unsigned which = i / per, piece = i % per, b = which >> 1;
-            const void* base = (which & 1) ? next.values : next.keys;
-            const unsigned o = piece * 4096u;
-            prefetch_l2(static_cast<const unsigned char*>(base) + (size_t)b * next.window_stride * 2 + o,
-                        min(4096u, bytes - o));
-        }
-    }
-    if (next.out_weight) {
-        // Head h's columns: 2 KB (chunks 2h, 2h + 1) of every 16-row tile.
-        const int chunks = p.kpd / 32, tiles = (p.width + 15) / 16;
-        for (int i = (int)cta; i < p.heads * tiles; i += (int)grid) {
-            const int h = i / tiles, t = i % tiles;
-            prefetch_l2(static_cast<const unsigned char*>(next.out_weight) + ((size_t)t * chunks + 2 * h) * 1024, 2048u);
-        }
+    if (op.kind != kOpProduct || !op.prefetch_keys) return;
+    const unsigned long long bytes = (unsigned long long)(position + p.tokens) * p.width * 2;
+    const unsigned long long per = (bytes + 4095) / 4096;
+    const unsigned long long window = (unsigned long long)p.max_positions * p.width * 2;
+    for (unsigned long long i = cta; i < 2ull * (unsigned long long)p.windows * per; i += grid) {
+        const unsigned long long which = i / per, o = (i % per) * 4096;
+        const unsigned char* base = static_cast<const unsigned char*>((which & 1) ? op.self_values : op.self_keys);
+        prefetch_l2(base + (which >> 1) * window + o, bytes - o < 4096 ? bytes - o : 4096);
     }
 }
 
@@ -2314,7 +2285,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
         if (stamp && step == 0) p.profile[0] = global_ns();
         for (int i = 0; i < p.n_ops; ++i) {
             const StepOp& op = p.ops[i];
-            if (threadIdx.x == 0) prefetch_op(p, p.ops[i + 1 < p.n_ops ? i + 1 : 0], position);
+            if (threadIdx.x == 0) prefetch_rows(p, op, position);
             Trace tro = trace_of(p.profile);
             tro.begin();
             switch (op.kind) {

@@ -146,6 +146,9 @@ struct StepOp {
     long long addend_stride;
     const float* addend_bias;
     float* sum_out;
+    // q/k/v products (a few rows): prefetch into L2 the self keys and values
+    // the self attention after it reads.
+    int prefetch_keys;
     // Tensor-core products: K splits of each tile's inner size.  With more
     // than one (only when all the items fit one wave of CTAs), each item
     // writes fp32 partials to p.partial_d [split][n_pad][rows_pad], the
@@ -228,10 +231,13 @@ __host__ __device__ inline UmmaItem umma_item(const StepParams& p, const StepOp&
 // One weight-stream unit: a 16-byte aligned source and its size in bytes.
 // Units hold what no op of the launch writes (weights, the token table, the
 // cross keys and values), so the producer may fetch them any time ahead.
+// An entry with kPrefetchOnly set in `bytes` is no unit: the producer asks
+// L2 for that range (an op's parameters and the like) and moves on.
 struct __align__(16) ScheduleEntry {
     unsigned long long source;
     unsigned long long bytes;
 };
+constexpr unsigned long long kPrefetchOnly = 1ull << 32;
 
 __host__ __device__ inline ScheduleEntry schedule_entry(const void* src, unsigned bytes) {
     return ScheduleEntry{(unsigned long long)(size_t)src, (unsigned long long)bytes};
