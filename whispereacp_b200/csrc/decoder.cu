@@ -1097,7 +1097,7 @@ private:
     }
 
     // Stage size: one 16-row tile over kpd (at least 16 KB); as many stages
-    // (2..8) as the shared memory left by the work area holds.
+    // (2..kMaxStreamStages) as the shared memory left by the work area holds.
     int stage_bytes_for_width() const {
         const int tile = 16 * padded(shape_.width) * 2;
         return std::max(16384, (tile + 1023) / 1024 * 1024);
@@ -1109,7 +1109,7 @@ private:
         // (The kernel's static shared memory -- barriers, flags, a fused
         // out-projection's input row -- comes out of the same budget.)
         const long long room = (long long)max_shared_ - kStaticSharedBytes - (long long)work;
-        p.stages = (int)std::min<long long>(8, room / p.stage_bytes);
+        p.stages = (int)std::min<long long>(kMaxStreamStages, room / p.stage_bytes);
         if (p.stages < 2) throw CudaFailure("the decode kernel's shared memory does not fit", false);
     }
 

@@ -2204,7 +2204,7 @@ __device__ void prefetch_rows(const StepParams& p, const StepOp& op, int positio
 
 // -------------------------------------------------------------- the kernel
 
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = kMaxStreamStages;
 
 // Consumers leave together; warp 0 frees the tensor memory (every product
 // that wrote it has completed: each item waited for its commit).

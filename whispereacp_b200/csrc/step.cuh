@@ -43,6 +43,8 @@ constexpr int kMaxCrossUnitKeys = 256;
 constexpr int kMaxCrossSplits = 32;
 // Join counters per op of a split tensor-core product.
 constexpr int kSplitSlots = 128;
+// Most stages of a CTA's weight-stream ring (as many as shared memory holds).
+constexpr int kMaxStreamStages = 12;
 
 enum OpKind : int {
     kOpEmbed = 0,
