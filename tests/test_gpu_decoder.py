@@ -219,6 +219,33 @@ def test_windows_are_independent_sequences(windows, tokens):
         assert worst_error(second.hidden[b], hidden[tokens:]) <= bound
 
 
+def test_few_row_steps_fuse_the_out_projections():
+    """Steps of at most 8 rows run the attention out-projections and the cross
+    query inside the attention ops, the heads' partials summed by the next
+    op's LayerNorm: 4 windows, a 2-token prompt (8 rows) then single tokens
+    (4 rows), each window against its own oracle sequence."""
+    storage = "float16"
+    windows, singles = 4, 4
+    tensors = stored_tensors(O.synthetic_decoder_tensors(MID_SHAPE, first_seed=7100), storage)
+    base = O.synthetic_encoder_output(MID_SHAPE.cross_positions, MID_SHAPE.width)
+    encoders = np.stack([(base * (1.0 + 0.07 * b) - 0.03 * b).astype(np.float32) for b in range(windows)])
+    rng = np.random.default_rng(71)
+    ids = rng.integers(0, MID_SHAPE.vocabulary_size, size=(windows, 2 + singles)).astype(np.uint32)
+    decoder = make_decoder(MID_SHAPE, tensors, storage, windows=windows)
+    decoder.begin_sequence(encoders)
+    results = [decoder.step(ids[:, :2])] + [decoder.step(ids[:, 2 + i:3 + i]) for i in range(singles)]
+    bound = MID_TOLERANCE[storage]
+    for b in range(windows):
+        hidden, logits = O.reference_decode(MID_SHAPE, tensors, encoders[b], ids[b])
+        row = 0
+        for result in results:
+            rows = result.logits.shape[1]
+            assert worst_error(result.logits[b], logits[row:row + rows]) <= bound
+            assert worst_error(result.hidden[b], hidden[row:row + rows]) <= bound
+            row += rows
+    assert decoder.position == 2 + singles
+
+
 # --- Argmax, Tests/Kernels/ArgmaxTests.cpp through wsp_argmax ----------------------------------
 
 def run_argmax(logits: np.ndarray, mask: np.ndarray | None):

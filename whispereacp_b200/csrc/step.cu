@@ -810,6 +810,15 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
         const int r_tile = item / n_tiles, n_tile = item % n_tiles;
         const int r0 = r_tile * RT, n0 = n_tile * 16;
         const int rows_valid = min(RT, p.rows - r0);
+        // This thread's outputs' biases, loaded now so the epilogue does not
+        // wait on memory for them.
+        constexpr int kOuts = (16 * RT + kThreads - 1) / kThreads;
+        float bias_of[kOuts];
+#pragma unroll
+        for (int k = 0; k < kOuts; ++k) {
+            const int n = n0 + (threadIdx.x + k * kThreads) / RT;
+            bias_of[k] = op.bias && threadIdx.x + k * kThreads < 16 * RT && n < op.n ? __ldg(op.bias + n) : 0.f;
+        }
         float acc[NT][4];
         bool ok;
         if (normalise || op.kp == p.kpd) {
@@ -845,13 +854,14 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
         Trace tre = trace_of(p.profile);
         tre.begin();
         product_reduce<NT>(red, acc);
-        for (int o = threadIdx.x; o < 16 * RT; o += kThreads) {
+#pragma unroll
+        for (int k = 0; k < kOuts; ++k) {
+            const int o = threadIdx.x + k * kThreads;
+            if (o >= 16 * RT) break;
             const int nl = o / RT, rl = o % RT;
             const int n = n0 + nl, r = r0 + rl;
             if (n >= op.n || rl >= rows_valid) continue;
-            float v = product_sum(red, RT, nl, rl);
-            if (op.bias) v += op.bias[n];
-            emit_output<WT>(p, op, position, n, r, v);
+            emit_output<WT>(p, op, position, n, r, product_sum(red, RT, nl, rl) + bias_of[k]);
         }
         consumer_sync();
         tre.end(kTrEpilogue);
@@ -1003,11 +1013,12 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
         if (warp < 4) {
             Trace tr = trace_of(p.profile);
             tr.begin();
+            // (The bias loads while the products finish.)
+            const int n = m * 128 + 32 * warp + lane;
+            const float bias = op.bias && n < op.n ? __ldg(op.bias + n) : 0.f;
             wait_parity(p, tm.done, tm.phase, nullptr, kWaitUnit, (unsigned long long)item);
             __syncwarp();
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const int n = m * 128 + 32 * warp + lane;
-            const float bias = op.bias && n < op.n ? __ldg(op.bias + n) : 0.f;
             for (int c0 = 0; c0 < n16; c0 += 32) {
                 uint32_t v[32];
                 tmem_load32(tm.base + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
