@@ -1932,6 +1932,12 @@ __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int he
                             unsigned char* area, float* q) {
     const int pitch = tile_pitch(p.kpd), D = p.head_width;
     WT* xs = reinterpret_cast<WT*>(area);
+    // The q biases of this lane's two rows, loaded with the LayerNorm's rows.
+    const int tiles = round16(D) / 16, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qn = 16 * warp + (lane >> 2);
+    const float* qbias = op.bias + head * round16(D);
+    const float bias_a = warp < tiles && qn < D ? __ldg(qbias + qn) : 0.f;
+    const float bias_b = warp < tiles && qn + 8 < D ? __ldg(qbias + qn + 8) : 0.f;
     Addends add;
     if (op.addend_count > 0)
         add = Addends{op.addends, op.addend_count, op.addend_stride, op.addend_bias, keep_sum ? op.sum_out : nullptr};
@@ -1940,7 +1946,6 @@ __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int he
     consumer_sync();
     // Warp j < tiles owns q tile j (one unit: a stage holds a whole tile)
     // over all of K, so no partial sums cross warps.
-    const int tiles = round16(D) / 16, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < tiles) {
         const unsigned long long index = s.next + warp;
         const unsigned char* unit = owned_unit_at(p, s, index);
@@ -1950,10 +1955,8 @@ __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int he
         release_at(s, index, kWarps);
         // Column 0 (the one row) sits in lanes t == 0: q rows g and g + 8 of the tile.
         if ((lane & 3) == 0) {
-            const int n = 16 * warp + (lane >> 2);
-            const float* bias = op.bias + head * round16(D);
-            if (n < D) q[n] = (acc[0][0] + __ldg(bias + n)) * p.scale;
-            if (n + 8 < D) q[n + 8] = (acc[0][2] + __ldg(bias + n + 8)) * p.scale;
+            if (qn < D) q[qn] = (acc[0][0] + bias_a) * p.scale;
+            if (qn + 8 < D) q[qn + 8] = (acc[0][2] + bias_b) * p.scale;
         }
     }
     s.next += tiles;
