@@ -8,13 +8,16 @@ values from the encoder rows), the prompt step, and greedy single-token steps
 until `steps` tokens per window are sampled -- WhisperEACP's decodeTranscript
 with no end-of-text stop.  The metric counts sampled tokens.
 
-Multi-GPU (torchrun, one process per GPU): every rank decodes its own batch
-of windows (weak scaling, no collective on the data path); the time is the
-maximum over ranks and the value is all ranks' tokens over that time.
+The default configuration is medium.en with 64 windows (bf16).  Multi-GPU
+(torchrun, one process per GPU): the batch's windows are split evenly over
+the ranks (strong scaling; every rank holds the weights and decodes its own
+windows, no collective on the data path); the time is the maximum over
+ranks and the value is the batch's tokens over that time.  Rank 0 also
+times base.en at one window (the batch-1 milliseconds per token step).
 
 `--impl reference` times the reference's own CPU decoder (its scalar test
 decoder, compiled from its sources into oracle/_ref/libref_decoder.so) on the
-host cores, on rank 0 only.
+host cores, on rank 0 only, on a bounded sample of the configuration.
 """
 from __future__ import annotations
 
@@ -36,7 +39,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decoder tokens/s"
 UNIT = "tokens/s"
-DEFAULT_CONFIG = "base_en_b1"
+DEFAULT_CONFIG = "medium_en_b64"
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -48,6 +51,7 @@ def parse_args():
     p.add_argument("--config", default=DEFAULT_CONFIG)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-batch1", action="store_true", help="skip the extra base.en batch-1 timing")
     p.add_argument("--tokens", type=int, default=0,
                    help="tokens per window (default: the config's); smaller for profiler captures")
     p.add_argument("--windows", type=int, default=0,
@@ -140,17 +144,15 @@ def committed_traffic(kernel: str, config: str):
     return float(match.group(1)) if match else None
 
 
-def step_bytes(run, mean_keys: float) -> dict:
-    """Algorithmic bytes of one single-token step (16-bit weights and caches):
-    w_b*(L*(6d^2 + 2dF) + V*d) + B*L*2d*(X + t + 1)*kv_b."""
+def step_bytes(run, windows: int, mean_keys: float) -> dict:
+    """Algorithmic bytes of one single-token step of `windows` windows on one
+    GPU (16-bit weights and caches): w_b*(L*(6d^2 + 2dF) + V*d) +
+    B*L*2d*(X + t + 1)*kv_b."""
     s = run.shape
     d, L, F, V, X = s.width, s.layers, s.feed_forward_width, s.vocabulary_size, s.cross_positions
     weights = 2 * (L * (6 * d * d + 2 * d * F) + V * d)
-    kv = run.windows * L * 2 * d * (X + mean_keys) * 2
-    return {"weights": weights, "kv": kv, "logits_launch": 2 * V * d,
-            "cross_launch": run.windows * 2 * d * X * 2,
-            "projection_launch": 2 * (6 * d * d + 2 * d * F) / 6,
-            "self_launch": run.windows * 2 * d * (mean_keys + 1) * 2}
+    kv = windows * L * 2 * d * (X + mean_keys) * 2
+    return {"weights": weights, "kv": kv}
 
 
 def cpu_baseline_port(run, tensors, encoder, threads: int) -> dict:
@@ -177,25 +179,88 @@ def cpu_baseline_port(run, tensors, encoder, threads: int) -> dict:
 
 # --------------------------------------------------------------------- ours
 
+def rank_encoder_rows(run, windows) -> np.ndarray:
+    """This rank's encoder rows: window w of the batch is seeded by w alone, so
+    a window's rows do not depend on how the batch is split across ranks."""
+    from whispereacp_b200 import synthetic as S
+    shape = run.shape
+    out = np.empty((len(windows), shape.cross_positions, shape.width), np.float32)
+    for i, w in enumerate(windows):
+        out[i] = S.encoder_output(1, shape.cross_positions, shape.width, seed=1000 + w)[0]
+    return out
+
+
+def time_transcriptions(decoder, device_rows, tokens_per_window, steps, stream, flush):
+    """Device-timed transcriptions (CUDA events on the decoder's stream, the L2
+    flushed before each, outside the timed interval) and each one's phases."""
+    import torch
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    phases = []
+    for i in range(steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            starts[i].record(stream)
+        decoder.enqueue_transcribe(device_rows.data_ptr(), tokens_per_window)
+        stops[i].record(stream)
+        # The step's own launches, from the decoder's CUDA events on the same
+        # stream (this waits for the step; the next flush is queued after).
+        phases.append(decoder.phase_ms())
+    decoder.synchronize()
+    return sum(a.elapsed_time(b) for a, b in zip(starts, stops)), phases
+
+
+def batch1_line(args, local, flush, peak):
+    """base.en at one window (configuration C2's decoder), timed on this GPU:
+    the batch-1 milliseconds per single-token step and their roofline share."""
+    import torch
+    from whispereacp_b200 import Decoder, synthetic as S
+    run = S.CONFIGS["base_en_b1"]
+    shape = run.shape
+    decoder = Decoder(shape, windows=1, device=local, storage=run.storage)
+    decoder.load_weights(S.normal_weights(shape, seed=0))
+    first, later = S.suppression_masks(shape.vocabulary_size)
+    decoder.set_generation(run.prompt, first, later, maximum_tokens=run.steps,
+                           end_of_text=S.END_OF_TEXT, stop_at_end_of_text=False)
+    stream = torch.cuda.ExternalStream(decoder.stream, device=local)
+    rows = torch.from_numpy(S.encoder_output(1, shape.cross_positions, shape.width, seed=1)).to(f"cuda:{local}")
+    for _ in range(3):
+        decoder.enqueue_transcribe(rows.data_ptr(), run.steps)
+    decoder.synchronize()
+    _, phases = time_transcriptions(decoder, rows, run.steps, max(3, min(args.steps, 10)), stream, flush)
+    decoder.close()
+    later_steps = run.steps - 1
+    launch_ms = statistics.median(p["steps"] for p in phases)
+    per_step = sum(step_bytes(run, 1, len(run.prompt) + later_steps / 2).values())
+    ms = launch_ms / later_steps
+    return {"workload": run.description, "ms_per_token_step": ms, "tokens_per_s": 1e3 / ms,
+            "algorithmic_bytes_per_token_step": per_step,
+            "roofline_frac": per_step / (ms * 1e-3) / 1e9 / peak}
+
+
 def run_ours(args, run):
     import torch
     from whispereacp_b200 import Decoder, synthetic as S
-    from whispereacp_b200.ranks import max_over_ranks
+    from whispereacp_b200.ranks import max_over_ranks, window_range
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
         import torch.distributed as dist
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
 
     shape = run.shape
     tokens_per_window = args.tokens or run.steps
+    # The batch's windows split evenly over the ranks (strong scaling): rank
+    # r decodes windows window_range(total, r, world) with its own weights.
+    mine = window_range(run.windows, rank, world)
+    windows = len(mine)
     tensors = S.normal_weights(shape, seed=0)
-    encoder = S.encoder_output(run.windows, shape.cross_positions, shape.width, seed=1 + rank)
+    encoder = rank_encoder_rows(run, mine)
     first, later = S.suppression_masks(shape.vocabulary_size)
 
-    decoder = Decoder(shape, windows=run.windows, device=local, storage=run.storage, products=args.products)
+    decoder = Decoder(shape, windows=windows, device=local, storage=run.storage, products=args.products)
     decoder.load_weights(tensors)
     decoder.set_generation(run.prompt, first, later, maximum_tokens=tokens_per_window,
                            end_of_text=S.END_OF_TEXT, stop_at_end_of_text=False)
@@ -204,36 +269,20 @@ def run_ours(args, run):
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{local}")
     torch.cuda.synchronize()
 
-    def one_step():
-        decoder.enqueue_transcribe(device_rows.data_ptr(), tokens_per_window)
-
     for _ in range(args.warmup):
-        one_step()
+        decoder.enqueue_transcribe(device_rows.data_ptr(), tokens_per_window)
     decoder.synchronize()
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     clocks = ClockSampler(local)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     clocks.start()
-    phases = []
-    for i in range(args.steps):
-        with torch.cuda.stream(stream):
-            flush.zero_()              # L2 flush, outside the timed intervals
-            starts[i].record(stream)
-        one_step()
-        stops[i].record(stream)
-        # The step's own launches, from the decoder's CUDA events on the same
-        # stream (this waits for the step; the next flush is queued after).
-        phases.append(decoder.phase_ms())
-    decoder.synchronize()
+    elapsed_ms, phases = time_transcriptions(decoder, device_rows, tokens_per_window, args.steps, stream, flush)
     torch.cuda.synchronize()
     clock_record = clocks.stop()
     if world > 1:
         torch.distributed.barrier()
-    elapsed_ms = sum(s.elapsed_time(e) for s, e in zip(starts, stops))
     transcript = decoder.read_transcript()
     assert all(len(t) == tokens_per_window for t in transcript)
 
@@ -251,54 +300,61 @@ def run_ours(args, run):
             e2e_ms.append(start.elapsed_time(stop))
     e2e_step_ms = statistics.median(e2e_ms)
 
-    # Per-kernel launch durations, measured live (events around each launch).
+    # Per-op times of the single-token step, measured live.
     decoder.enqueue_transcribe(device_rows.data_ptr(), 2)
     per_kernel = decoder.time_kernels(min(64, shape.max_positions - len(run.prompt) - 2, tokens_per_window))
     decoder.synchronize()
+    launches = decoder.step_launches()
+    decoder.close()
 
     step_ms = elapsed_ms / args.steps
     # The slowest rank's device-timed step (an all-reduce MAX over NCCL).
     step_ms, e2e_step_ms = max_over_ranks([step_ms, e2e_step_ms], device=f"cuda:{local}")
 
-    tokens = run.windows * tokens_per_window * world
+    peak, peak_kind = peaks()
+    extra = batch1_line(args, local, flush, peak) if rank == 0 and not args.no_batch1 else None
+    if world > 1:
+        torch.distributed.barrier()
+    tokens = run.windows * tokens_per_window
     result = None
     if rank == 0:
-        peak, peak_kind = peaks()
         # The dominant kernel: the decode kernel's launch that runs every
         # single-token step of the transcription (the prompt launch and the
-        # sequence start are the rest of the step).
+        # sequence start are the rest of the step), on this rank's windows.
         later_steps = tokens_per_window - 1
         mean_keys = len(run.prompt) + later_steps / 2
-        nbytes = step_bytes(run, mean_keys)
+        nbytes = step_bytes(run, windows, mean_keys)
         per_step_bytes = nbytes["weights"] + nbytes["kv"]
         launch_ms = statistics.median(p["steps"] for p in phases)
         algorithmic = later_steps * per_step_bytes
         achieved = algorithmic / (launch_ms * 1e-3) / 1e9 if launch_ms > 0 else 0.0
         traffic_step = committed_traffic("decode_kernel", run.name)
         h2d = encoder.nbytes
-        d2h = run.windows * (shape.max_positions + 1) * 4
+        d2h = windows * (shape.max_positions + 1) * 4
         result = {
             "metric": METRIC, "value": tokens / (step_ms * 1e-3), "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": step_ms, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "f16" if run.storage == "float16" else "bf16",
             "data": "synthetic (random-init weights N(0,0.02), encoder rows N(0,1))",
-            "config": {"workload": run.description, "name": run.name, "windows_per_gpu": run.windows,
-                       "tokens_per_window": tokens_per_window, "prompt": list(run.prompt),
-                       "cross_positions": shape.cross_positions, "d_model": shape.width,
-                       "decoder_layers": shape.layers, "vocabulary": shape.vocabulary_size,
+            "config": {"workload": run.description, "name": run.name, "windows": run.windows,
+                       "windows_per_gpu": windows, "tokens_per_window": tokens_per_window,
+                       "prompt": list(run.prompt), "cross_positions": shape.cross_positions,
+                       "d_model": shape.width, "decoder_layers": shape.layers,
+                       "vocabulary": shape.vocabulary_size,
                        "step": "sequence start + prompt step + greedy single-token steps (one persistent launch)",
-                       "l2": "flushed (256 MiB write) between timed steps, outside the timed intervals",
-                       "parallelism": f"dp{world} (independent windows per GPU)",
+                       "l2": "flushed (256 MiB write) between timed steps, outside the timed intervals; "
+                             "the cross keys and values alone exceed L2",
+                       "parallelism": f"dp{world} ({run.windows} windows split evenly across the GPUs)",
                        "products": args.products},
-            "batch1_ms_per_token_step": launch_ms / max(1, later_steps),
             "e2e": {"value": tokens / (e2e_step_ms * 1e-3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * decoder.step_launches(),
+            "gpu_launches": args.steps * launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": traffic_step * later_steps if traffic_step else None,
-                         "kernel": "decode_kernel (launch of the single-token steps)",
+                         "kernel": "decode_kernel (launch of the single-token steps), rank 0's windows",
                          "peak_source": f"{peak_kind} hbm_gbs (burst)",
                          "algorithmic_bytes_per_launch": algorithmic,
                          "algorithmic_bytes_per_token_step": per_step_bytes,
@@ -308,11 +364,13 @@ def run_ours(args, run):
                               for k, v in per_kernel.items() if v[1]},
             "clocks": clock_record,
         }
+        if extra is not None:
+            result["batch1"] = extra
+            result["batch1_ms_per_token_step"] = extra["ms_per_token_step"]
         if not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
             result["cpu_baseline"] = cpu_baseline_port(run, tensors_for_oracle(tensors, run.storage),
                                                        encoder, threads)
-    decoder.close()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -330,8 +388,18 @@ def run_reference(args, run):
     """The reference's own CPU decoder (Tests/Decoder/Common.h:360-468, compiled
     from its sources) as a greedy decoder: each generated token is one
     referenceDecode over the prefix, which is how that implementation decodes.
-    All host threads decode independent windows at once (ctypes releases the GIL)."""
+    All host threads decode independent windows at once (ctypes releases the GIL).
+
+    One token of a 24- or 32-layer decoder takes that code minutes, so a step
+    is a bounded sample of the same workload: every thread decodes one token
+    of a ONE-layer decoder of the configured architecture (the same width,
+    heads, feed-forward width, vocabulary and 1500 encoder rows).  A token's
+    cost is fixed (embedding, final norm, logits) plus L times a layer's
+    (its cross keys and values, its three sublayers): a one-off two-layer
+    decode before the warm-up separates the two, and the value is the
+    configured L-layer decoder's tokens/s on all threads."""
     from concurrent.futures import ThreadPoolExecutor
+    from dataclasses import replace
     from oracle import oracle as O
     from whispereacp_b200 import synthetic as S
     from tests.golden.make_golden import load_reference, ref_decode
@@ -343,34 +411,46 @@ def run_reference(args, run):
     if not os.path.exists(path):
         return {"impl": "reference", "unavailable": "oracle/_ref/libref_decoder.so was not built"}
     ref, _ = load_reference()
-    shape = O.Shape(**run.shape.__dict__)
-    tensors = tensors_for_oracle(S.normal_weights(run.shape, seed=0), run.storage)
-    encoder = S.encoder_output(1, shape.cross_positions, shape.width, seed=1)[0]
+    layers = run.shape.layers
     threads = os.cpu_count() or 1
     prefix = [*run.prompt, 50, 51]
-
-    def one_token(_):
-        ref_decode(ref, shape, tensors, encoder, prefix)
-        return 1
-
+    encoder = S.encoder_output(1, run.shape.cross_positions, run.shape.width, seed=1)[0]
     pool = ThreadPoolExecutor(max_workers=threads)
-    for _ in range(args.warmup):
-        list(pool.map(one_token, range(threads)))
-    times = []
-    for _ in range(args.steps):
+
+    def decoder_of(count):
+        shape = replace(run.shape, layers=count)
+        return O.Shape(**shape.__dict__), tensors_for_oracle(S.normal_weights(shape, seed=0), run.storage)
+
+    def all_threads(model):
+        shape, tensors = model
         t0 = time.perf_counter()
-        list(pool.map(one_token, range(threads)))
-        times.append(time.perf_counter() - t0)
+        list(pool.map(lambda _: ref_decode(ref, shape, tensors, encoder, prefix), range(threads)))
+        return time.perf_counter() - t0
+
+    one, two = decoder_of(1), decoder_of(2)
+    all_threads(one)
+    all_threads(two)
+    t_two = all_threads(two)
+    for _ in range(args.warmup):
+        all_threads(one)
+    times = [all_threads(one) for _ in range(args.steps)]
     pool.shutdown()
-    step_s = sum(times) / len(times)
-    value = threads / step_s
-    sample = (f"{threads} concurrent referenceDecode calls (one per host thread), each over a "
-              f"{len(prefix)}-token prefix with {shape.cross_positions} encoder rows: one generated "
-              f"token each, the cost of one greedy step in that implementation")
+    t_one = sum(times) / len(times)
+    # A layer costs at most the whole one-layer token (the fixed part is not negative).
+    per_layer = min(max(t_two - t_one, 0.0), t_one)
+    token_s = (t_one - per_layer) + layers * per_layer
+    value = threads / token_s
+    sample = (f"each step: {threads} concurrent referenceDecode calls (one per host thread) of a 1-layer "
+              f"decoder of this architecture over a {len(prefix)}-token prefix and "
+              f"{run.shape.cross_positions} encoder rows ({t_one:.2f} s); a 2-layer run ({t_two:.2f} s) "
+              f"splits that into a fixed part and a per-layer part, extrapolated to {layers} layers "
+              f"({token_s:.1f} s a token on every thread)")
     return {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": run.description, "name": run.name}, "impl": "reference",
+            "warmup": args.warmup, "ms_per_step": t_one * 1e3, "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic", "config": {"workload": run.description, "name": run.name,
+                                            "windows": run.windows},
+            "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
                              "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

@@ -144,7 +144,9 @@ int wsp_decoder_cross_positions(const wsp_decoder* decoder, int* cross_positions
  * (buildPrompt, :207-225), the two suppression masks (buildSuppressionMasks,
  * :227-254; fp32 [vocabulary], nonzero = suppressed; the first applies to the
  * prompt step only), the token limit (maximumTokens, 448 - prompt) and the
- * end-of-text id that stops a window.
+ * end-of-text id that stops a window.  The call first waits for any
+ * transcription still queued on the decoder's stream, which reads the
+ * previous masks and prompt.
  */
 typedef struct wsp_generation_config {
     const uint32_t* prompt;
@@ -261,12 +263,11 @@ int wsp_argmax(const float* logits, const float* mask, uint32_t* indices, int ro
 /*
  * wsp_argmax for callers that must not allocate device memory: the same
  * masked argmax, the same result, but no cudaMalloc, cudaMallocAsync,
- * cudaFree or allocating library call.  No counterpart in the reference
- * (Argmax::encode, Argmax.h:207-262, records into buffers KernelNet sized up
- * front); it is for host code that cannot enter the CUDA allocator -- a
- * real-time audio thread, where an allocation may block on driver locks or
- * wait on other work in the stream's pool, or a runtime that has already
- * reserved every byte of its memory budget.
+ * cudaFree or allocating library call.  No counterpart in the reference.
+ * It is for host code that cannot enter the CUDA allocator -- a real-time
+ * audio thread, where an allocation may block on driver locks or wait on
+ * other work in the stream's pool, or a runtime that has already reserved
+ * every byte of its memory budget.
  *
  * Its scratch is a fixed 512 KB array inside this library (static device
  * memory, loaded with the module), so row_count x ceil(row_length / 2048)
@@ -276,7 +277,10 @@ int wsp_argmax(const float* logits, const float* mask, uint32_t* indices, int ro
  *
  * The first call on a device looks the scratch's address up
  * (cudaGetSymbolAddress) with that device current and remembers it: make
- * that first call during set-up, before any stream capture.  The call works
+ * that first call during set-up, before any stream capture.  The address
+ * lives as long as the device's context: after cudaDeviceReset (or anything
+ * else that destroys the primary context) the remembered address is stale,
+ * so do not call this entry point again in that process.  The call works
  * on the current device; logits, mask and indices are device pointers there.
  * It queues two kernels on `stream` (NULL: the legacy stream) and returns
  * without waiting; indices hold the result once the stream has passed them.

@@ -218,22 +218,105 @@ static void layer_norm(const double* rows, int row_count, int width,
     }
 }
 
-/* Tests/Encoder/Common.h:483-507: nn.Linear, weight [out, inner]; bias NULL for k_proj. */
+/*
+ * Tests/Encoder/Common.h:483-507: nn.Linear, weight [out, inner]; bias NULL for
+ * k_proj.  Every output is its bias plus x[step] * w[step] added in step
+ * order, exactly the reference's loop.  Only the order in which outputs are
+ * visited differs: tiles of LINEAR_ROWS input rows x LINEAR_COLUMNS weight
+ * rows, so a tile's weight rows stay in cache across its input rows, with
+ * four outputs' sums carried side by side (each still in step order).  The
+ * results are bit-identical to the one-output-at-a-time loop.
+ */
+#define LINEAR_ROWS 32
+#define LINEAR_COLUMNS 16
+/* One output: bias + x . w in step order. */
+static double linear_one(const double* x, const float* w, const float* bias, int column, int inner)
+{
+    double total = bias == NULL ? 0.0 : (double)bias[column];
+    for (int step = 0; step < inner; ++step)
+        total += x[step] * (double)w[step];
+    return total;
+}
+
 static void linear(const double* input, int row_count, int inner,
                    const float* weight, const float* bias, int out_width,
                    double* out, int threads)
 {
     long total_outputs = (long)row_count * out_width;
-#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1) if (threads > 1 && total_outputs > 4096)
-    for (long at = 0; at < total_outputs; ++at) {
-        int row = (int)(at / out_width);
-        int column = (int)(at % out_width);
-        const double* x = input + (size_t)row * inner;
-        const float* w = weight + (size_t)column * inner;
-        double total = bias == NULL ? 0.0 : (double)bias[column];
-        for (int step = 0; step < inner; ++step)
-            total += x[step] * (double)w[step];
-        out[at] = total;
+    long row_tiles = (row_count + LINEAR_ROWS - 1) / LINEAR_ROWS;
+    long column_tiles = (out_width + LINEAR_COLUMNS - 1) / LINEAR_COLUMNS;
+    long tiles = row_tiles * column_tiles;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads > 0 ? threads : 1) if (threads > 1 && total_outputs > 4096)
+    for (long tile = 0; tile < tiles; ++tile) {
+        int c0 = (int)(tile % column_tiles) * LINEAR_COLUMNS;
+        int r0 = (int)(tile / column_tiles) * LINEAR_ROWS;
+        int c1 = c0 + LINEAR_COLUMNS < out_width ? c0 + LINEAR_COLUMNS : out_width;
+        int r1 = r0 + LINEAR_ROWS < row_count ? r0 + LINEAR_ROWS : row_count;
+        int row = r0;
+        /* two input rows by four weight rows: eight sums, each in step order */
+        for (; row + 2 <= r1; row += 2) {
+            const double* x = input + (size_t)row * inner;
+            const double* x2 = x + inner;
+            double* y = out + (size_t)row * out_width;
+            double* y2 = y + out_width;
+            int column = c0;
+            for (; column + 4 <= c1; column += 4) {
+                const float* w0 = weight + (size_t)column * inner;
+                const float* w1 = w0 + inner;
+                const float* w2 = w1 + inner;
+                const float* w3 = w2 + inner;
+                double b0 = bias == NULL ? 0.0 : (double)bias[column];
+                double b1 = bias == NULL ? 0.0 : (double)bias[column + 1];
+                double b2 = bias == NULL ? 0.0 : (double)bias[column + 2];
+                double b3 = bias == NULL ? 0.0 : (double)bias[column + 3];
+                double t0 = b0, t1 = b1, t2 = b2, t3 = b3;
+                double u0 = b0, u1 = b1, u2 = b2, u3 = b3;
+                for (int step = 0; step < inner; ++step) {
+                    double xv = x[step], xw = x2[step];
+                    double v0 = w0[step], v1 = w1[step], v2 = w2[step], v3 = w3[step];
+                    t0 += xv * v0;
+                    t1 += xv * v1;
+                    t2 += xv * v2;
+                    t3 += xv * v3;
+                    u0 += xw * v0;
+                    u1 += xw * v1;
+                    u2 += xw * v2;
+                    u3 += xw * v3;
+                }
+                y[column] = t0; y[column + 1] = t1; y[column + 2] = t2; y[column + 3] = t3;
+                y2[column] = u0; y2[column + 1] = u1; y2[column + 2] = u2; y2[column + 3] = u3;
+            }
+            for (; column < c1; ++column) {
+                const float* w = weight + (size_t)column * inner;
+                y[column] = linear_one(x, w, bias, column, inner);
+                y2[column] = linear_one(x2, w, bias, column, inner);
+            }
+        }
+        for (; row < r1; ++row) {
+            const double* x = input + (size_t)row * inner;
+            double* y = out + (size_t)row * out_width;
+            int column = c0;
+            for (; column + 4 <= c1; column += 4) {
+                const float* w0 = weight + (size_t)column * inner;
+                const float* w1 = w0 + inner;
+                const float* w2 = w1 + inner;
+                const float* w3 = w2 + inner;
+                double t0 = bias == NULL ? 0.0 : (double)bias[column];
+                double t1 = bias == NULL ? 0.0 : (double)bias[column + 1];
+                double t2 = bias == NULL ? 0.0 : (double)bias[column + 2];
+                double t3 = bias == NULL ? 0.0 : (double)bias[column + 3];
+                for (int step = 0; step < inner; ++step) {
+                    double xv = x[step];
+                    t0 += xv * (double)w0[step];
+                    t1 += xv * (double)w1[step];
+                    t2 += xv * (double)w2[step];
+                    t3 += xv * (double)w3[step];
+                }
+                y[column] = t0; y[column + 1] = t1; y[column + 2] = t2; y[column + 3] = t3;
+            }
+            for (; column < c1; ++column)
+                y[column] = linear_one(x, weight + (size_t)column * inner, bias, column, inner);
+        }
     }
 }
 

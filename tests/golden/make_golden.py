@@ -3,7 +3,7 @@
 Run where the WhisperEACP checkout is (it needs oracle/_ref/, which
 oracle/Makefile compiles from the reference's sources):
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle REF=<reference checkout> && python tests/golden/make_golden.py
 
 Every array in the fixture comes out of the reference's scalar test decoder
 (Tests/Decoder/Common.h:258-500 with Tests/Encoder/Common.h:390-507) or its

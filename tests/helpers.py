@@ -15,15 +15,24 @@ def round_to(storage: str, values: np.ndarray) -> np.ndarray:
     values = np.asarray(values, dtype=np.float32)
     if storage == "float16":
         return values.astype(np.float16).astype(np.float32)
-    bits = values.view(np.uint32).astype(np.uint64)
-    rounded = ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16) << 16
-    return rounded.astype(np.uint32).view(np.float32)
+    # round to nearest even on the top 16 bits (finite values: the sum
+    # cannot wrap below the NaN patterns)
+    bits = values.view(np.uint32)
+    rounded = (bits + np.uint32(0x7FFF) + ((bits >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xFFFF0000)
+    return rounded.view(np.float32)
 
 
 def stored_tensors(tensors: dict, storage: str) -> dict:
     """The tensors as the CUDA path holds them, widened back to fp32 for the oracle."""
-    return {name: (round_to(storage, v) if name.endswith(NARROWED) else v)
-            for name, v in tensors.items()}
+    from concurrent.futures import ThreadPoolExecutor
+    import os
+
+    def one(item):
+        name, v = item
+        return name, (round_to(storage, v) if name.endswith(NARROWED) else v)
+
+    with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as pool:
+        return dict(pool.map(one, tensors.items()))
 
 
 def shape_of(o: O.Shape):

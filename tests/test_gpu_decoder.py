@@ -4,8 +4,8 @@ Each test here is one of Tests/Decoder/DecoderTests.cpp's, run through the C
 ABI on the same inputs (smallDecoderShape, syntheticDecoderFile's weights,
 syntheticEncoderOutput, the same prompts).  The reference asserts 5e-6
 against fp32 kernels; this decoder stores weights, activations and caches in
-16 bits with fp32 accumulation, so the bound is the one the north star sets
-for that arithmetic: logits within 2e-2 (here in the reference's own
+16 bits with fp32 accumulation, so the bound is the one set for that
+arithmetic across this suite: logits within 2e-2 (here in the reference's own
 worstError measure, |a - e| / (1 + |e|)), and the greedy token equal to the
 oracle's wherever the oracle's top-2 margin exceeds 5e-2.
 """
@@ -28,9 +28,9 @@ MARGIN = 5e-2
 # weights gives logits up to ~7 and peaky attention, so the rounding of the
 # 16-bit activations (normalised rows, caches, attended rows, GELU output)
 # shows more than on a real checkpoint: its worstError bound is set per
-# storage from the unit roundoff, fp16 2^-11 and bf16 2^-8 (8x larger).  The
-# north star's max-abs 2e-2 is asserted on the real architectures in
-# test_gpu_parity.py.
+# storage from the unit roundoff, fp16 2^-11 and bf16 2^-8 (8x larger).
+# Max-abs 2e-2 is asserted on the Whisper architectures in
+# test_gpu_parity.py and test_gpu_architectures.py.
 MID_TOLERANCE = {"float16": 3e-2, "bfloat16": 6e-2}
 
 

@@ -1,10 +1,11 @@
-"""The BASELINE configurations' decoders against the oracle (random-init weights).
+"""The tiny.en and base.en decoders against the oracle (random-init weights).
 
-Teacher forcing as in the north star: the prompt [50257, 50362], then
-seeded uniform ids in [0, 50256], through the CUDA decoder and the
-double-precision oracle on the same 16-bit weights.  Logits must agree
-within max-abs 2e-2, and every greedy id must equal the oracle's wherever
-the oracle's top-2 margin exceeds 5e-2.  The greedy search is checked by
+Teacher forcing: the English prompt [50257, 50362], then seeded uniform ids
+in [0, 50256], through the CUDA decoder and the double-precision oracle
+(Tests/Decoder/Common.h:360-468) on the same 16-bit weights.  Logits must
+agree within max-abs 2e-2 (16-bit weights, fp32 accumulation), and every
+greedy id must equal the oracle's wherever the oracle's top-2 margin
+exceeds 5e-2.  The greedy search is checked by
 replaying the GPU's own transcript through the oracle: each id it chose
 must be the oracle's masked argmax wherever the masked margin exceeds 5e-2.
 """

@@ -1,7 +1,7 @@
 """wsp_argmax_no_alloc against wsp_argmax: two calls in a row on different
 inputs, each equal to the allocating entry point on the same inputs (and to
-the masked argmax the oracle defines), then the size limit of its fixed
-scratch.  Collected last, so it runs after every other test has used the
+the masked argmax the oracle defines); later calls leave the device's free
+memory unchanged; then the size limit of its fixed scratch.  Collected last, so it runs after every other test has used the
 device, and it passes on its own too."""
 import numpy as np
 import pytest
@@ -42,6 +42,28 @@ def test_two_calls_in_a_row_match_the_allocating_argmax():
         allocating = _device_argmax(argmax, logits, mask)
         assert np.array_equal(static, allocating)
         assert np.array_equal(static, O.masked_argmax(logits, mask))
+
+
+def test_calls_after_the_first_take_no_device_memory():
+    """The property the entry point exists for: once its first call on the
+    device has looked its scratch up, later calls leave the device's free
+    memory (cudaMemGetInfo) exactly where it was."""
+    import torch
+    from whispereacp_b200 import argmax_no_alloc
+    logits, mask = _cases()[0]
+    rows, length = logits.shape
+    dl = torch.from_numpy(logits).cuda()
+    dm = torch.from_numpy(mask).cuda()
+    out = torch.empty((rows,), dtype=torch.int32, device="cuda")
+    argmax_no_alloc(dl.data_ptr(), dm.data_ptr(), out.data_ptr(), rows, length)
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(8):
+        argmax_no_alloc(dl.data_ptr(), dm.data_ptr(), out.data_ptr(), rows, length)
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before
+    assert np.array_equal(out.cpu().numpy().astype(np.uint32), O.masked_argmax(logits, mask))
 
 
 def test_more_rows_than_the_fixed_scratch_holds_are_refused():

@@ -410,6 +410,10 @@ public:
             if (c.prompt[i] >= (uint32_t)shape_.vocabulary_size)
                 throw ModelError("prompt token " + std::to_string(c.prompt[i]) + " is outside the vocabulary");
         CUDA_CHECK(cudaSetDevice(device_));
+        // A transcription still queued (enqueue_transcribe without its read)
+        // reads the masks and the prompt ring from the device: let it finish
+        // before they are overwritten.
+        CUDA_CHECK(cudaStreamSynchronize(stream_));
         prompt_.assign(c.prompt, c.prompt + c.prompt_length);
         maximum_tokens_ = c.maximum_tokens;
         end_of_text_ = c.end_of_text;

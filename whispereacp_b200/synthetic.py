@@ -9,7 +9,9 @@ depend on any library's normal sampler.
 """
 from __future__ import annotations
 
+import os
 import zlib
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass
 
 import numpy as np
@@ -95,15 +97,20 @@ def decoder_tensor_extents(shape: DecoderShape) -> dict[str, tuple[int, ...]]:
 
 
 def normal_weights(shape: DecoderShape, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
-    """Random-init decoder: N(0, std) everywhere but layer norms (gain 1, offset 0)."""
-    tensors = {}
-    for name, extents in decoder_tensor_extents(shape).items():
+    """Random-init decoder: N(0, std) everywhere but layer norms (gain 1, offset 0).
+
+    Each tensor has its own generator, so the tensors are drawn on several
+    threads at once (numpy releases the GIL while it fills and transforms)."""
+    def draw(item):
+        name, extents = item
         count = int(np.prod(extents))
         if "layer_norm" in name:
-            tensors[name] = np.full(extents, 1.0 if name.endswith("weight") else 0.0, np.float32)
-        else:
-            tensors[name] = box_muller(count, _seed(name, seed), std).reshape(extents)
-    return tensors
+            return name, np.full(extents, 1.0 if name.endswith("weight") else 0.0, np.float32)
+        return name, box_muller(count, _seed(name, seed), std).reshape(extents)
+
+    items = list(decoder_tensor_extents(shape).items())
+    with ThreadPoolExecutor(max_workers=min(16, os.cpu_count() or 1)) as pool:
+        return dict(pool.map(draw, items))
 
 
 def encoder_output(windows: int, positions: int, width: int, seed: int = 1) -> np.ndarray:
