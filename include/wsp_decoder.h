@@ -105,6 +105,27 @@ void wsp_decoder_destroy(wsp_decoder* decoder);
 int wsp_decoder_set_tensor(wsp_decoder* decoder, const char* name, wsp_dtype dtype,
                            const int64_t* extents, int rank, const void* data);
 
+/*
+ * How wsp_decoder_set_tensor narrows the projection matrices and the token
+ * table to the storage type.  WSP_NARROW_ROUND (the default): round to
+ * nearest even.  WSP_NARROW_EXACT: the ExactHalf rule of DecoderWeights
+ * (Lib/WhisperEACP/Model/SafeTensors.h:146-159, Decoder/DecoderWeights.cpp:
+ * 149-178) -- a tensor is narrowed only when every value survives unchanged;
+ * where the reference then keeps that tensor in fp32, this decoder, whose
+ * kernels read 16-bit weights only, refuses it with WSP_MODEL_ERROR naming
+ * the tensor and the first value that would change (Whisper's checkpoints,
+ * fp16 values in fp32 containers, narrow exactly to float16).  Set it before
+ * the tensors.
+ */
+enum { WSP_NARROW_ROUND = 0, WSP_NARROW_EXACT = 1 };
+int wsp_decoder_set_narrowing(wsp_decoder* decoder, int mode);
+
+/*
+ * Of the tensors set so far, how many were narrowed inexactly, and the
+ * largest absolute change any value took.  No counterpart in the reference.
+ */
+int wsp_decoder_narrowing(const wsp_decoder* decoder, int* inexact_tensors, double* largest_change);
+
 /* WSP_MODEL_ERROR naming the first decoder tensor not yet set, else WSP_OK. */
 int wsp_decoder_check_weights(const wsp_decoder* decoder);
 

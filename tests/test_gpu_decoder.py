@@ -25,13 +25,11 @@ LOGIT_TOLERANCE = 2e-2
 HIDDEN_TOLERANCE = 2e-2
 MARGIN = 5e-2
 # The 64-wide-head shape (MID_SHAPE) with the reference's synthetic spread
-# weights gives logits up to ~7 and peaky attention, so the rounding of the
-# 16-bit activations (normalised rows, caches, attended rows, GELU output)
-# shows more than on a real checkpoint: its worstError bound is set per
-# storage from the unit roundoff, fp16 2^-11 and bf16 2^-8 (8x larger).
-# Max-abs 2e-2 is asserted on the Whisper architectures in
-# test_gpu_parity.py and test_gpu_architectures.py.
-MID_TOLERANCE = {"float16": 3e-2, "bfloat16": 6e-2}
+# weights gives logits up to ~7 and peaky attention, where the rounding of
+# 16-bit activations would show most; the decoder carries the activations a
+# product reads as hi + lo pairs, so the same 2e-2 worstError bound holds
+# for both storages here too.
+MID_TOLERANCE = {"float16": 2e-2, "bfloat16": 2e-2}
 
 
 def small(storage):

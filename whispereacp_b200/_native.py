@@ -70,6 +70,8 @@ SIGNATURES = {
     "wsp_decoder_destroy": ([_P], None),
     "wsp_decoder_set_tensor": ([_P, ctypes.c_char_p, _I, ctypes.POINTER(ctypes.c_int64), _I, _P], _I),
     "wsp_decoder_check_weights": ([_P], _I),
+    "wsp_decoder_set_narrowing": ([_P, _I], _I),
+    "wsp_decoder_narrowing": ([_P, ctypes.POINTER(_I), ctypes.POINTER(ctypes.c_double)], _I),
     "wsp_decoder_begin_sequence": ([_P, _P, _I], _I),
     "wsp_decoder_step": ([_P, _P, _I, _P, _P, _P], _I),
     "wsp_decoder_position": ([_P, ctypes.POINTER(_I)], _I),

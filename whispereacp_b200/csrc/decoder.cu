@@ -6,11 +6,11 @@
 //   DecoderWeights                                     Lib/WhisperEACP/Decoder/DecoderWeights.{h,cpp}
 //   greedy search                                      Lib/WhisperEACP/Whisper/Whisper.cpp:148-254,1158-1449
 #include "../../include/wsp_decoder.h"
+#include "cross_kv.cuh"
 #include "kernels.cuh"
 #include "schedule.h"
 #include "step_launch.h"
 
-#include <cublas_v2.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -44,12 +44,6 @@ void cuda_check(cudaError_t e, const char* what) {
         throw CudaFailure(std::string(what) + ": " + cudaGetErrorString(e), e == cudaErrorMemoryAllocation);
 }
 #define CUDA_CHECK(x) cuda_check((x), #x)
-
-void cublas_check(cublasStatus_t s, const char* what) {
-    if (s != CUBLAS_STATUS_SUCCESS)
-        throw CudaFailure(std::string(what) + ": cuBLAS status " + std::to_string((int)s),
-                          s == CUBLAS_STATUS_ALLOC_FAILED);
-}
 
 // ------------------------------------------------------- device memory
 
@@ -162,8 +156,6 @@ public:
         CUDA_CHECK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
         CUDA_CHECK(cudaDeviceGetAttribute(&sm_count_, cudaDevAttrMultiProcessorCount, device_));
         CUDA_CHECK(cudaDeviceGetAttribute(&max_shared_, cudaDevAttrMaxSharedMemoryPerBlockOptin, device_));
-        cublas_check(cublasCreate(&cublas_), "cublasCreate");
-        cublas_check(cublasSetStream(cublas_, stream_), "cublasSetStream");
         for (cudaEvent_t& e : phase_events_) CUDA_CHECK(cudaEventCreate(&e));
         allocate_weights();
         allocate_state();
@@ -172,7 +164,6 @@ public:
 
     ~Decoder() {
         cudaSetDevice(device_);
-        if (cublas_) cublasDestroy(cublas_);
         for (cudaEvent_t e : phase_events_)
             if (e) cudaEventDestroy(e);
         if (stream_) cudaStreamDestroy(stream_);
@@ -196,6 +187,7 @@ public:
         if (global >= 0) {
             if (global == 0) {
                 require_extents(name, extents, rank, {shape_.vocabulary_size, d});
+                audit_narrowing(name, dtype, data, (size_t)shape_.vocabulary_size * d);
                 upload_packed(token_table_, 0, shape_.vocabulary_size, d, padded(d), dtype, data);
             } else if (global == 1) {
                 // A model may carry more positions than a run needs; fewer is an error.
@@ -232,6 +224,17 @@ public:
 
         LayerBuffers& L = layers_[layer];
         const int kpd = padded(d), kpf = padded(f);
+        // The projection matrices are narrowed to the storage type.
+        static const bool kNarrowed[24] = {false, false, true,  false, true,  true,  false, true,
+                                           false, false, false, true,  false, true,  true,  false,
+                                           true,  false, false, false, true,  false, true,  false};
+        if (kNarrowed[which]) {
+            size_t count = 1;
+            for (int i = 0; i < rank; ++i) count *= (size_t)std::max<int64_t>(extents[i], 0);
+            if (which == 20 || which == 22) require_extents(name, extents, rank, which == 20 ? std::initializer_list<int>{f, d} : std::initializer_list<int>{d, f});
+            else require_extents(name, extents, rank, {d, d});
+            audit_narrowing(name, dtype, data, count);
+        }
         switch (which) {
         case 0: require_extents(name, extents, rank, {d}); upload_floats(L.ln1_w, 0, d, dtype, data); break;
         case 1: require_extents(name, extents, rank, {d}); upload_floats(L.ln1_b, 0, d, dtype, data); break;
@@ -311,38 +314,46 @@ public:
         const int rows = cross_positions == 0 ? shape_.cross_positions : cross_positions;
         const size_t elements = (size_t)windows_ * shape_.cross_positions * shape_.width;
         const float* source = encoder_rows;
-        if (!is_device_pointer(encoder_rows)) {
+        // Host rows, or device rows the kernel cannot read as float4s, go
+        // through the staging buffer.
+        if (!is_device_pointer(encoder_rows) || reinterpret_cast<uintptr_t>(encoder_rows) % 16 != 0) {
             CUDA_CHECK(cudaMemcpyAsync(encoder_staging_.get(), encoder_rows, elements * sizeof(float),
-                                       cudaMemcpyHostToDevice, stream_));
+                                       cudaMemcpyDefault, stream_));
             source = encoder_staging_.get<float>();
         }
-        launch_to_storage(storage_, source, encoder16_.get(), (long long)elements, stream_);
-        ++launches_;
+        if (cross_weights_dirty_) {
+            CUDA_CHECK(cudaMemcpy(cross_kv_w_.get(), cross_kv_host_.data(), cross_kv_host_.size() * 2,
+                                  cudaMemcpyHostToDevice));
+            settle_legacy_stream();
+            cross_weights_dirty_ = false;
+        }
 
         // recordSequenceStart (Decoder.cpp:121-146): every layer's cross keys
-        // and values, per window one batched product over the (layer, head)
-        // groups, each [rows, 2D] = encoder rows x [K_h; V_h]^T, written as
-        // the cache layout [window][layer][head][X][K | V].  The value bias is
-        // added after the attention instead (the weights sum to one).
-        const int d = shape_.width, D = d / shape_.heads, X = shape_.cross_positions;
-        const int groups = shape_.layers * shape_.heads;
-        const float one = 1.f, zero = 0.f;
-        const cudaDataType_t type = storage_ == Storage::f16 ? CUDA_R_16F : CUDA_R_16BF;
-        for (int b = 0; b < windows_; ++b) {
-            const size_t window = (size_t)b * groups * X * 2 * D;
-            cublas_check(cublasGemmStridedBatchedEx(
-                             cublas_, CUBLAS_OP_T, CUBLAS_OP_N, 2 * D, rows, d, &one, cross_kv_w_.get(), type, d,
-                             (long long)2 * D * d, encoder16_.get<uint16_t>() + (size_t)b * X * d, type, d, 0,
-                             &zero, cross_kv_.get<uint16_t>() + window, type, 2 * D, (long long)X * 2 * D, groups,
-                             CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT),
-                         "cross key/value projection");
+        // and values for every window in one tcgen05 launch (cross_kv.cuh),
+        // written as the cache layout [window][layer][head][X][K | V].  The
+        // value bias is added after the attention instead (the weights sum
+        // to one).
+        const int d = shape_.width, D = d / shape_.heads;
+        CrossKvArgs args{};
+        args.encoder = source;
+        args.weight = cross_kv_w_.get();
+        args.out = cross_kv_.get();
+        args.windows = windows_;
+        args.rows = rows;
+        args.row_stride = shape_.cross_positions;
+        args.width = d;
+        args.kblocks = (d + kCrossBlockCols - 1) / kCrossBlockCols;
+        args.columns = 2 * d * shape_.layers;
+        args.head_width = D;
+        args.groups = shape_.layers * shape_.heads;
+        args.status = state_.get<int>() + kCrossStatusWord;
+        CUDA_CHECK(cudaMemsetAsync(args.status, 0, sizeof(int), stream_));
+        try {
+            launch_cross_kv(storage_ == Storage::f16, args, sm_count_, stream_);
+        } catch (const std::runtime_error& e) {
+            throw CudaFailure(e.what(), false);
         }
-        // 64-wide heads: rotate each key row's pieces into the order the
-        // tensor-core attention reads conflict-free (cross_piece).
-        if (D == 64) {
-            launch_swizzle_cross(cross_kv_.get(), (long long)windows_ * groups * X, X, stream_);
-            ++launches_;
-        }
+        ++launches_;
         CUDA_CHECK(cudaMemsetAsync(state_.get(), 0, kStateWords * sizeof(int), stream_));
         CUDA_CHECK(cudaGetLastError());
         active_cross_ = rows;
@@ -624,10 +635,9 @@ public:
         for (int i = 0; i < 3; ++i) CUDA_CHECK(cudaEventElapsedTime(ms + i, phase_events_[i], phase_events_[i + 1]));
     }
 
-    // Kernel launches of this library per transcription: the encoder-row
-    // narrowing, the cross-row rotation (64-wide heads), the prompt step, and
-    // the launch that runs every later step.
-    int step_launches() const { return head_width() == 64 ? 4 : 3; }
+    // Kernel launches of this library per transcription: the cross key/value
+    // projection, the prompt step, and the launch that runs every later step.
+    int step_launches() const { return 3; }
 
 private:
     int ring_stride() const { return shape_.max_positions + 1; }
@@ -700,7 +710,8 @@ private:
         position_table_.allocate((size_t)shape_.max_positions * d * 4);
         final_w_.allocate(d * 4);
         final_b_.allocate(d * 4);
-        cross_kv_w_.allocate(2 * d * L * d * 2);
+        cross_kv_host_.assign(cross_weight_elements(), 0);
+        cross_kv_w_.allocate(cross_kv_host_.size() * 2);
         layers_.reset(new LayerBuffers[L]);
         for (size_t i = 0; i < L; ++i) {
             LayerBuffers& l = layers_[i];
@@ -725,10 +736,9 @@ private:
         self_values_.allocate(L * B * P * d * 2);
         cross_kv_.allocate(B * X * 2 * d * L * 2);
         encoder_staging_.allocate(B * X * d * 4);
-        encoder16_.allocate(B * X * d * 2);
         ring_.allocate(B * ring_stride() * 4);
         ring_prompt_.allocate(B * ring_stride() * 4);
-        state_.allocate(kStateWords * sizeof(int));
+        state_.allocate((kCrossStatusWord + 1) * sizeof(int));
         barrier_.allocate(64);
         ended_.allocate((size_t)windows_);
         profile_.allocate(1024 * sizeof(unsigned long long));
@@ -743,10 +753,11 @@ private:
         const size_t d = shape_.width, f = shape_.feed_forward_width, H = shape_.heads, D = d / H;
         hidden_.allocate(R * d * 4);
         queries_.allocate(R * d * 4);
+        // 16-bit activations a product reads: a hi plane and a lo plane.
         const size_t A = (R + 15) / 16 * 16;
-        normalised_.allocate(A * padded(d) * 2);
-        attended_.allocate(A * padded(d) * 2);
-        feed_forward_.allocate(A * padded(f) * 2);
+        normalised_.allocate(2 * A * padded(d) * 2);
+        attended_.allocate(2 * A * padded(d) * 2);
+        feed_forward_.allocate(2 * A * padded(f) * 2);
         partial_.allocate(R * H * kMaxCrossSplits * (D + 2) * 4);
         // Fused out-projections (a few rows): the heads' partial rows of the
         // self and the cross attention, and the residual rows between them.
@@ -765,8 +776,16 @@ private:
     }
 
     void check_device_errors() {
-        int state[kStateWords];
+        int state[kCrossStatusWord + 1];
         CUDA_CHECK(cudaMemcpy(state, state_.get(), sizeof state, cudaMemcpyDeviceToHost));
+        if (state[kCrossStatusWord] != 0) {
+            static const char* const kinds[] = {"?", "encoder rows", "weights", "a free stage", "a free accumulator",
+                                                "its products to drain", "an accumulator"};
+            const int kind = state[kCrossStatusWord] >= 1 && state[kCrossStatusWord] <= 6 ? state[kCrossStatusWord] : 0;
+            CUDA_CHECK(cudaMemset(state_.get<int>() + kCrossStatusWord, 0, sizeof(int)));
+            settle_legacy_stream();
+            throw CudaFailure(std::string("the cross key/value projection gave up waiting for ") + kinds[kind], false);
+        }
         if (state[kError] != 0) {
             CUDA_CHECK(cudaMemset(state_.get<int>() + kError, 0, sizeof(int)));
             settle_legacy_stream();
@@ -802,6 +821,7 @@ private:
     static constexpr int kMaxCrossChunk = 0;
     static constexpr int kMaxBlocksPerSm = 2;
     static constexpr int kStaticSharedBytes = 2048;
+    static constexpr int kMinStages = 3;
 
     // The step: recordDecoderStep (Decoder.cpp:151-177) with decoderLayer
     // (Decoder.cpp:73-115), lowered onto the ops of step.cuh.
@@ -1107,13 +1127,20 @@ private:
         return std::max(16384, (tile + 1023) / 1024 * 1024);
     }
 
+    // The weight stream's stages: as many as the shared memory left by the
+    // work area holds.  Should a tile of 32 input rows (its hi and lo planes)
+    // leave fewer than kMinStages, the tiles shrink to 16 rows, then 8.
     void configure_stream(bool half, StepParams& p) const {
         p.stage_bytes = stage_bytes_for_width();
-        const size_t work = decode_work_bytes(half, p, kMaxCrossChunk);
-        // (The kernel's static shared memory -- barriers, flags, a fused
-        // out-projection's input row -- comes out of the same budget.)
-        const long long room = (long long)max_shared_ - kStaticSharedBytes - (long long)work;
-        p.stages = (int)std::min<long long>(kMaxStreamStages, room / p.stage_bytes);
+        for (int columns = 4; columns >= 1; columns /= 2) {
+            p.tile_columns = columns;
+            const size_t work = decode_work_bytes(half, p, kMaxCrossChunk);
+            // (The kernel's static shared memory -- barriers, flags, a fused
+            // out-projection's input row -- comes out of the same budget.)
+            const long long room = (long long)max_shared_ - kStaticSharedBytes - (long long)work;
+            p.stages = (int)std::min<long long>(kMaxStreamStages, room / p.stage_bytes);
+            if (p.stages >= kMinStages) return;
+        }
         if (p.stages < 2) throw CudaFailure("the decode kernel's shared memory does not fit", false);
     }
 
@@ -1178,13 +1205,14 @@ private:
         p.profile = profile;
         const bool half = storage_ == Storage::f16;
         // A tensor-core item's rows: as many as a weight stage holds (128
-        // bytes a row), at most 256, a multiple of 16; the activation ring
-        // holds kMaxXStages blocks of that many rows.
+        // bytes a row), at most 128, a multiple of 16; the activation ring
+        // holds three k-blocks of that many rows, each its hi plane then its
+        // lo plane (two products into one accumulator).
         p.stage_bytes = stage_bytes_for_width();
-        p.umma_rows = std::min(256, p.stage_bytes / 128 / 16 * 16);
+        p.umma_rows = std::min(128, p.stage_bytes / 128 / 16 * 16);
         if (umma_) {
-            p.umma_x_stage_bytes = std::min(p.umma_rows, (R + 15) / 16 * 16) * 128;
-            p.umma_x_stages = 4;
+            p.umma_x_stage_bytes = 2 * std::min(p.umma_rows, (R + 15) / 16 * 16) * 128;
+            p.umma_x_stages = 3;
             p.umma_blocks = std::max(1, p.stage_bytes / 16384);
         }
         configure_stream(half, p);
@@ -1223,6 +1251,52 @@ private:
     }
 
     // ------------------------------------------------------ upload helpers
+
+    // The narrowing of a projection matrix (or the token table) to the
+    // storage type.  WSP_NARROW_EXACT is the reference's ExactHalf rule
+    // (Model/SafeTensors.h:146-159, DecoderWeights.cpp:149-178): narrow only
+    // a tensor every value of which survives unchanged.  Where the reference
+    // then keeps the fp32 tensor, this decoder (16-bit weights only) refuses
+    // it, naming the tensor and the first value that would change.  The
+    // default, WSP_NARROW_ROUND, rounds to nearest even; either way the
+    // tensors narrowed inexactly and the largest change are counted.
+    void audit_narrowing(const std::string& name, wsp_dtype dtype, const void* data, size_t count) {
+        if (dtype != WSP_FLOAT32 && ((dtype == WSP_FLOAT16) == (storage_ == Storage::f16))) return;  // same type
+        double largest = 0.0;
+        size_t first = count;
+        for (size_t i = 0; i < count; ++i) {
+            const float v = widen(data, dtype, i);
+            const float back = widen16(narrow(v, storage_));
+            if (!(back == v) && !(std::isnan(v) && std::isnan(back))) {
+                if (first == count) first = i;
+                largest = std::max(largest, (double)std::fabs(back - v));
+            }
+        }
+        if (first == count) return;
+        if (narrowing_ == WSP_NARROW_EXACT)
+            throw ModelError(name + " does not narrow exactly to " +
+                             (storage_ == Storage::f16 ? "float16" : "bfloat16") + ": element " +
+                             std::to_string(first) + " is " + std::to_string(widen(data, dtype, first)));
+        ++inexact_tensors_;
+        largest_change_ = std::max(largest_change_, largest);
+    }
+
+    float widen16(uint16_t bits) const {
+        return widen(&bits, storage_ == Storage::f16 ? WSP_FLOAT16 : WSP_BFLOAT16, 0);
+    }
+
+public:
+    void set_narrowing(int mode) {
+        if (mode != WSP_NARROW_ROUND && mode != WSP_NARROW_EXACT)
+            throw InvalidArgument("narrowing must be WSP_NARROW_ROUND or WSP_NARROW_EXACT");
+        narrowing_ = mode;
+    }
+    void narrowing_stats(int* tensors, double* largest) const {
+        if (tensors) *tensors = inexact_tensors_;
+        if (largest) *largest = largest_change_;
+    }
+
+private:
 
     static std::string describe(const int64_t* extents, int rank) {
         std::string s = "[";
@@ -1281,19 +1355,30 @@ private:
 
     // Cross k_proj (kv 0) or v_proj (kv 1) of a layer into the projection
     // that writes the cross caches: per layer and head, the head's D key rows
-    // then its D value rows, [L][H][2D][d], so the product of a window's
-    // encoder rows with one (layer, head) group is [X][K | V].
+    // then its D value rows -- weight row ((layer * H + head) * 2 + kv) * D +
+    // i -- so the product of a window's encoder rows with one (layer, head)
+    // group's 2D rows is [X][K | V]; stored in the tensor-core layout
+    // (cross_weight_offset) in the host copy.
     void upload_cross_projection(int layer, int kv, wsp_dtype dtype, const void* data) {
-        const int d = shape_.width, H = shape_.heads, D = d / H;
-        std::vector<uint16_t> v((size_t)d * d);
-        for (size_t i = 0; i < v.size(); ++i) v[i] = narrow(widen(data, dtype, i), storage_);
-        for (int h = 0; h < H; ++h) {
-            const size_t row = ((size_t)(layer * H + h) * 2 + kv) * D;
-            CUDA_CHECK(cudaMemcpy(cross_kv_w_.get<uint16_t>() + row * d, v.data() + (size_t)h * D * d,
-                                  (size_t)D * d * 2, cudaMemcpyHostToDevice));
-        }
+        const int d = shape_.width, H = shape_.heads, D = d / H, kblocks = (d + kCrossBlockCols - 1) / kCrossBlockCols;
+        for (int h = 0; h < H; ++h)
+            for (int i = 0; i < D; ++i) {
+                const int n = ((layer * H + h) * 2 + kv) * D + i;
+                const size_t src = (size_t)(h * D + i) * d;
+                for (int c = 0; c < d; ++c)
+                    cross_kv_host_[cross_weight_offset(n, c, kblocks)] = narrow(widen(data, dtype, src + c), storage_);
+            }
+        cross_weights_dirty_ = true;
     }
 
+    // Elements of the cross projection's weights: L*2d rows in whole tiles,
+    // d columns in whole k-blocks (cross_weight_offset).
+    size_t cross_weight_elements() const {
+        const size_t rows = (size_t)2 * shape_.width * shape_.layers;
+        const size_t tiles = (rows + kCrossTileRows - 1) / kCrossTileRows;
+        const size_t kblocks = (shape_.width + kCrossBlockCols - 1) / kCrossBlockCols;
+        return tiles * kblocks * kCrossTileRows * kCrossBlockCols;
+    }
 
     // rows x cols of a row-major [rows, cols] tensor into rows
     // [row_offset, row_offset+rows) of a fragment-packed [*, kp] matrix
@@ -1327,13 +1412,17 @@ private:
     int max_shared_ = 232448;
     cudaStream_t stream_ = nullptr;
     cudaEvent_t phase_events_[4] = {nullptr, nullptr, nullptr, nullptr};
-    cublasHandle_t cublas_ = nullptr;
 
     DeviceBuffer token_table_, position_table_, final_w_, final_b_, cross_kv_w_;
     std::unique_ptr<LayerBuffers[]> layers_;
     std::vector<bool> present_;
 
-    DeviceBuffer self_keys_, self_values_, cross_kv_, encoder_staging_, encoder16_;
+    DeviceBuffer self_keys_, self_values_, cross_kv_, encoder_staging_;
+    // The cross projection's weights in their tensor-core layout, kept on the
+    // host too so each k_proj / v_proj upload patches it; copied to the
+    // device once before the next sequence start.
+    std::vector<uint16_t> cross_kv_host_;
+    bool cross_weights_dirty_ = false;
     DeviceBuffer ring_, ring_prompt_, state_, masks_;
     DeviceBuffer hidden_, queries_, normalised_, attended_, feed_forward_, partial_, partial_d_, split_counters_;
     DeviceBuffer out_partials_, hidden_mid_;
@@ -1363,8 +1452,14 @@ private:
     std::vector<double> op_us_;
     std::vector<int> op_kinds_;
     static constexpr int kTraceOffset = 512;   // kTraceBase of step.cu
+    // The state word (after the decode kernel's) the cross projection
+    // reports a wait that gave up in.
+    static constexpr int kCrossStatusWord = kStateWords;
     static constexpr int kTraceSections = 16;
     int queued_steps_ = 0;
+    int narrowing_ = WSP_NARROW_ROUND;
+    int inexact_tensors_ = 0;
+    double largest_change_ = 0.0;
 };
 
 template <typename F>
@@ -1448,6 +1543,20 @@ int wsp_decoder_set_tensor(wsp_decoder* decoder, const char* name, wsp_dtype dty
         WSP_NEED(decoder);
         decoder->impl->set_tensor(name, dtype, extents, rank, data);
         wsp::settle_legacy_stream();  // the uploads are pageable copies
+    });
+}
+
+int wsp_decoder_set_narrowing(wsp_decoder* decoder, int mode) {
+    return guarded([&] {
+        WSP_NEED(decoder);
+        decoder->impl->set_narrowing(mode);
+    });
+}
+
+int wsp_decoder_narrowing(const wsp_decoder* decoder, int* inexact_tensors, double* largest_change) {
+    return guarded([&] {
+        WSP_NEED(decoder);
+        decoder->impl->narrowing_stats(inexact_tensors, largest_change);
     });
 }
 

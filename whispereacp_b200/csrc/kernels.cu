@@ -1,6 +1,5 @@
 // Kernels outside the decode step (sm_100a): the standalone masked argmax of
-// Argmax.h:83-201 / Argmax.cpp:47-80 (WhisperEACP, Lib/WhisperEACP/Kernels),
-// and the fp32 -> 16-bit narrowing of encoder rows.
+// Argmax.h:83-201 / Argmax.cpp:47-80 (WhisperEACP, Lib/WhisperEACP/Kernels).
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -11,10 +10,6 @@
 namespace wsp {
 
 namespace {
-
-template <Storage S> struct StorageType;
-template <> struct StorageType<Storage::f16> { using type = __half; };
-template <> struct StorageType<Storage::bf16> { using type = __nv_bfloat16; };
 
 // ----------------------------------------------------------------- argmax
 
@@ -78,29 +73,6 @@ __global__ void __launch_bounds__(kThreads) argmax_partial_kernel(const float* l
     }
 }
 
-// Rotates the 16-byte pieces of every 256-byte cross key row (D = 64) into
-// the order cross_piece gives; rows are key j = row % keys of their block.
-__global__ void swizzle_cross_kernel(uint4* data, long long rows, int keys) {
-    // Every lane of a warp runs every iteration (the bound is on the warp's
-    // first piece), so the row's 16 loads all precede its stores.
-    const long long pieces = rows * 16;
-    const long long stride = (long long)gridDim.x * blockDim.x;
-    for (long long first = (long long)blockIdx.x * blockDim.x + (threadIdx.x & ~31); first < pieces; first += stride) {
-        const long long i = first + (threadIdx.x & 31);
-        uint4 v;
-        if (i < pieces) v = data[i];
-        __syncwarp();
-        if (i < pieces) data[((i >> 4) << 4) + cross_piece((int)(i & 15), (int)((i >> 4) % keys))] = v;
-    }
-}
-
-template <typename WT>
-__global__ void to_storage_kernel(const float* in, WT* out, long long count) {
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < count;
-         i += (long long)gridDim.x * blockDim.x)
-        out[i] = Half16<WT>::from_float(in[i]);
-}
-
 }  // namespace
 
 // The no-allocation argmax's scratch: 65536 candidate pairs (512 KB), values
@@ -147,18 +119,6 @@ void launch_argmax_rows(const float* logits, const float* mask, uint32_t* out, i
     f.step_tokens = 1;
     f.row_tokens = out;
     argmax_final_kernel<<<rows, kThreads, 0, stream>>>(f);
-}
-
-void launch_swizzle_cross(void* data, long long rows, int keys, cudaStream_t stream) {
-    const long long pieces = rows * 16;
-    const int grid = (int)std::min<long long>((pieces + kThreads - 1) / kThreads, 148LL * 16);
-    swizzle_cross_kernel<<<grid, kThreads, 0, stream>>>(static_cast<uint4*>(data), rows, keys);
-}
-
-void launch_to_storage(Storage s, const float* in, void* out, long long count, cudaStream_t stream) {
-    const int grid = (int)std::min<long long>((count + kThreads - 1) / kThreads, 148LL * 16);
-    if (s == Storage::f16) to_storage_kernel<__half><<<grid, kThreads, 0, stream>>>(in, static_cast<__half*>(out), count);
-    else to_storage_kernel<__nv_bfloat16><<<grid, kThreads, 0, stream>>>(in, static_cast<__nv_bfloat16*>(out), count);
 }
 
 }  // namespace wsp

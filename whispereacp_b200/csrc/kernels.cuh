@@ -1,5 +1,4 @@
-// Kernels outside the decode step: the standalone masked argmax and the
-// narrowing of the encoder rows ahead of the cross key/value projection.
+// Kernels outside the decode step: the standalone masked argmax.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -39,12 +38,5 @@ constexpr int kNoAllocArgmaxCandidates = 65536;
 // then as many uint32 indices), looked up with cudaGetSymbolAddress the first
 // time a device asks, with that device current, and remembered after.
 cudaError_t no_alloc_argmax_scratch(int device, void** scratch);
-
-// Rotates the pieces of `rows` 256-byte cross key rows (keys rows a block)
-// into the shared-memory order the tensor-core cross attention reads.
-void launch_swizzle_cross(void* data, long long rows, int keys, cudaStream_t stream);
-
-// ------------------------------------------------------------- plumbing ---
-void launch_to_storage(Storage s, const float* in, void* out, long long count, cudaStream_t stream);
 
 }  // namespace wsp

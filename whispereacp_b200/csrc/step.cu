@@ -12,6 +12,7 @@
 // Data written by one CTA and read by another inside the launch is read with
 // ld.global.cg (L2, never a stale L1 line); the grid barrier orders it.
 #include "step.cuh"
+#include "umma.cuh"
 
 #include <type_traits>
 #include "step_launch.h"
@@ -96,6 +97,23 @@ __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_c
 // row-major, or the tensor-core block layout (act_offset) when p.umma.
 __device__ __forceinline__ size_t act_index(const StepParams& p, int r, int c, int ld) {
     return p.umma ? act_offset(r, c, p.act_rows) : (size_t)r * ld + c;
+}
+
+// The 16-bit activations a product reads (normalised rows, attended rows,
+// GELU outputs) carry two planes: hi = the value rounded to 16 bits, and lo
+// = the rest (value - hi) rounded again, act_rows * ld elements past hi in
+// the same layout.  A product sums W . hi + W . lo, two tensor-core products
+// into one fp32 accumulator, so its input carries about twice the 16-bit
+// precision (the rounding of a bf16 activation would otherwise dominate the
+// error against fp32 arithmetic).  Tiles in shared memory keep the same two
+// planes, `lo` elements apart.
+__device__ __forceinline__ size_t lo_plane(const StepParams& p, int ld) { return (size_t)p.act_rows * ld; }
+
+template <typename WT>
+__device__ __forceinline__ void store_split(WT* hi, size_t lo, float v) {
+    const WT h = Half16<WT>::from_float(v);
+    hi[0] = h;
+    hi[lo] = Half16<WT>::from_float(v - Half16<WT>::to_float(h));
 }
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
@@ -214,10 +232,6 @@ __device__ bool grid_barrier(const StepParams& p, unsigned& epoch) {
 // through empty[u % S].  The consumers wait on full[], read, and release
 // warp by warp, so no CTA-wide sync is spent per unit, and the next op's
 // first units land while this op and the grid barrier run.
-
-__device__ __forceinline__ uint32_t smem_address(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
 
 struct Stream {
     unsigned char* ring;          // stages x stage_bytes
@@ -437,8 +451,9 @@ __device__ __forceinline__ void add_addends(const Addends& a, size_t row, int d,
     }
 }
 
-// LayerNorm of rows_in_tile rows of h into the 16-bit tile xs [rows][ldx]:
-// output row rl reads h row (r0 + rl)*row_step + row_offset.  One warp a row,
+// LayerNorm of rows_in_tile rows of h into the 16-bit tile xs [rows][ldx]
+// (hi) and xs + lo (lo): output row rl reads h row (r0 + rl)*row_step +
+// row_offset.  One warp a row,
 // the row in registers: the mean, then the centred variance, as
 // LayerNorm.h:19-98 does.  hidden_out, when given, receives the fp32 rows.
 // With addends, each row is first input + bias + the partial rows (the
@@ -446,7 +461,7 @@ __device__ __forceinline__ void add_addends(const Addends& a, size_t row, int d,
 template <typename WT>
 __device__ void layer_norm_tile(const StepParams& p, const float* input, const float* gamma, const float* beta,
                                 int r0, int rows_in_tile, int row_step, int row_offset, WT* xs, int ldx,
-                                float* hidden_out, const Addends& add = Addends()) {
+                                size_t lo, float* hidden_out, const Addends& add = Addends()) {
     const int d = p.width;
     if (rows_in_tile <= 2) {
         // A row or two: the whole CTA on each row, every load of the row,
@@ -499,11 +514,11 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
                 const int c = threadIdx.x + i * kThreads;
                 if (c < d) {
                     const float y = (v[i] - mean) * scale * g[i] + b[i];
-                    out[c] = Half16<WT>::from_float(y);
+                    store_split(out + c, lo, y);
                     if (hidden_out) hidden_out[(size_t)(r0 + rl) * d + c] = y;
                 }
             }
-            for (int c = d + threadIdx.x; c < ldx; c += kThreads) out[c] = Half16<WT>::from_float(0.f);
+            for (int c = d + threadIdx.x; c < ldx; c += kThreads) out[c] = out[c + lo] = Half16<WT>::from_float(0.f);
             trl.end(kTrNormRest);
         }
         return;
@@ -553,10 +568,10 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
         for (int i = 0; i < kNormMaxPerLane; ++i) {
             const int c = lane + 32 * i;
             if (c < d) {
-                out[c] = Half16<WT>::from_float(v[i]);
+                store_split(out + c, lo, v[i]);
                 if (hidden_out) hidden_out[(size_t)(r0 + rl) * d + c] = v[i];
             } else if (c < ldx) {
-                out[c] = Half16<WT>::from_float(0.f);
+                out[c] = out[c + lo] = Half16<WT>::from_float(0.f);
             }
         }
     }
@@ -564,37 +579,46 @@ __device__ void layer_norm_tile(const StepParams& p, const float* input, const f
 
 __device__ __forceinline__ int round16(int n) { return (n + 15) / 16 * 16; }
 
-// Copies rows r0 .. r0+rows-1 of 16-bit rows X [.., ld] into the tile xs
-// [rows][ldx], kp values a row (a multiple of 8), all loads in flight.
+// Copies rows r0 .. r0+rows-1 of 16-bit rows X [.., ld] and of their lo
+// plane (x_lo elements on) into the tile xs [rows][ldx] and xs + xs_lo, kp
+// values a row (a multiple of 8), all loads in flight.
 template <typename WT>
-__device__ void stage_rows(const WT* X, int ld, int r0, int rows, int kp, WT* xs, int ldx) {
+__device__ void stage_rows(const WT* X, int ld, size_t x_lo, int r0, int rows, int kp, WT* xs, int ldx,
+                           size_t xs_lo) {
     const int per_row = kp / 8;
     const int total = rows * per_row;
 #pragma unroll 4
     for (int i = threadIdx.x; i < total; i += kThreads) {
         const int rl = i / per_row, c = (i % per_row) * 8;
-        *reinterpret_cast<uint4*>(xs + (size_t)rl * ldx + c) = ld_cg4(X + (size_t)(r0 + rl) * ld + c);
+        const WT* from = X + (size_t)(r0 + rl) * ld + c;
+        const uint4 hi = ld_cg4(from), lo = ld_cg4(from + x_lo);
+        *reinterpret_cast<uint4*>(xs + (size_t)rl * ldx + c) = hi;
+        *reinterpret_cast<uint4*>(xs + (size_t)rl * ldx + c + xs_lo) = lo;
     }
 }
 
-// LayerNorm of op.norm_rows rows into 16-bit rows, a row per CTA at a time
-// with the whole CTA on it.
+// LayerNorm of op.norm_rows rows into 16-bit rows (both planes), a row per
+// CTA at a time with the whole CTA on it.
 template <typename WT>
 __device__ void op_norm(const StepParams& p, const StepOp& op, unsigned char* work) {
     WT* out = static_cast<WT*>(op.out);
-    WT* row16 = reinterpret_cast<WT*>(work);  // the block layout: a row first, then its pieces
+    const size_t lo = lo_plane(p, op.ld_out);
+    WT* row16 = reinterpret_cast<WT*>(work);  // the block layout: a row (hi, lo) first, then its pieces
     for (int row = blockIdx.x; row < op.norm_rows; row += gridDim.x) {
         consumer_sync();
         if (!op.norm_umma) {
             layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, row, 1, op.norm_step, op.norm_offset,
-                                out + (size_t)row * op.ld_out, op.ld_out, op.norm_hidden);
+                                out + (size_t)row * op.ld_out, op.ld_out, lo, op.norm_hidden);
             continue;
         }
         layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, row, 1, op.norm_step, op.norm_offset, row16, op.ld_out,
-                            op.norm_hidden);
+                            (size_t)op.ld_out, op.norm_hidden);
         consumer_sync();
-        for (int c = 8 * threadIdx.x; c < op.ld_out; c += 8 * kThreads)
-            *reinterpret_cast<uint4*>(out + act_offset(row, c, p.act_rows)) = *reinterpret_cast<const uint4*>(row16 + c);
+        for (int c = 8 * threadIdx.x; c < op.ld_out; c += 8 * kThreads) {
+            WT* at = out + act_offset(row, c, p.act_rows);
+            *reinterpret_cast<uint4*>(at) = *reinterpret_cast<const uint4*>(row16 + c);
+            *reinterpret_cast<uint4*>(at + lo) = *reinterpret_cast<const uint4*>(row16 + op.ld_out + c);
+        }
     }
 }
 
@@ -612,28 +636,36 @@ __host__ __device__ inline int tile_pitch(int kpd) { return kpd % 64 == 0 ? kpd 
 // k-steps take the halves, so the input fragments follow the weight
 // fragments' k permutation and every product pairs the right elements.
 template <typename WT, int NT, bool X_SHARED>
-__device__ __forceinline__ void product_chunk(const unsigned char* unit, int c, const WT* X, int ldx, int k0,
-                                              const bool (&x_ok)[NT], float (&acc)[NT][4]) {
+__device__ __forceinline__ void product_chunk(const unsigned char* unit, int c, const WT* X, int ldx, size_t x_lo,
+                                              int k0, const bool (&x_ok)[NT], float (&acc)[NT][4]) {
     const int lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
     const uint4* w = reinterpret_cast<const uint4*>(unit + ((size_t)c * 32 + lane) * 32);
     const uint4 lo = w[0], hi = w[1];
-    uint4 B[NT];
+    uint4 B[NT], L[NT];
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
         const WT* at = X + (size_t)(x_ok[j] ? 8 * j + gq : 0) * ldx + k0 + 8 * tq;
-        if (!x_ok[j]) B[j] = make_uint4(0, 0, 0, 0);
-        else if constexpr (X_SHARED) B[j] = *reinterpret_cast<const uint4*>(at);
-        else B[j] = ld_cg4(at);
+        if (!x_ok[j]) {
+            B[j] = L[j] = make_uint4(0, 0, 0, 0);
+        } else if constexpr (X_SHARED) {
+            B[j] = *reinterpret_cast<const uint4*>(at);
+            L[j] = *reinterpret_cast<const uint4*>(at + x_lo);
+        } else {
+            B[j] = ld_cg4(at);
+            L[j] = ld_cg4(at + x_lo);
+        }
     }
     const uint32_t a0[4] = {lo.x, hi.x, lo.y, hi.y};
     const uint32_t a1[4] = {lo.z, hi.z, lo.w, hi.w};
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
-        const uint32_t b0[2] = {B[j].x, B[j].y};
-        const uint32_t b1[2] = {B[j].z, B[j].w};
+        const uint32_t b0[2] = {B[j].x, B[j].y}, b1[2] = {B[j].z, B[j].w};
+        const uint32_t l0[2] = {L[j].x, L[j].y}, l1[2] = {L[j].z, L[j].w};
         mma_16816<WT>(acc[j], a0, b0);
         mma_16816<WT>(acc[j], a1, b1);
+        mma_16816<WT>(acc[j], a0, l0);
+        mma_16816<WT>(acc[j], a1, l1);
     }
 }
 
@@ -642,25 +674,29 @@ __device__ __forceinline__ void product_chunk(const unsigned char* unit, int c, 
 // (the k-halves alternate), so the warp waits on one MMA latency, not four.
 template <typename WT, int NT, bool X_SHARED>
 __device__ __forceinline__ void product_chunk_pair(const unsigned char* unit, int c, int c2, const WT* X, int ldx,
-                                                   int k0, int k02, const bool (&x_ok)[NT], float (&acc)[NT][4],
-                                                   float (&acc2)[NT][4]) {
+                                                   size_t x_lo, int k0, int k02, const bool (&x_ok)[NT],
+                                                   float (&acc)[NT][4], float (&acc2)[NT][4]) {
     const int lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
     const uint4* w = reinterpret_cast<const uint4*>(unit + ((size_t)c * 32 + lane) * 32);
     const uint4* w2 = reinterpret_cast<const uint4*>(unit + ((size_t)c2 * 32 + lane) * 32);
     const uint4 lo = w[0], hi = w[1], lo2 = w2[0], hi2 = w2[1];
-    uint4 B[NT], B2[NT];
+    uint4 B[NT], B2[NT], L[NT], L2[NT];
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
         const WT* row = X + (size_t)(x_ok[j] ? 8 * j + gq : 0) * ldx + 8 * tq;
         if (!x_ok[j]) {
-            B[j] = B2[j] = make_uint4(0, 0, 0, 0);
+            B[j] = B2[j] = L[j] = L2[j] = make_uint4(0, 0, 0, 0);
         } else if constexpr (X_SHARED) {
             B[j] = *reinterpret_cast<const uint4*>(row + k0);
             B2[j] = *reinterpret_cast<const uint4*>(row + k02);
+            L[j] = *reinterpret_cast<const uint4*>(row + x_lo + k0);
+            L2[j] = *reinterpret_cast<const uint4*>(row + x_lo + k02);
         } else {
             B[j] = ld_cg4(row + k0);
             B2[j] = ld_cg4(row + k02);
+            L[j] = ld_cg4(row + x_lo + k0);
+            L2[j] = ld_cg4(row + x_lo + k02);
         }
     }
     const uint32_t a0[4] = {lo.x, hi.x, lo.y, hi.y}, a1[4] = {lo.z, hi.z, lo.w, hi.w};
@@ -669,10 +705,16 @@ __device__ __forceinline__ void product_chunk_pair(const unsigned char* unit, in
     for (int j = 0; j < NT; ++j) {
         const uint32_t b0[2] = {B[j].x, B[j].y}, b1[2] = {B[j].z, B[j].w};
         const uint32_t d0[2] = {B2[j].x, B2[j].y}, d1[2] = {B2[j].z, B2[j].w};
+        const uint32_t l0[2] = {L[j].x, L[j].y}, l1[2] = {L[j].z, L[j].w};
+        const uint32_t m0[2] = {L2[j].x, L2[j].y}, m1[2] = {L2[j].z, L2[j].w};
         mma_16816<WT>(acc[j], a0, b0);
         mma_16816<WT>(acc2[j], a1, b1);
         mma_16816<WT>(acc[j], c0, d0);
         mma_16816<WT>(acc2[j], c1, d1);
+        mma_16816<WT>(acc[j], a0, l0);
+        mma_16816<WT>(acc2[j], a1, l1);
+        mma_16816<WT>(acc[j], c0, m0);
+        mma_16816<WT>(acc2[j], c1, m1);
     }
 }
 
@@ -680,15 +722,16 @@ __device__ __forceinline__ void product_chunk_pair(const unsigned char* unit, in
 // k_base + 32 c, two at a time.
 template <typename WT, int NT, bool X_SHARED>
 __device__ __forceinline__ void chunks_product(const unsigned char* unit, int c_first, int step, int n, const WT* X,
-                                               int ldx, int k_base, const bool (&x_ok)[NT], float (&acc)[NT][4]) {
+                                               int ldx, size_t x_lo, int k_base, const bool (&x_ok)[NT],
+                                               float (&acc)[NT][4]) {
     float acc2[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc2[j][0] = acc2[j][1] = acc2[j][2] = acc2[j][3] = 0.f;
     int c = c_first;
     for (; c + step < n; c += 2 * step)
-        product_chunk_pair<WT, NT, X_SHARED>(unit, c, c + step, X, ldx, k_base + c * 32, k_base + (c + step) * 32,
-                                             x_ok, acc, acc2);
-    if (c < n) product_chunk<WT, NT, X_SHARED>(unit, c, X, ldx, k_base + c * 32, x_ok, acc2);
+        product_chunk_pair<WT, NT, X_SHARED>(unit, c, c + step, X, ldx, x_lo, k_base + c * 32,
+                                             k_base + (c + step) * 32, x_ok, acc, acc2);
+    if (c < n) product_chunk<WT, NT, X_SHARED>(unit, c, X, ldx, x_lo, k_base + c * 32, x_ok, acc2);
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
         acc[j][0] += acc2[j][0];
@@ -702,8 +745,8 @@ __device__ __forceinline__ void chunks_product(const unsigned char* unit, int c_
 // order, the 8 warps taking alternate chunks of each.  False if a wait gave
 // up (the abort word is then raised and the kernel is on its way out).
 template <typename WT, int NT, bool X_SHARED>
-__device__ bool product_tile(const StepParams& p, Stream& s, int kp, const WT* X, int ldx, int rows_valid,
-                             float (&acc)[NT][4]) {
+__device__ bool product_tile(const StepParams& p, Stream& s, int kp, const WT* X, int ldx, size_t x_lo,
+                             int rows_valid, float (&acc)[NT][4]) {
     const int warp = threadIdx.x >> 5, gq = (threadIdx.x & 31) >> 2;
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -718,7 +761,7 @@ __device__ bool product_tile(const StepParams& p, Stream& s, int kp, const WT* X
         if (!unit) return false;
         Trace tr = trace_of(p.profile);
         tr.begin();
-        chunks_product<WT, NT, X_SHARED>(unit, warp, kWarps, n, X, ldx, c0 * 32, x_ok, acc);
+        chunks_product<WT, NT, X_SHARED>(unit, warp, kWarps, n, X, ldx, x_lo, c0 * 32, x_ok, acc);
         tr.end(kTrCompute);
         release_unit(s);
     }
@@ -772,7 +815,7 @@ __device__ __forceinline__ void emit_output(const StepParams& p, const StepOp& o
         atomicAdd(static_cast<float*>(op.out) + (size_t)r * op.ld_out + n, v);
         return;
     case kEpGelu:
-        static_cast<WT*>(op.out)[act_index(p, r, n, op.ld_out)] = Half16<WT>::from_float(gelu_exact(v));
+        store_split(static_cast<WT*>(op.out) + act_index(p, r, n, op.ld_out), lo_plane(p, op.ld_out), gelu_exact(v));
         return;
     case kEpQkv: {
         // Head h's rows: its q, k and v rows, padded to a whole tile.
@@ -793,14 +836,15 @@ __device__ __forceinline__ void emit_output(const StepParams& p, const StepOp& o
     }
 }
 
-// Work area of a product: [xs: RT x pitch 16-bit][red: 8 x 16 x RT][tile: 16 x RT]
+// Work area of a product: [xs: 2 planes x RT x pitch 16-bit][red: 8 x 16 x RT][tile: 16 x RT]
 //                         [best values: out_rows][best indices: out_rows]
 template <typename WT, int NT>
 __device__ void op_product(const StepParams& p, const StepOp& op, int position, Stream& s, unsigned char* work) {
     constexpr int RT = 8 * NT;
     const int pitch = tile_pitch(p.kpd);
     WT* xs = reinterpret_cast<WT*>(work);
-    float* red = reinterpret_cast<float*>(work + (size_t)RT * pitch * sizeof(WT));
+    const size_t xs_lo = (size_t)RT * pitch;
+    float* red = reinterpret_cast<float*>(work + 2 * xs_lo * sizeof(WT));
     const bool normalise = op.gamma != nullptr;
     const int n_tiles = (op.n + 15) / 16;
     const int r_tiles = (p.rows + RT - 1) / RT;
@@ -837,18 +881,19 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
                                       blockIdx.x == (unsigned)((r_tile * n_tiles) % gridDim.x) ? op.sum_out : nullptr};
                     }
                     layer_norm_tile<WT>(p, op.norm_input ? op.norm_input : p.h, op.gamma, op.beta, r0, rows_valid,
-                                        1, 0, xs, pitch, nullptr, add);
+                                        1, 0, xs, pitch, xs_lo, nullptr, add);
                 }
                 else
-                    stage_rows<WT>(static_cast<const WT*>(op.input16), op.ld_input, r0, rows_valid, op.kp, xs, pitch);
+                    stage_rows<WT>(static_cast<const WT*>(op.input16), op.ld_input, lo_plane(p, op.ld_input), r0,
+                                   rows_valid, op.kp, xs, pitch, xs_lo);
                 consumer_sync();
                 trn.end(kTrNorm);
                 cached_tile = r_tile;
             }
-            ok = product_tile<WT, NT, true>(p, s, op.kp, xs, pitch, rows_valid, acc);
+            ok = product_tile<WT, NT, true>(p, s, op.kp, xs, pitch, xs_lo, rows_valid, acc);
         } else {
             const WT* X = static_cast<const WT*>(op.input16) + (size_t)r0 * op.ld_input;
-            ok = product_tile<WT, NT, false>(p, s, op.kp, X, op.ld_input, rows_valid, acc);
+            ok = product_tile<WT, NT, false>(p, s, op.kp, X, op.ld_input, lo_plane(p, op.ld_input), rows_valid, acc);
         }
         if (!ok) return;
         Trace tre = trace_of(p.profile);
@@ -897,51 +942,11 @@ constexpr int kMaxXStages = 4;
 constexpr int kIssueWarp = 4;  // not one of the epilogue warps 0..3
 constexpr int kJoinBatch = 8;  // split partials a thread loads before summing
 
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (version 1 for sm_100).
-__device__ __forceinline__ uint64_t umma_desc(uint32_t address) {
-    return (uint64_t)((address >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-// Instruction descriptor of kind::f16: fp32 accumulation, both operands
-// 16-bit (f16 or bf16 alike) and K-major, M = 128, N = n.
-template <typename WT>
-__device__ __forceinline__ uint32_t umma_idesc(int n) {
-    const uint32_t ab = std::is_same<WT, __nv_bfloat16>::value ? 1u : 0u;
-    return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-__device__ __forceinline__ void umma_mma(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-}
-// The mbarrier receives one arrival once every product this thread issued
-// so far has completed.
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_address(bar))
-                 : "memory");
-}
 __device__ __forceinline__ void stage_arrive(const Stream& s, unsigned long long index, unsigned count) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_address(s.empty + index % s.stages)),
                  "r"(count)
                  : "memory");
 }
-// 32 columns of this warp's 32 lanes; the load and its wait are one asm
-// statement, so no use of the registers can be scheduled before the wait.
-__device__ __forceinline__ void tmem_load32(uint32_t address, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
-        "tcgen05.wait::ld.sync.aligned;\n"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(address)
-        : "memory");
-}
-
 template <typename WT>
 __device__ void product_umma(const StepParams& p, const StepOp& op, int position, int step, int op_index, Stream& s,
                              TensorMemory& tm) {
@@ -962,8 +967,11 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
             // (whose grid barrier has passed): generic writes ordered before
             // these bulk reads, then one copy a block into the X stages.
             asm volatile("fence.proxy.async.global;\n" ::: "memory");
+            // Each stage takes the block's hi rows, then its lo rows (the lo
+            // plane, act_rows * kp elements on).
             const unsigned char* src = static_cast<const unsigned char*>(op.input16) +
                                        ((size_t)u.kb0 * p.act_rows + r0) * 128;
+            const size_t lo_bytes = lo_plane(p, op.kp) * 2;
             const unsigned bytes = (unsigned)n16 * 128u;
             for (int j = 0; j < nkb; ++j) {
                 const unsigned long long q = x0 + j;
@@ -972,11 +980,18 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
                     !wait_parity(p, tm.x_empty + st, (uint32_t)((q / tm.x_stages - 1) & 1), nullptr, kWaitEmpty, q))
                     break;
                 const uint32_t bar = smem_address(tm.x_full + st);
-                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+                const uint32_t dst = smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes);
+                const unsigned char* from = src + (size_t)j * p.act_rows * 128;
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(2 * bytes)
+                             : "memory");
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                    "l"(from), "r"(bytes), "r"(bar)
+                    : "memory");
                 asm volatile(
                     "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                        smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes)),
-                    "l"(src + (size_t)j * p.act_rows * 128), "r"(bytes), "r"(bar)
+                        dst + bytes),
+                    "l"(from + lo_bytes), "r"(bytes), "r"(bar)
                     : "memory");
             }
         }
@@ -991,10 +1006,13 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
                     const int st = (int)(q % tm.x_stages);
                     wait_parity(p, tm.x_full + st, (uint32_t)((q / tm.x_stages) & 1), nullptr, kWaitUnit, q);
                     const uint32_t x = smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes);
+                    const uint32_t x_lo = x + (uint32_t)n16 * 128u;
                     const uint32_t wb = w + (uint32_t)(j - j0) * 16384u;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
+                    for (int kk = 0; kk < 4; ++kk) {
                         umma_mma(tm.base, umma_desc(wb + 32 * kk), umma_desc(x + 32 * kk), idesc, (j | kk) != 0);
+                        umma_mma(tm.base, umma_desc(wb + 32 * kk), umma_desc(x_lo + 32 * kk), idesc, 1u);
+                    }
                     umma_commit(tm.x_empty + st);  // the X stage: free once these products have read it
                 }
                 // The weight stage is free after kWarps arrivals: kWarps - 1
@@ -1113,7 +1131,8 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
     constexpr int RT = 8 * NT;
     const int pitch = tile_pitch(p.kpd);
     WT* xs = reinterpret_cast<WT*>(work);
-    float* fold_v = reinterpret_cast<float*>(work + (size_t)RT * pitch * sizeof(WT));  // [8 warps][RT]
+    const size_t xs_lo = (size_t)RT * pitch;
+    float* fold_v = reinterpret_cast<float*>(work + 2 * xs_lo * sizeof(WT));  // [8 warps][RT]
     uint32_t* fold_i = reinterpret_cast<uint32_t*>(fold_v + kWarps * RT);
     float* best_v = reinterpret_cast<float*>(fold_i + kWarps * RT);
     uint32_t* best_i = reinterpret_cast<uint32_t*>(best_v + p.out_rows);
@@ -1148,10 +1167,11 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
         Trace trn = trace_of(p.profile);
         trn.begin();
         if (op.input16)  // rows normalised by a norm op
-            stage_rows<WT>(static_cast<const WT*>(op.input16), op.ld_input, r0, rows_valid, p.kpd, xs, pitch);
+            stage_rows<WT>(static_cast<const WT*>(op.input16), op.ld_input, lo_plane(p, op.ld_input), r0, rows_valid,
+                           p.kpd, xs, pitch, xs_lo);
         else
             layer_norm_tile<WT>(p, p.h, p.final_gamma, p.final_beta, r0, rows_valid, p.row_step, p.row_offset, xs,
-                                pitch, p.hidden_out);
+                                pitch, xs_lo, p.hidden_out);
         consumer_sync();
         trn.end(kTrNorm);
 
@@ -1183,7 +1203,7 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
                 Trace tr = trace_of(p.profile);
                 tr.begin();
                 const int c0 = b * stage_chunks, n = min(stage_chunks, chunks - c0);
-                chunks_product<WT, NT, true>(unit, 0, 1, n, xs, pitch, c0 * 32, x_ok, acc);
+                chunks_product<WT, NT, true>(unit, 0, 1, n, xs, pitch, xs_lo, c0 * 32, x_ok, acc);
                 tr.end(kTrCompute);
                 release_at(s, index, kWarps);
             }
@@ -1304,7 +1324,8 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
 
 // Head `head`'s share of the attention out-projection for row r: the d
 // outputs W[:, 64 head .. 64 head + 63] . a, with a the head's 64 attended
-// values (16-bit, shared memory, 16-byte aligned), written to op.out_partial
+// values (16-bit, shared memory, 16-byte aligned: hi a[0..63], lo
+// a[64..127], both multiplied), written to op.out_partial
 // [head][r][:] (Decoder.cpp:80-104 adds out_proj(attention) to h; the op
 // after this one adds the heads' partials in head order, with the bias).
 // The head's columns are chunks 2 head and 2 head + 1 of every 16-row tile
@@ -1321,6 +1342,8 @@ __device__ void head_out_projection(const StepParams& p, const StepOp& op, int r
     const uint4 zero = make_uint4(0, 0, 0, 0);
     const uint4 x0 = gq == 0 ? *reinterpret_cast<const uint4*>(a + 8 * tq) : zero;
     const uint4 x1 = gq == 0 ? *reinterpret_cast<const uint4*>(a + 32 + 8 * tq) : zero;
+    const uint4 y0 = gq == 0 ? *reinterpret_cast<const uint4*>(a + 64 + 8 * tq) : zero;
+    const uint4 y1 = gq == 0 ? *reinterpret_cast<const uint4*>(a + 96 + 8 * tq) : zero;
     const unsigned char* wbase = static_cast<const unsigned char*>(op.out_weight);
     float* out = op.out_partial + ((size_t)head * p.rows + r) * d;
     constexpr int kBatch = 6;
@@ -1351,10 +1374,16 @@ __device__ void head_out_projection(const StepParams& p, const StepOp& op, int r
             const uint32_t a3[4] = {w[i][2].z, w[i][3].z, w[i][2].w, w[i][3].w};
             const uint32_t b0[2] = {x0.x, x0.y}, b1[2] = {x0.z, x0.w};
             const uint32_t b2[2] = {x1.x, x1.y}, b3[2] = {x1.z, x1.w};
+            const uint32_t c0[2] = {y0.x, y0.y}, c1[2] = {y0.z, y0.w};
+            const uint32_t c2[2] = {y1.x, y1.y}, c3[2] = {y1.z, y1.w};
             mma_16816<WT>(acc, a0, b0);
             mma_16816<WT>(acc, a1, b1);
             mma_16816<WT>(acc, a2, b2);
             mma_16816<WT>(acc, a3, b3);
+            mma_16816<WT>(acc, a0, c0);
+            mma_16816<WT>(acc, a1, c1);
+            mma_16816<WT>(acc, a2, c2);
+            mma_16816<WT>(acc, a3, c3);
             // Column 0 (the one input row) sits in lanes tq == 0: weight rows gq, gq + 8.
             if (tq == 0) {
                 const int n = 16 * t + gq;
@@ -1587,16 +1616,16 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
         }
         trs.end(kTrSelf);
         if (op.out_weight) {
-            // The head's out-projection share, from its 16-bit values.
-            __shared__ __align__(16) WT attended[64];
-            for (int c = threadIdx.x; c < 64; c += kThreads) attended[c] = Half16<WT>::from_float(result[c] / l);
+            // The head's out-projection share, from its 16-bit values (hi, lo).
+            __shared__ __align__(16) WT attended[128];
+            for (int c = threadIdx.x; c < 64; c += kThreads) store_split(attended + c, 64, result[c] / l);
             consumer_sync();
             head_out_projection<WT>(p, op, r, head, attended);
             continue;
         }
         WT* out = static_cast<WT*>(p.attn16);
         for (int c = threadIdx.x; c < D; c += kThreads)
-            out[act_index(p, r, head * D + c, p.kpd)] = Half16<WT>::from_float(result[c] / l);
+            store_split(out + act_index(p, r, head * D + c, p.kpd), lo_plane(p, p.kpd), result[c] / l);
     }
 }
 
@@ -1708,7 +1737,7 @@ __device__ void self_attention_warps(const StepParams& p, const StepOp& op, int 
             const float inv = 1.f / l;
 #pragma unroll
             for (int i = 0; i < 8; ++i)
-                out[act_index(p, r, head * 64 + 8 * piece + i, p.kpd)] = Half16<WT>::from_float(acc[i] * inv);
+                store_split(out + act_index(p, r, head * 64 + 8 * piece + i, p.kpd), lo_plane(p, p.kpd), acc[i] * inv);
         }
         __syncwarp();
     }
@@ -1812,14 +1841,15 @@ __device__ void cross_join(const StepParams& p, const StepOp& op, int r, int hea
     const float a0 = o[0] / l + (op.value_bias && c0 < D ? __ldg(op.value_bias + head * D + c0) : 0.f);
     const float a1 = o[1] / l + (op.value_bias && c1 < D ? __ldg(op.value_bias + head * D + c1) : 0.f);
     if (to_shared) {
-        // A fused out-projection reads the 16-bit values from shared memory.
-        if (c0 < D) to_shared[c0] = Half16<WT>::from_float(a0);
-        if (c1 < D) to_shared[c1] = Half16<WT>::from_float(a1);
+        // A fused out-projection reads the 16-bit values (hi, then lo 64 on)
+        // from shared memory.
+        if (c0 < D) store_split(to_shared + c0, 64, a0);
+        if (c1 < D) store_split(to_shared + c1, 64, a1);
         return;
     }
     WT* out = static_cast<WT*>(p.attn16);
-    if (c0 < D) out[act_index(p, r, head * D + c0, p.kpd)] = Half16<WT>::from_float(a0);
-    if (c1 < D) out[act_index(p, r, head * D + c1, p.kpd)] = Half16<WT>::from_float(a1);
+    if (c0 < D) store_split(out + act_index(p, r, head * D + c0, p.kpd), lo_plane(p, p.kpd), a0);
+    if (c1 < D) store_split(out + act_index(p, r, head * D + c1, p.kpd), lo_plane(p, p.kpd), a1);
 }
 
 // Shared memory: [q: 64][max: 2 x 8][sum: 2 x 8][fold: 2 x kWarps x 64][scores: kMaxCrossUnitKeys]
@@ -1880,8 +1910,9 @@ __device__ void cross_attention_cores(const StepParams& p, const StepOp& op, Str
         }
         if (S == 1) {
             if (threadIdx.x < D)
-                static_cast<WT*>(p.attn16)[act_index(p, r, head * D + threadIdx.x, p.kpd)] = Half16<WT>::from_float(
-                    o_run / l_run + (op.value_bias ? __ldg(op.value_bias + head * D + threadIdx.x) : 0.f));
+                store_split(static_cast<WT*>(p.attn16) + act_index(p, r, head * D + threadIdx.x, p.kpd),
+                            lo_plane(p, p.kpd),
+                            o_run / l_run + (op.value_bias ? __ldg(op.value_bias + head * D + threadIdx.x) : 0.f));
             continue;
         }
         float* part = p.partial + (((size_t)r * H + head) * S + split) * (D + 2);
@@ -1926,7 +1957,7 @@ constexpr int kCrossQueryOffset = 2304;
 // keep_sum: this CTA stores the sums as the new residual rows.  The head's
 // four 16-row weight tiles come off the weight stream ahead of the item's
 // keys, one tile to each of the first four warps.  Work area at `area`:
-// [xs: 8 x pitch 16-bit].
+// [xs: 2 planes x 8 x pitch 16-bit].
 template <typename WT>
 __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int head, bool keep_sum, Stream& s,
                             unsigned char* area, float* q) {
@@ -1941,8 +1972,8 @@ __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int he
     Addends add;
     if (op.addend_count > 0)
         add = Addends{op.addends, op.addend_count, op.addend_stride, op.addend_bias, keep_sum ? op.sum_out : nullptr};
-    layer_norm_tile<WT>(p, op.norm_input ? op.norm_input : p.h, op.gamma, op.beta, r, 1, 1, 0, xs, pitch, nullptr,
-                        add);
+    layer_norm_tile<WT>(p, op.norm_input ? op.norm_input : p.h, op.gamma, op.beta, r, 1, 1, 0, xs, pitch,
+                        (size_t)8 * pitch, nullptr, add);
     consumer_sync();
     // Warp j < tiles owns q tile j (one unit: a stage holds a whole tile)
     // over all of K, so no partial sums cross warps.
@@ -1951,7 +1982,7 @@ __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int he
         const unsigned char* unit = owned_unit_at(p, s, index);
         float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
         const bool x_ok[1] = {(lane >> 2) == 0};
-        chunks_product<WT, 1, true>(unit, 0, 1, op.kp / 32, xs, pitch, 0, x_ok, acc);
+        chunks_product<WT, 1, true>(unit, 0, 1, op.kp / 32, xs, pitch, (size_t)8 * pitch, 0, x_ok, acc);
         release_at(s, index, kWarps);
         // Column 0 (the one row) sits in lanes t == 0: q rows g and g + 8 of the tile.
         if ((lane & 3) == 0) {
@@ -1989,7 +2020,7 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
     float* wsum = wmax + 8;
     float* wrows = wsum + 8;
     __shared__ int is_last;
-    __shared__ __align__(16) WT attended[64];  // a fused out-projection's input
+    __shared__ __align__(16) WT attended[128];  // a fused out-projection's input (hi, lo)
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int split = item % S, head = (item / S) % H, r = item / (S * H);
         const int count = cross_item_units(op, item, units);
@@ -2143,13 +2174,14 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
         if (S == 1) {
             const float a = O / L + (op.value_bias ? __ldg(op.value_bias + head * 64 + (threadIdx.x & 63)) : 0.f);
             if (op.out_weight) {
-                if (threadIdx.x < 64) attended[threadIdx.x] = Half16<WT>::from_float(a);
+                if (threadIdx.x < 64) store_split(attended + threadIdx.x, 64, a);
                 consumer_sync();
                 head_out_projection<WT>(p, op, r, head, attended);
                 continue;
             }
             if (threadIdx.x < 64)
-                static_cast<WT*>(p.attn16)[act_index(p, r, head * 64 + threadIdx.x, p.kpd)] = Half16<WT>::from_float(a);
+                store_split(static_cast<WT*>(p.attn16) + act_index(p, r, head * 64 + threadIdx.x, p.kpd),
+                            lo_plane(p, p.kpd), a);
             continue;
         }
         Trace trj = trace_of(p.profile);
@@ -2351,7 +2383,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
 template <typename WT, int NT>
 size_t work_bytes(const StepParams& p, int max_chunk) {
     constexpr int RT = 8 * NT;
-    const size_t product = (size_t)RT * tile_pitch(p.kpd) * sizeof(WT) +
+    const size_t product = (size_t)2 * RT * tile_pitch(p.kpd) * sizeof(WT) +
                            sizeof(float) * (kWarps * 16 * RT + 16 * RT) + (size_t)p.out_rows * 8 +
                            sizeof(float) * 2 * kWarps * RT;
     const size_t attention =
@@ -2398,10 +2430,13 @@ int occupancy_typed(const StepParams& p, int max_chunk) {
     return blocks;
 }
 
-// Input rows per tile: 8, 16, or 32 (more rows run as several tiles).
+// Input rows per tile: 8, 16, or 32 (more rows run as several tiles); the
+// host may ask for fewer (p.tile_columns) when the tile's two planes leave
+// too little shared memory for the weight stream.
 inline int tile_columns(const StepParams& p) {
     const int rows = std::max(p.rows, p.out_rows);
-    return rows <= 8 ? 1 : (rows <= 16 ? 2 : 4);
+    const int wanted = rows <= 8 ? 1 : (rows <= 16 ? 2 : 4);
+    return p.tile_columns > 0 && p.tile_columns < wanted ? p.tile_columns : wanted;
 }
 
 template <typename WT>

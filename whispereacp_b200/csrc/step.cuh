@@ -167,6 +167,9 @@ struct StepParams {
     // above; act_rows rows an activation block; a product item covers
     // umma_rows rows (<= 256) of 128 weight rows.
     int umma, act_rows, umma_rows;
+    // Input rows of a general product's or the logits' tile: 8 * tile_columns
+    // (1, 2 or 4; 0: chosen from the rows).
+    int tile_columns;
     float* partial_d;                   // fp32 split-K partials of a tensor-core product
     unsigned* split_counters;           // [n_ops][kSplitSlots] split arrivals (zero at launch)
     int umma_x_stages, umma_x_stage_bytes;  // the activation ring in the work area

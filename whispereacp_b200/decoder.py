@@ -130,6 +130,22 @@ class Decoder:
         check(self._lib.wsp_decoder_set_tensor(self._handle, name.encode(), dtype, extents,
                                                values.ndim, _pointer(values)))
 
+    NARROWING = {"round": 0, "exact": 1}
+
+    def set_narrowing(self, mode: str) -> None:
+        """"round" (the default: nearest even) or "exact" (the reference's
+        ExactHalf rule: a projection that does not narrow to the storage type
+        unchanged is refused with ModelError naming it)."""
+        if mode not in self.NARROWING:
+            raise ValueError(f"narrowing must be one of {sorted(self.NARROWING)}")
+        check(self._lib.wsp_decoder_set_narrowing(self._handle, self.NARROWING[mode]))
+
+    def narrowing(self) -> tuple[int, float]:
+        """(tensors narrowed inexactly so far, the largest change of a value)."""
+        tensors, largest = ctypes.c_int(), ctypes.c_double()
+        check(self._lib.wsp_decoder_narrowing(self._handle, ctypes.byref(tensors), ctypes.byref(largest)))
+        return tensors.value, largest.value
+
     def load_weights(self, tensors: dict[str, np.ndarray]) -> None:
         """Every decoder tensor of a checkpoint (a safetensors file's dict)."""
         for name, values in tensors.items():
