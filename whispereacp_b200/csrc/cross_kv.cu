@@ -21,7 +21,7 @@
 //                the epilogue of one overlaps the products of the next;
 //   warps 0..3   read the accumulator back (tcgen05.ld, a TMEM lane = an
 //                encoder row), narrow to the cache's 16-bit type and store
-//                each row's pieces straight into the (window, layer, head)
+//                each row's pieces straight into the (layer, window, head)
 //                block they belong to, rotated for the attention's reads.
 //
 // Three stages of (A hi, A lo, B) = 64 KB ring between producers and the
@@ -249,10 +249,17 @@ __device__ void issue_products(const CrossKvArgs& a, unsigned char* smem, uint64
         }
 }
 
+// The cache block of (window, group = layer * H + head): [layer][window][head].
+__device__ __forceinline__ size_t cache_block(const CrossKvArgs& a, int window, int group) {
+    const int layer = group / a.heads, head = group % a.heads;
+    return ((size_t)layer * a.windows + window) * a.heads + head;
+}
+
 // Warps 0..3: row 32 w + lane of each tile from its accumulator into the
 // cache.  With 64-wide heads a 256-column accumulator is two (layer, head)
 // groups of K | V; each 32-column read is four 16-byte pieces of one row,
-// stored at their rotated places (cross_piece).
+// stored at their rotated places (cross_piece) in their (layer, window,
+// head) block.
 template <typename WT>
 __device__ void store_tiles(const CrossKvArgs& a, uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem,
                             int row_tiles, int weight_tiles, long long tiles, volatile int* abort) {
@@ -274,7 +281,7 @@ __device__ void store_tiles(const CrossKvArgs& a, uint64_t* acc_full, uint64_t* 
             if (!row_ok || n0 >= a.columns) continue;
             if (a.head_width == 64) {
                 const int group = n0 / 128, piece0 = (n0 % 128) / 8;
-                WT* block = out + (((size_t)t.window * a.groups + group) * a.row_stride + row) * 128;
+                WT* block = out + (cache_block(a, t.window, group) * a.row_stride + row) * 128;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     uint4 piece;
@@ -289,7 +296,7 @@ __device__ void store_tiles(const CrossKvArgs& a, uint64_t* acc_full, uint64_t* 
                     const int n = n0 + j;
                     if (n >= a.columns) break;
                     const int group = n / two_d, c = n % two_d;
-                    out[(((size_t)t.window * a.groups + group) * a.row_stride + row) * two_d + c] =
+                    out[(cache_block(a, t.window, group) * a.row_stride + row) * two_d + c] =
                         Half16<WT>::from_float(__uint_as_float(v[j]));
                 }
             }
@@ -383,6 +390,7 @@ size_t cross_kv_shared_bytes() { return 1024 + (size_t)kStages * kStageBytes; }
 void launch_cross_kv(bool half, const CrossKvArgs& a, int sm_count, cudaStream_t stream) {
     if (a.windows <= 0 || a.rows <= 0 || a.rows > a.row_stride || a.width <= 0 || a.width % 4 != 0 ||
         a.kblocks != (a.width + 63) / 64 || a.columns <= 0 || a.head_width <= 0 || a.groups <= 0 ||
+        a.heads <= 0 || a.groups % a.heads != 0 ||
         a.columns != a.groups * 2 * a.head_width || (reinterpret_cast<uintptr_t>(a.encoder) & 15) != 0 ||
         (reinterpret_cast<uintptr_t>(a.weight) & 15) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15) != 0)
         throw std::runtime_error("cross key/value projection: arguments out of range");

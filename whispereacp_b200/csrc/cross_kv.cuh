@@ -8,7 +8,9 @@
 // head) group's 2D weight rows gives one product per window,
 // E_b [X, d] x W^T [d, L*2d], whose columns are the groups' blocks side by
 // side; the kernel writes each 2D-column slice straight into the group's
-// block of the cache layout [window][layer][head][X][K | V] (64-wide heads:
+// block of the cache layout [layer][window][head][X][K | V] (a layer's keys
+// and values for every window contiguous, as one step's cross attention of
+// that layer reads them; 64-wide heads:
 // with each 256-byte row's 16-byte pieces rotated by cross_piece, the order
 // the decode kernel's tensor-core attention reads).  The value bias is not
 // added here: the attention adds it after normalising (the weights sum to
@@ -38,7 +40,7 @@ __host__ __device__ inline size_t cross_weight_offset(int n, int k, int kblocks)
 struct CrossKvArgs {
     const float* encoder;   // fp32 [windows][row_stride][width], 16-byte aligned
     const void* weight;     // 16-bit, cross_weight_offset layout, n_tiles x kblocks blocks
-    void* out;              // 16-bit [windows][groups][row_stride][2 * head_width]
+    void* out;              // 16-bit [layers][windows][heads][row_stride][2 * head_width]
     int windows;
     int rows;               // encoder rows of each window projected (<= row_stride)
     int row_stride;         // rows a window holds in `encoder` and in `out` (X)
@@ -47,6 +49,7 @@ struct CrossKvArgs {
     int columns;            // L * 2d: weight rows
     int head_width;         // D
     int groups;             // L * H
+    int heads;              // H
     int* status;            // nonzero on return: a bounded wait gave up (which one)
 };
 

@@ -188,7 +188,13 @@ public:
             if (global == 0) {
                 require_extents(name, extents, rank, {shape_.vocabulary_size, d});
                 audit_narrowing(name, dtype, data, (size_t)shape_.vocabulary_size * d);
-                upload_packed(token_table_, 0, shape_.vocabulary_size, d, padded(d), dtype, data);
+                // The layout of the logits' products (fragment-packed, or the
+                // tcgen05 tiles); the embedding gathers from the same table.
+                if (umma_)
+                    patch16(token_table_, shape_.vocabulary_size, d, dtype, data,
+                            [&](int r, int c) { return weight_offset(r, c, padded(d)); });
+                else
+                    upload_packed(token_table_, 0, shape_.vocabulary_size, d, padded(d), dtype, data);
             } else if (global == 1) {
                 // A model may carry more positions than a run needs; fewer is an error.
                 if (rank != 2 || extents[1] != d || extents[0] < shape_.max_positions)
@@ -330,7 +336,7 @@ public:
 
         // recordSequenceStart (Decoder.cpp:121-146): every layer's cross keys
         // and values for every window in one tcgen05 launch (cross_kv.cuh),
-        // written as the cache layout [window][layer][head][X][K | V].  The
+        // written as the cache layout [layer][window][head][X][K | V].  The
         // value bias is added after the attention instead (the weights sum
         // to one).
         const int d = shape_.width, D = d / shape_.heads;
@@ -346,6 +352,7 @@ public:
         args.columns = 2 * d * shape_.layers;
         args.head_width = D;
         args.groups = shape_.layers * shape_.heads;
+        args.heads = shape_.heads;
         args.status = state_.get<int>() + kCrossStatusWord;
         CUDA_CHECK(cudaMemsetAsync(args.status, 0, sizeof(int), stream_));
         try {
@@ -661,11 +668,11 @@ private:
     // The products' form.  tcgen05 tiles (128 weight rows against every
     // window's row, accumulated in tensor memory) need widths in 64-column
     // blocks, 64-wide heads and at least 16 windows (an MMA's N >= 16).
-    // Measured on B200 they beat the mma.sync tiles once 128 windows share
-    // each weight tile (large-v3, 128 windows: 33 us a product against 37)
-    // and lose below (medium.en at 64 windows: 19 against 14), so AUTO picks
-    // them from kUmmaWindows windows.
-    static constexpr int kUmmaWindows = 128;
+    // With the activations' hi and lo planes, measured on B200 they beat the
+    // mma.sync tiles from 32 windows (small.en at 32 windows: 10.3 us a
+    // product against 13.2; medium.en at 64: 12.7 against 20.4), so AUTO
+    // picks them from kUmmaWindows windows.
+    static constexpr int kUmmaWindows = 32;
     bool umma_possible() const {
         return windows_ >= 16 && shape_.width % 64 == 0 && shape_.feed_forward_width % 64 == 0 && head_width() == 64;
     }
@@ -706,7 +713,7 @@ private:
         const size_t d = shape_.width, f = shape_.feed_forward_width, L = shape_.layers;
         const size_t H = shape_.heads, D = d / H;
         const size_t kpd = padded(d), kpf = padded(f);
-        token_table_.allocate(round16(shape_.vocabulary_size) * kpd * 2);
+        token_table_.allocate(weight_rows(shape_.vocabulary_size) * kpd * 2);
         position_table_.allocate((size_t)shape_.max_positions * d * 4);
         final_w_.allocate(d * 4);
         final_b_.allocate(d * 4);
@@ -939,10 +946,11 @@ private:
             }
             cross.kind = kOpCrossAttention;
             const long long head_block = (long long)shape_.cross_positions * 2 * D;
-            cross.keys = cross_kv_.get<char>() + (size_t)l * H * head_block * elem;
+            // [layer][window][head][X][K | V]: the layer's blocks for every window together.
+            cross.keys = cross_kv_.get<char>() + (size_t)l * windows_ * H * head_block * elem;
             cross.key_stride = 2 * D;
             cross.head_stride = head_block;
-            cross.window_stride = (long long)shape_.layers * H * head_block;
+            cross.window_stride = (long long)H * head_block;
             cross.key_count = active_cross_;
             cross.chunk = cs.chunk;
             cross.span = cs.span;
@@ -997,6 +1005,7 @@ private:
             norm.norm_step = p.row_step;
             norm.norm_offset = p.row_offset;
             norm.norm_hidden = p.hidden_out;
+            norm.norm_umma = umma_ ? 1 : 0;  // the tcgen05 logits read the block layout
             ops.push_back(norm);
             logits.input16 = normalised_.get();
             logits.ld_input = kpd;

@@ -120,6 +120,23 @@ inline void append_umma_units(const StepParams& p, const StepOp& op, int cta, in
     }
 }
 
+// Tensor-core logits: item (128 vocabulary rows, 128 sampled rows), CTA c
+// taking items c, c + grid, ...; the token table's k-blocks of the item's
+// vocabulary tile, umma_blocks to a unit, as logits_umma reads them.
+inline void append_logits_umma_units(const StepParams& p, int cta, int grid, std::vector<ScheduleEntry>& out) {
+    const int kblocks = p.kpd / 64, vocab_tiles = (p.vocabulary + 127) / 128;
+    const int items = vocab_tiles * ((p.out_rows + 127) / 128);
+    for (int item = cta; item < items; item += grid) {
+        const int m = item % vocab_tiles;
+        for (int kb = 0; kb < kblocks; kb += p.umma_blocks) {
+            const int n = std::min(p.umma_blocks, kblocks - kb);
+            out.push_back(schedule_entry(static_cast<const unsigned char*>(p.token_table) +
+                                             ((size_t)m * kblocks + kb) * 16384,
+                                         16384u * (unsigned)n));
+        }
+    }
+}
+
 // What an op reads straight from memory that no op writes, for the
 // producers to prefetch into L2 just ahead of it: LayerNorm gains and
 // offsets, biases, the mask, a fused out-projection's head columns (2 KB of
@@ -186,6 +203,10 @@ inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, 
             }
             if (op.kind == kOpProduct && p.umma) {
                 append_umma_units(p, op, cta, grid, units);
+                continue;
+            }
+            if (op.kind == kOpLogits && p.umma) {
+                append_logits_umma_units(p, cta, grid, units);
                 continue;
             }
             const int items = op_items(p, op, rt);

@@ -401,8 +401,12 @@ __device__ void op_embed(const StepParams& p, int position) {
         const float* pos = p.position_table + (size_t)at * p.width;
         float* out = p.h + (size_t)r * p.width;
         const int chunks = p.kpd / 32;
+        // The token table is laid out for the logits' products: fragment-packed,
+        // or the tcgen05 tiles with the tensor-core products.
         for (int c = threadIdx.x; c < p.width; c += kThreads)
-            out[c] = Half16<WT>::to_float(table[packed_offset((int)token, c, chunks)]) + pos[c];
+            out[c] = Half16<WT>::to_float(table[p.umma ? umma_offset((int)token, c, p.kpd / 64)
+                                                       : packed_offset((int)token, c, chunks)]) +
+                     pos[c];
     }
 }
 
@@ -1121,6 +1125,67 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
 
 // ------------------------------------------------------------------- logits
 
+// This CTA's per-row candidates best_v/best_i (shared memory, out_rows
+// each), then the fold of every CTA's by whichever CTA finishes last: it
+// writes each window's sampled id into its next token slot and advances the
+// position (Argmax.h:83-201's two passes, across CTAs).
+__device__ void logits_fold(const StepParams& p, int position, const float* best_v, const uint32_t* best_i) {
+    __shared__ int is_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // This CTA's candidates, then the fold by whichever CTA finishes last.
+    Trace trf = trace_of(p.profile);
+    trf.begin();
+    for (int r = threadIdx.x; r < p.out_rows; r += kThreads) {
+        p.candidate_values[(size_t)r * gridDim.x + blockIdx.x] = best_v[r];
+        p.candidate_indices[(size_t)r * gridDim.x + blockIdx.x] = best_i[r];
+    }
+    consumer_sync();
+    if (threadIdx.x == 0) is_last = arrive_acq_rel(p.logits_counter) == gridDim.x - 1;
+    consumer_sync();
+    if (!is_last) {
+        trf.end(kTrLogitsFold);
+        return;
+    }
+    const int rows_per_window = p.out_rows / p.windows;
+    for (int r = warp; r < p.out_rows; r += kWarps) {
+        float bv = -INFINITY;
+        uint32_t bi = kUnchosen;
+        for (int c = lane; c < (int)gridDim.x; c += 32) {
+            const float v = ld_cg(p.candidate_values + (size_t)r * gridDim.x + c);
+            const uint32_t i = ld_cg(p.candidate_indices + (size_t)r * gridDim.x + c);
+            if (candidate_better(v, i, bv, bi)) { bv = v; bi = i; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (candidate_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) {
+            const uint32_t chosen = bi == kUnchosen ? 0u : bi;  // Argmax.h:190-193
+            if (p.row_tokens) p.row_tokens[r] = chosen;
+            const int b = r / rows_per_window;
+            if (p.write_ring && r % rows_per_window == rows_per_window - 1) {
+                p.ring[(size_t)b * p.ring_stride + position + p.tokens] = chosen;
+                if (p.stop_enabled && chosen == p.stop_token) p.ended[b] = 1;
+            }
+        }
+    }
+    consumer_sync();
+    if (threadIdx.x == 0) {
+        if (p.stop_enabled) {
+            int all = 1;
+            for (int b = 0; b < p.windows; ++b) all &= p.ended[b] ? 1 : 0;
+            if (all) atomicExch(p.state + kAllEnded, 1);
+        }
+        atomicAdd(p.state + kStepsDone, 1);
+        atomicAdd(p.state + kPosition, p.tokens);
+        atomicExch(p.logits_counter, 0u);
+        // (The grid barrier after this op releases these writes.)
+    }
+    trf.end(kTrLogitsFold);
+}
+
 // LN(h) of the sampled rows against the tied token table, with the masked
 // argmax folded in: each CTA keeps, per row, the first maximum over the
 // columns it produced; the last CTA to finish folds the CTAs' candidates,
@@ -1136,7 +1201,6 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
     uint32_t* fold_i = reinterpret_cast<uint32_t*>(fold_v + kWarps * RT);
     float* best_v = reinterpret_cast<float*>(fold_i + kWarps * RT);
     uint32_t* best_i = reinterpret_cast<uint32_t*>(best_v + p.out_rows);
-    __shared__ int is_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
 
@@ -1266,58 +1330,157 @@ __device__ void op_logits(const StepParams& p, const StepOp& op, int position, S
     s.next = base + (unsigned long long)mine * blocks;
     consumer_sync();
 
-    // This CTA's candidates, then the fold by whichever CTA finishes last.
-    Trace trf = trace_of(p.profile);
-    trf.begin();
+    logits_fold(p, position, best_v, best_i);
+}
+
+// With the tensor-core products the logits are tcgen05 tiles too (the
+// token table is in their layout): item (128 vocabulary rows, up to 128
+// sampled rows), the table's k-blocks off the weight ring, the rows'
+// normalised hi and lo blocks off the activation ring, both products into
+// one accumulator (lane = vocabulary row, column = sampled row).  Warps 0..3
+// read it back 32 columns at a time into shared memory, [vocabulary row]
+// [row], masked; then every consumer thread takes a share of one row's 128
+// entries, ascending, and the shares fold in order into the CTA's per-row
+// first maximum.  The fold across CTAs is logits_fold's.
+// Work area: [activation ring | tile: 128 x 33, shares: 2 x kWarps x 32]
+// [best values: out_rows][best indices: out_rows] -- the tile scratch
+// shares the activation ring's bytes: a tile is read back only once every
+// product of its item has completed, and the next item's blocks are fetched
+// after the CTA barrier that ends the item.
+constexpr int kLogitsTilePitch = 33;
+constexpr int kLogitsScratchBytes = (int)sizeof(float) * (128 * kLogitsTilePitch + 2 * kWarps * 32);
+
+template <typename WT>
+__device__ void logits_umma(const StepParams& p, const StepOp& op, int position, Stream& s, TensorMemory& tm) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t ring_bytes = (size_t)tm.x_stages * tm.x_stage_bytes;
+    float* tile = reinterpret_cast<float*>(tm.x_ring);
+    float* best_v = reinterpret_cast<float*>(tm.x_ring + max(ring_bytes, (size_t)kLogitsScratchBytes));
+    uint32_t* best_i = reinterpret_cast<uint32_t*>(best_v + p.out_rows);
+    float* share_v = tile + 128 * kLogitsTilePitch;
+    uint32_t* share_i = reinterpret_cast<uint32_t*>(share_v + kWarps * 32);
     for (int r = threadIdx.x; r < p.out_rows; r += kThreads) {
-        p.candidate_values[(size_t)r * gridDim.x + blockIdx.x] = best_v[r];
-        p.candidate_indices[(size_t)r * gridDim.x + blockIdx.x] = best_i[r];
+        best_v[r] = -INFINITY;
+        best_i[r] = kUnchosen;
     }
-    consumer_sync();
-    if (threadIdx.x == 0) is_last = arrive_acq_rel(p.logits_counter) == gridDim.x - 1;
-    consumer_sync();
-    if (!is_last) {
-        trf.end(kTrLogitsFold);
-        return;
-    }
-    const int rows_per_window = p.out_rows / p.windows;
-    for (int r = warp; r < p.out_rows; r += kWarps) {
-        float bv = -INFINITY;
-        uint32_t bi = kUnchosen;
-        for (int c = lane; c < (int)gridDim.x; c += 32) {
-            const float v = ld_cg(p.candidate_values + (size_t)r * gridDim.x + c);
-            const uint32_t i = ld_cg(p.candidate_indices + (size_t)r * gridDim.x + c);
-            if (candidate_better(v, i, bv, bi)) { bv = v; bi = i; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (candidate_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-        }
-        if (lane == 0) {
-            const uint32_t chosen = bi == kUnchosen ? 0u : bi;  // Argmax.h:190-193
-            if (p.row_tokens) p.row_tokens[r] = chosen;
-            const int b = r / rows_per_window;
-            if (p.write_ring && r % rows_per_window == rows_per_window - 1) {
-                p.ring[(size_t)b * p.ring_stride + position + p.tokens] = chosen;
-                if (p.stop_enabled && chosen == p.stop_token) p.ended[b] = 1;
+    const int vocab_tiles = (p.vocabulary + 127) / 128;
+    const int row_tiles = (p.out_rows + 127) / 128;
+    const int kblocks = p.kpd / 64;
+    const size_t lo_bytes = lo_plane(p, op.ld_input) * 2;
+    for (int item = blockIdx.x; item < vocab_tiles * row_tiles; item += gridDim.x) {
+        const int m = item % vocab_tiles, r0 = (item / vocab_tiles) * 128;
+        const int rows = min(128, p.out_rows - r0), n16 = (rows + 15) & ~15;
+        const unsigned long long x0 = tm.x_next;
+        if (threadIdx.x == 32 * kLoadWarp) {
+            // The rows' normalised blocks (the norm op before this one wrote
+            // them): hi, then lo, one stage a k-block.
+            asm volatile("fence.proxy.async.global;\n" ::: "memory");
+            const unsigned char* src = static_cast<const unsigned char*>(op.input16) + (size_t)r0 * 128;
+            const unsigned bytes = (unsigned)n16 * 128u;
+            for (int j = 0; j < kblocks; ++j) {
+                const unsigned long long q = x0 + j;
+                const int st = (int)(q % tm.x_stages);
+                if (q >= (unsigned long long)tm.x_stages &&
+                    !wait_parity(p, tm.x_empty + st, (uint32_t)((q / tm.x_stages - 1) & 1), nullptr, kWaitEmpty, q))
+                    break;
+                const uint32_t bar = smem_address(tm.x_full + st);
+                const uint32_t dst = smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes);
+                const unsigned char* from = src + (size_t)j * p.act_rows * 128;
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(2 * bytes)
+                             : "memory");
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+                    "l"(from), "r"(bytes), "r"(bar)
+                    : "memory");
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                        dst + bytes),
+                    "l"(from + lo_bytes), "r"(bytes), "r"(bar)
+                    : "memory");
             }
         }
-    }
-    consumer_sync();
-    if (threadIdx.x == 0) {
-        if (p.stop_enabled) {
-            int all = 1;
-            for (int b = 0; b < p.windows; ++b) all &= p.ended[b] ? 1 : 0;
-            if (all) atomicExch(p.state + kAllEnded, 1);
+        if (threadIdx.x == 32 * kIssueWarp) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t idesc = umma_idesc<WT>(n16);
+            for (int j0 = 0; j0 < kblocks; j0 += p.umma_blocks) {
+                const unsigned long long iw = s.next + j0 / p.umma_blocks;
+                const uint32_t w = smem_address(unit_at(p, s, iw));
+                for (int j = j0; j < kblocks && j < j0 + p.umma_blocks; ++j) {
+                    const unsigned long long q = x0 + j;
+                    const int st = (int)(q % tm.x_stages);
+                    wait_parity(p, tm.x_full + st, (uint32_t)((q / tm.x_stages) & 1), nullptr, kWaitUnit, q);
+                    const uint32_t x = smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes);
+                    const uint32_t x_lo = x + (uint32_t)n16 * 128u;
+                    const uint32_t wb = w + (uint32_t)(j - j0) * 16384u;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        umma_mma(tm.base, umma_desc(wb + 32 * kk), umma_desc(x + 32 * kk), idesc, (j | kk) != 0);
+                        umma_mma(tm.base, umma_desc(wb + 32 * kk), umma_desc(x_lo + 32 * kk), idesc, 1u);
+                    }
+                    umma_commit(tm.x_empty + st);
+                }
+                stage_arrive(s, iw, kWarps - 1);
+                umma_commit(s.empty + iw % s.stages);
+            }
+            umma_commit(tm.done);
         }
-        atomicAdd(p.state + kStepsDone, 1);
-        atomicAdd(p.state + kPosition, p.tokens);
-        atomicExch(p.logits_counter, 0u);
-        // (The grid barrier after this op releases these writes.)
+        s.next += (unsigned long long)((kblocks + p.umma_blocks - 1) / p.umma_blocks);
+        tm.x_next += (unsigned long long)kblocks;
+        // This thread's vocabulary row (warps 0..3) and whether it may win.
+        const int n = m * 128 + 32 * warp + lane;
+        const bool pick = warp < 4 && n < p.vocabulary && (p.mask == nullptr || __ldg(p.mask + n) == 0.f);
+        if (warp < 4) {
+            wait_parity(p, tm.done, tm.phase, nullptr, kWaitUnit, (unsigned long long)item);
+            __syncwarp();
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        }
+        tm.phase ^= 1u;
+        for (int c0 = 0; c0 < n16; c0 += 32) {
+            consumer_sync();  // the tile scratch is free
+            if (warp < 4) {
+                uint32_t v[32];
+                tmem_load32(tm.base + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float value = __uint_as_float(v[j]);
+                    if (p.logits_out && n < p.vocabulary && c0 + j < rows)
+                        p.logits_out[(size_t)(r0 + c0 + j) * p.vocabulary + n] = value;
+                    tile[(32 * warp + lane) * kLogitsTilePitch + j] = pick ? value : -INFINITY;
+                }
+            }
+            consumer_sync();
+            // Thread (part, column): vocabulary rows part*19 .. of column j.
+            const int j = threadIdx.x & 31, part = threadIdx.x >> 5;
+            float bv = -INFINITY;
+            uint32_t bi = kUnchosen;
+            for (int t = part * 19; t < min(128, part * 19 + 19); ++t) {
+                const float value = tile[t * kLogitsTilePitch + j];
+                const uint32_t index = (uint32_t)(m * 128 + t);
+                if (value != -INFINITY && candidate_better(value, index, bv, bi)) {
+                    bv = value;
+                    bi = index;
+                }
+            }
+            share_v[part * 32 + j] = bv;
+            share_i[part * 32 + j] = bi;
+            consumer_sync();
+            if (threadIdx.x < 32 && c0 + threadIdx.x < rows) {
+                const int r = r0 + c0 + threadIdx.x;
+                float v0 = best_v[r];
+                uint32_t i0 = best_i[r];
+                for (int w = 0; w < kWarps; ++w)
+                    if (candidate_better(share_v[w * 32 + threadIdx.x], share_i[w * 32 + threadIdx.x], v0, i0)) {
+                        v0 = share_v[w * 32 + threadIdx.x];
+                        i0 = share_i[w * 32 + threadIdx.x];
+                    }
+                best_v[r] = v0;
+                best_i[r] = i0;
+            }
+        }
+        if (warp < 4) asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        consumer_sync();
     }
-    trf.end(kTrLogitsFold);
+    logits_fold(p, position, best_v, best_i);
 }
 
 // ------------------------------------------------ fused out-projection
@@ -1996,6 +2159,82 @@ __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int he
     return true;
 }
 
+// One warp's 16-key group n0 of a cross unit (rows: the unit's keys in
+// the rotated layout, n of them) against q (qa: q's hi + lo halves as rows 0
+// and 1 of A): scores as m16n8k16 products with the keys as B, loaded by
+// ldmatrix.  Lanes 0..7 end with the scores of keys n0 + 2t, n0 + 2t + 1,
+// n0 + 8 + 2t, n0 + 9 + 2t (t = lane % 4) in v[0..3]; -inf past n, off
+// those lanes, or for a group at or past n.
+template <typename WT>
+__device__ __forceinline__ void cross_group_scores(const WT* rows, int n, int n0, const uint32_t (&qa)[4][2],
+                                                   float (&v)[4]) {
+    const int lane = threadIdx.x & 31, t4 = lane & 3, mi = lane >> 3, rr = lane & 7;
+    const bool row0 = lane < 4, pair = lane < 8;
+    if (n0 >= n) {
+        v[0] = v[1] = v[2] = v[3] = -INFINITY;
+        return;
+    }
+    // Even and odd key pieces accumulate apart: four chains of two products.
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+    float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+        // Keys n0 + 8*(mi/2) + rr, key pieces 2kk + mi%2 (rows past the
+        // unit's keys read its last key; their scores are dropped).
+        const int key = min(n0 + 8 * (mi >> 1) + rr, n - 1);
+        uint32_t b[4][4];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+            ldmatrix_x4(b[kk], rows + (size_t)key * 128 + cross_piece(2 * kk + (mi & 1), key) * 8);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t a[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
+            const uint32_t b0[2] = {b[kk][0], b[kk][1]}, b1[2] = {b[kk][2], b[kk][3]};
+            mma_16816<WT>(kk & 1 ? t0 : s0, a, b0);
+            mma_16816<WT>(kk & 1 ? t1 : s1, a, b1);
+        }
+    }
+    // Rows 0 (hi, lanes 0..3) and 1 (lo, lanes 4..7): keys n0+2t, n0+2t+1
+    // (s0) and n0+8+2t, n0+9+2t (s1).  Their sum reaches lanes 0..7 alike.
+    float sc[4] = {s0[0] + t0[0], s0[1] + t0[1], s1[0] + t1[0], s1[1] + t1[1]};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float other = __shfl_xor_sync(0xffffffffu, sc[i], 4);
+        sc[i] = row0 ? sc[i] + other : other + sc[i];
+    }
+    const int ka = n0 + 2 * t4;
+    v[0] = pair && ka < n ? sc[0] : -INFINITY;
+    v[1] = pair && ka + 1 < n ? sc[1] : -INFINITY;
+    v[2] = pair && ka + 8 < n ? sc[2] : -INFINITY;
+    v[3] = pair && ka + 9 < n ? sc[3] : -INFINITY;
+}
+
+// o += P . V for the group's weights e (as cross_group_scores lays them
+// out): P's hi half as row 0 of A, its lo half as row 1, the values as B by
+// ldmatrix.trans.  Lanes 0..3 (row 0) and 4..7 (row 1) hold channels
+// 8i + 2t, 8i + 2t + 1 in o[i]; the two rows add once per item.
+template <typename WT>
+__device__ __forceinline__ void cross_group_values(const WT* rows, int n, int n0, const float (&e)[4],
+                                                   float (&o)[8][4]) {
+    const int lane = threadIdx.x & 31, mi = lane >> 3, rr = lane & 7;
+    const bool row0 = lane < 4, pair = lane < 8;
+    uint32_t ph0, pl0, ph2, pl2;
+    split_pair<WT>(e[0], e[1], ph0, pl0);
+    split_pair<WT>(e[2], e[3], ph2, pl2);
+    const uint32_t a[4] = {pair ? (row0 ? ph0 : pl0) : 0u, 0u, pair ? (row0 ? ph2 : pl2) : 0u, 0u};
+    // Keys n0 + 8*(mi%2) + rr, value pieces 8 + 2cc + mi/2.
+    const int key = min(n0 + 8 * (mi & 1) + rr, n - 1);
+    uint32_t b[4][4];
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc)
+        ldmatrix_x4_trans(b[cc], rows + (size_t)key * 128 + cross_piece(8 + 2 * cc + (mi >> 1), key) * 8);
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+        const uint32_t b0[2] = {b[cc][0], b[cc][1]}, b1[2] = {b[cc][2], b[cc][3]};
+        mma_16816<WT>(o[2 * cc], a, b0);
+        mma_16816<WT>(o[2 * cc + 1], a, b1);
+    }
+}
+
 // 64-wide heads on the tensor cores.  A warp takes the unit's 16-key groups
 // 16*warp, 16*(warp + kWarps), ...:
 //   scores  m16n8k16 with q as row 0 of A (split hi + lo, so the product
@@ -2007,6 +2246,12 @@ __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int he
 // channels 8i+2t, 8i+2t+1 of the output.  Each warp keeps its own online
 // softmax over the item; the warps join once per item.
 // Shared memory: [q: 64][warp max: 8][warp sum: 8][warp rows: kWarps x 64]
+// [the queries of the CTA's first kCrossQueryBatch items: 64 each]
+constexpr int kCrossQueryBatch = 32;
+// Stages of the weight-stream ring from which the cross attention takes its
+// units two at a time (it holds two while the rest land).
+constexpr int kCrossPairStages = 3;
+
 template <typename WT>
 __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -2015,22 +2260,38 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
     const int H = p.heads, S = op.splits;
     const int units = cross_units(op);
     const int items = p.rows * H * S;
-    float* q = reinterpret_cast<float*>(work);
-    float* wmax = q + 64;
+    float* const q_home = reinterpret_cast<float*>(work);
+    float* q = q_home;
+    float* wmax = q_home + 64;
     float* wsum = wmax + 8;
     float* wrows = wsum + 8;
+    float* qbatch = wrows + kWarps * 64;
     __shared__ int is_last;
     __shared__ __align__(16) WT attended[128];  // a fused out-projection's input (hi, lo)
-    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    // The queries the previous op wrote, for the CTA's first items at once:
+    // one round trip for the op rather than one an item.
+    if (!op.gamma) {
+        const int mine = min(kCrossQueryBatch, (items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x);
+        for (int i = threadIdx.x; i < mine * 64; i += kThreads) {
+            const int item = blockIdx.x + (i >> 6) * gridDim.x;
+            const int head = (item / S) % H, r = item / (S * H);
+            qbatch[i] = ld_cg(p.q + (size_t)r * p.width + head * 64 + (i & 63)) * p.scale;
+        }
+    }
+    int nth = 0;  // this item's place among the CTA's items
+    for (int item = blockIdx.x; item < items; item += gridDim.x, ++nth) {
         const int split = item % S, head = (item / S) % H, r = item / (S * H);
         const int count = cross_item_units(op, item, units);
         consumer_sync();
+        q = q_home;
         if (op.gamma) {
             // The item's own query; item (r, head 0, split 0) keeps row r's residual sums.
             Trace trq = trace_of(p.profile);
             trq.begin();
             if (!cross_query<WT>(p, op, r, head, head == 0 && split == 0, s, work + kCrossQueryOffset, q)) return;
             trq.end(kTrQuery);
+        } else if (nth < kCrossQueryBatch) {
+            q = qbatch + 64 * nth;
         } else if (threadIdx.x < 64) {
             q[threadIdx.x] = ld_cg(p.q + (size_t)r * p.width + head * 64 + threadIdx.x) * p.scale;
         }
@@ -2054,60 +2315,40 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
         float o[8][4];
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-        // Matrix mi = lane / 8 of an x4 load, row rr = lane % 8 of it.
-        const int mi = lane >> 3, rr = lane & 7;
-        for (int t = 0; t < count; ++t) {
-            const WT* rows = reinterpret_cast<const WT*>(acquire_unit(p, s));
+        // Two units at a time (with three stages or more, so one more lands
+        // meanwhile): each warp takes its 16-key group(s) in both, the scores
+        // of both before one softmax update, then both groups' values --
+        // twice the independent work between the dependent steps of one
+        // group (its shuffles, its exponentials).  Measured on medium.en at
+        // 64 windows: 96 us a layer against 118 one unit at a time.
+        const int per = s.stages >= kCrossPairStages ? 2 : 1;
+        for (int t = 0; t < count; t += per) {
+            const bool two = per == 2 && t + 1 < count;
+            const WT* ra = reinterpret_cast<const WT*>(unit_at(p, s, s.next));
+            const WT* rb = two ? reinterpret_cast<const WT*>(unit_at(p, s, s.next + 1)) : ra;
             const int k0 = (split * op.span + t) * op.chunk;
-            const int n = min(op.chunk, op.key_count - k0);
+            const int na = min(op.chunk, op.key_count - k0);
+            const int nb = two ? min(op.chunk, op.key_count - k0 - op.chunk) : 0;
             Trace tr = trace_of(p.profile);
             tr.begin();
-            for (int n0 = 16 * warp; n0 < n; n0 += 16 * kWarps) {
-                // Even and odd key pieces accumulate apart: four chains of two
-                // products, summed after.
-                float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-                float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
-                {
-                    // Keys n0 + 8*(mi/2) + rr, key pieces 2kk + mi%2 (rows past
-                    // the unit's keys read its last key; their scores are dropped).
-                    const int key = min(n0 + 8 * (mi >> 1) + rr, n - 1);
-                    uint32_t b[4][4];
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        ldmatrix_x4(b[kk], rows + (size_t)key * 128 + cross_piece(2 * kk + (mi & 1), key) * 8);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint32_t a[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
-                        const uint32_t b0[2] = {b[kk][0], b[kk][1]}, b1[2] = {b[kk][2], b[kk][3]};
-                        mma_16816<WT>(kk & 1 ? t0 : s0, a, b0);
-                        mma_16816<WT>(kk & 1 ? t1 : s1, a, b1);
-                    }
-                }
-                // Rows 0 (hi, lanes 0..3) and 1 (lo, lanes 4..7): keys n0+2t,
-                // n0+2t+1 (s0) and n0+8+2t, n0+9+2t (s1).  Their sum reaches
-                // lanes 0..7 alike.
-                float sc[4] = {s0[0] + t0[0], s0[1] + t0[1], s1[0] + t1[0], s1[1] + t1[1]};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float other = __shfl_xor_sync(0xffffffffu, sc[i], 4);
-                    sc[i] = row0 ? sc[i] + other : other + sc[i];
-                }
-                const int ka = n0 + 2 * t4;
-                float v[4];
-                v[0] = pair && ka < n ? sc[0] : -INFINITY;
-                v[1] = pair && ka + 1 < n ? sc[1] : -INFINITY;
-                v[2] = pair && ka + 8 < n ? sc[2] : -INFINITY;
-                v[3] = pair && ka + 9 < n ? sc[3] : -INFINITY;
-                float gm = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+            for (int n0 = 16 * warp; n0 < max(na, nb); n0 += 16 * kWarps) {
+                float va[4], vb[4];
+                cross_group_scores<WT>(ra, na, n0, qa, va);
+                cross_group_scores<WT>(rb, nb, n0, qa, vb);
+                float gm = fmaxf(fmaxf(fmaxf(va[0], va[1]), fmaxf(va[2], va[3])),
+                                 fmaxf(fmaxf(vb[0], vb[1]), fmaxf(vb[2], vb[3])));
                 gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 1));
                 gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, 2));
                 gm = __shfl_sync(0xffffffffu, gm, 0);
                 const float m_new = fmaxf(m_w, gm);
                 const float keep = m_w == -INFINITY ? 0.f : __expf(m_w - m_new);
-                float e[4];
+                float ea[4], eb[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) e[i] = v[i] == -INFINITY ? 0.f : __expf(v[i] - m_new);
-                float ls = (e[0] + e[1]) + (e[2] + e[3]);
+                for (int i = 0; i < 4; ++i) {
+                    ea[i] = va[i] == -INFINITY ? 0.f : __expf(va[i] - m_new);
+                    eb[i] = vb[i] == -INFINITY ? 0.f : __expf(vb[i] - m_new);
+                }
+                float ls = ((ea[0] + ea[1]) + (ea[2] + ea[3])) + ((eb[0] + eb[1]) + (eb[2] + eb[3]));
                 ls += __shfl_xor_sync(0xffffffffu, ls, 1);
                 ls += __shfl_xor_sync(0xffffffffu, ls, 2);
                 ls = __shfl_sync(0xffffffffu, ls, 0);
@@ -2118,29 +2359,13 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
                     o[i][0] *= keep;
                     o[i][1] *= keep;
                 }
-                // P likewise: its hi half as row 0, its lo half as row 1; the
-                // two output rows add once per item.
-                uint32_t ph0, pl0, ph2, pl2;
-                split_pair<WT>(e[0], e[1], ph0, pl0);
-                split_pair<WT>(e[2], e[3], ph2, pl2);
-                const uint32_t a[4] = {pair ? (row0 ? ph0 : pl0) : 0u, 0u, pair ? (row0 ? ph2 : pl2) : 0u, 0u};
-                {
-                    // Keys n0 + 8*(mi%2) + rr, value pieces 8 + 2cc + mi/2.
-                    const int key = min(n0 + 8 * (mi & 1) + rr, n - 1);
-                    uint32_t b[4][4];
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc)
-                        ldmatrix_x4_trans(b[cc], rows + (size_t)key * 128 + cross_piece(8 + 2 * cc + (mi >> 1), key) * 8);
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {
-                        const uint32_t b0[2] = {b[cc][0], b[cc][1]}, b1[2] = {b[cc][2], b[cc][3]};
-                        mma_16816<WT>(o[2 * cc], a, b0);
-                        mma_16816<WT>(o[2 * cc + 1], a, b1);
-                    }
-                }
+                if (n0 < na) cross_group_values<WT>(ra, na, n0, ea, o);
+                if (n0 < nb) cross_group_values<WT>(rb, nb, n0, eb, o);
             }
             tr.end(kTrAttention);
-            release_unit(s);
+            release_at(s, s.next);
+            if (two) release_at(s, s.next + 1);
+            s.next += two ? 2 : 1;
         }
         // Rows 0 and 1 of the output (P's hi and lo halves) add; then the
         // warps' softmaxes join.
@@ -2353,7 +2578,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
             case kOpLogits: {
                 Trace trl = trace_of(p.profile);
                 trl.begin();
-                op_logits<WT, NT>(p, op, position, s, work);
+                if constexpr (UMMA)
+                    logits_umma<WT>(p, op, position, s, tm);
+                else
+                    op_logits<WT, NT>(p, op, position, s, work);
                 trl.end(kTrLogits);
                 break;
             }
@@ -2389,11 +2617,21 @@ size_t work_bytes(const StepParams& p, int max_chunk) {
     const size_t attention =
         sizeof(float) * std::max<size_t>({(size_t)kAttentionFixed + std::max(max_chunk, p.max_positions),
                                           (size_t)(64 + 32 + 2 * kWarps * 64 + kMaxCrossUnitKeys),
+                                          (size_t)(64 + 16 + kWarps * 64 + kCrossQueryBatch * 64),
                                           (size_t)kWarps * kSelfWarpKeys});
-    // A fused cross query's tile sits past the cross attention's own area.
-    size_t work = std::max(product + kCrossQueryOffset, attention);
-    // The activation ring of the tensor-core products (1024-byte aligned).
-    if (p.umma) work = std::max(work, (size_t)1024 + (size_t)p.umma_x_stages * p.umma_x_stage_bytes);
+    size_t work;
+    if (p.umma) {
+        // Tensor-core products and logits: the activation ring (1024-byte
+        // aligned), the logits' per-row best and tile scratch past it; a
+        // norm op's row (both planes).
+        const size_t ring = (size_t)1024 + std::max((size_t)p.umma_x_stages * p.umma_x_stage_bytes,
+                                                    (size_t)kLogitsScratchBytes);
+        const size_t logits = ring + (size_t)8 * p.out_rows;
+        work = std::max({attention, logits, (size_t)4 * p.kpd * sizeof(WT)});
+    } else {
+        // A fused cross query's tile sits past the cross attention's own area.
+        work = std::max(product + kCrossQueryOffset, attention);
+    }
     return (work + 127) / 128 * 128;
 }
 
