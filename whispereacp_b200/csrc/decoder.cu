@@ -1216,7 +1216,9 @@ private:
         // A tensor-core item's rows: as many as a weight stage holds (128
         // bytes a row), at most 128, a multiple of 16; the activation ring
         // holds three k-blocks of that many rows, each its hi plane then its
-        // lo plane (two products into one accumulator).
+        // lo plane (two products into one accumulator).  (Two stages of 128
+        // rows, leaving a fourth weight stage, measured 14 % slower in the
+        // large-v3 cross attention at 128 windows.)
         p.stage_bytes = stage_bytes_for_width();
         p.umma_rows = std::min(128, p.stage_bytes / 128 / 16 * 16);
         if (umma_) {
