@@ -233,11 +233,28 @@ __device__ bool grid_barrier(const StepParams& p, unsigned& epoch) {
 // warp by warp, so no CTA-wide sync is spent per unit, and the next op's
 // first units land while this op and the grid barrier run.
 
+// Ring positions: unit u sits in stage u % stages, round u / stages.  The
+// division is by a launch constant (2 or more stages), so it is a
+// multiply-high by its reciprocal, ceil(2^32 / stages): exact for u < 2^32 /
+// stages (a launch streams a few million units at most), where a 64-bit % or
+// / by a runtime value would be a software routine of a hundred-odd
+// instructions on every wait and release.
+struct RingDivisor {
+    uint32_t count, magic;
+    __device__ __forceinline__ void set(int n) {
+        count = (uint32_t)n;
+        magic = (uint32_t)(0xFFFFFFFFull / (unsigned long long)n) + 1u;
+    }
+    __device__ __forceinline__ uint32_t round(unsigned long long u) const { return __umulhi((uint32_t)u, magic); }
+    __device__ __forceinline__ uint32_t slot(unsigned long long u) const { return (uint32_t)u - round(u) * count; }
+};
+
 struct Stream {
     unsigned char* ring;          // stages x stage_bytes
     uint64_t* full;               // per stage: the unit landed (tx bytes)
     uint64_t* empty;              // per stage: the 8 consumer warps released it
     int stages;
+    RingDivisor div;              // stage and round of a unit index
     int stage_bytes;
     unsigned long long next;      // the next unit this CTA's consumers reach
     volatile unsigned long long* armed;  // units the producer has armed full[] for
@@ -284,8 +301,8 @@ __device__ bool wait_parity(const StepParams& p, uint64_t* bar, uint32_t parity,
 __device__ __forceinline__ const unsigned char* unit_at(const StepParams& p, const Stream& s, unsigned long long index) {
     Trace tr = trace_of(p.profile);
     tr.begin();
-    const int stage = (int)(index % s.stages);
-    wait_parity(p, s.full + stage, (uint32_t)((index / s.stages) & 1), nullptr, kWaitUnit, index);
+    const int stage = (int)s.div.slot(index);
+    wait_parity(p, s.full + stage, s.div.round(index) & 1u, nullptr, kWaitUnit, index);
     tr.end(kTrWait);
     return s.ring + (size_t)stage * s.stage_bytes;
 }
@@ -318,7 +335,7 @@ __device__ __forceinline__ const unsigned char* owned_unit_at(const StepParams& 
 __device__ __forceinline__ void release_at(const Stream& s, unsigned long long index, unsigned count = 1) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0)
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_address(s.empty + index % s.stages)),
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_address(s.empty + s.div.slot(index))),
                      "r"(count)
                      : "memory");
 }
@@ -361,9 +378,9 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
                 prefetch_l2(reinterpret_cast<const void*>(e.x), (unsigned)e.y);
                 continue;
             }
-            const int stage = (int)(u % s.stages);
+            const int stage = (int)s.div.slot(u);
             if (u >= (unsigned long long)s.stages &&
-                !wait_parity(p, s.empty + stage, (uint32_t)((u / s.stages - 1) & 1), stop, kWaitEmpty, u)) {
+                !wait_parity(p, s.empty + stage, (s.div.round(u) - 1u) & 1u, stop, kWaitEmpty, u)) {
                 go = false;
                 break;
             }
@@ -382,7 +399,7 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
     }
     const unsigned long long stages = (unsigned long long)s.stages;
     for (unsigned long long v = u > stages ? u - stages : 0; v < u; ++v)
-        if (!wait_parity(p, s.full + v % stages, (uint32_t)((v / stages) & 1), nullptr, kWaitDrain, v)) break;
+        if (!wait_parity(p, s.full + s.div.slot(v), s.div.round(v) & 1u, nullptr, kWaitDrain, v)) break;
 }
 
 // -------------------------------------------------------------------- embed
@@ -939,6 +956,7 @@ struct TensorMemory {
     uint64_t* x_empty;       // [x_stages] the products that read it completed
     int x_stages, x_stage_bytes;
     unsigned long long x_next;
+    RingDivisor x_div;       // stage and round of an activation block
 };
 constexpr uint32_t kTmemColumns = 256;
 constexpr int kLoadWarp = 5;      // lane 0 fetches the activation blocks
@@ -947,7 +965,7 @@ constexpr int kIssueWarp = 4;  // not one of the epilogue warps 0..3
 constexpr int kJoinBatch = 8;  // split partials a thread loads before summing
 
 __device__ __forceinline__ void stage_arrive(const Stream& s, unsigned long long index, unsigned count) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_address(s.empty + index % s.stages)),
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_address(s.empty + s.div.slot(index))),
                  "r"(count)
                  : "memory");
 }
@@ -979,9 +997,9 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
             const unsigned bytes = (unsigned)n16 * 128u;
             for (int j = 0; j < nkb; ++j) {
                 const unsigned long long q = x0 + j;
-                const int st = (int)(q % tm.x_stages);
+                const int st = (int)tm.x_div.slot(q);
                 if (q >= (unsigned long long)tm.x_stages &&
-                    !wait_parity(p, tm.x_empty + st, (uint32_t)((q / tm.x_stages - 1) & 1), nullptr, kWaitEmpty, q))
+                    !wait_parity(p, tm.x_empty + st, (tm.x_div.round(q) - 1u) & 1u, nullptr, kWaitEmpty, q))
                     break;
                 const uint32_t bar = smem_address(tm.x_full + st);
                 const uint32_t dst = smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes);
@@ -1007,8 +1025,8 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
                 const uint32_t w = smem_address(unit_at(p, s, iw));
                 for (int j = j0; j < nkb && j < j0 + p.umma_blocks; ++j) {
                     const unsigned long long q = x0 + j;
-                    const int st = (int)(q % tm.x_stages);
-                    wait_parity(p, tm.x_full + st, (uint32_t)((q / tm.x_stages) & 1), nullptr, kWaitUnit, q);
+                    const int st = (int)tm.x_div.slot(q);
+                    wait_parity(p, tm.x_full + st, tm.x_div.round(q) & 1u, nullptr, kWaitUnit, q);
                     const uint32_t x = smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes);
                     const uint32_t x_lo = x + (uint32_t)n16 * 128u;
                     const uint32_t wb = w + (uint32_t)(j - j0) * 16384u;
@@ -1022,7 +1040,7 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
                 // The weight stage is free after kWarps arrivals: kWarps - 1
                 // now, the last once the products above have read it.
                 stage_arrive(s, iw, kWarps - 1);
-                umma_commit(s.empty + iw % s.stages);
+                umma_commit(s.empty + s.div.slot(iw));
             }
             umma_commit(tm.done);
         }
@@ -1379,9 +1397,9 @@ __device__ void logits_umma(const StepParams& p, const StepOp& op, int position,
             const unsigned bytes = (unsigned)n16 * 128u;
             for (int j = 0; j < kblocks; ++j) {
                 const unsigned long long q = x0 + j;
-                const int st = (int)(q % tm.x_stages);
+                const int st = (int)tm.x_div.slot(q);
                 if (q >= (unsigned long long)tm.x_stages &&
-                    !wait_parity(p, tm.x_empty + st, (uint32_t)((q / tm.x_stages - 1) & 1), nullptr, kWaitEmpty, q))
+                    !wait_parity(p, tm.x_empty + st, (tm.x_div.round(q) - 1u) & 1u, nullptr, kWaitEmpty, q))
                     break;
                 const uint32_t bar = smem_address(tm.x_full + st);
                 const uint32_t dst = smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes);
@@ -1407,8 +1425,8 @@ __device__ void logits_umma(const StepParams& p, const StepOp& op, int position,
                 const uint32_t w = smem_address(unit_at(p, s, iw));
                 for (int j = j0; j < kblocks && j < j0 + p.umma_blocks; ++j) {
                     const unsigned long long q = x0 + j;
-                    const int st = (int)(q % tm.x_stages);
-                    wait_parity(p, tm.x_full + st, (uint32_t)((q / tm.x_stages) & 1), nullptr, kWaitUnit, q);
+                    const int st = (int)tm.x_div.slot(q);
+                    wait_parity(p, tm.x_full + st, tm.x_div.round(q) & 1u, nullptr, kWaitUnit, q);
                     const uint32_t x = smem_address(tm.x_ring + (size_t)st * tm.x_stage_bytes);
                     const uint32_t x_lo = x + (uint32_t)n16 * 128u;
                     const uint32_t wb = w + (uint32_t)(j - j0) * 16384u;
@@ -1420,7 +1438,7 @@ __device__ void logits_umma(const StepParams& p, const StepOp& op, int position,
                     umma_commit(tm.x_empty + st);
                 }
                 stage_arrive(s, iw, kWarps - 1);
-                umma_commit(s.empty + iw % s.stages);
+                umma_commit(s.empty + s.div.slot(iw));
             }
             umma_commit(tm.done);
         }
@@ -2508,6 +2526,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
                                : dynamic_smem;
     Stream s;
     s.stages = p.stages;
+    s.div.set(p.stages);
     s.stage_bytes = p.stage_bytes;
     s.ring = smem;
     s.full = reinterpret_cast<uint64_t*>(smem + (size_t)s.stages * s.stage_bytes);
@@ -2543,7 +2562,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
     TensorMemory tm{UMMA ? tmem_slot : 0u, &tmem_done, 0u,
                     reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(work) + 1023) &
                                                      ~static_cast<uintptr_t>(1023)),
-                    x_full, x_empty, p.umma_x_stages, p.umma_x_stage_bytes, 0ull};
+                    x_full, x_empty, p.umma_x_stages, p.umma_x_stage_bytes, 0ull, RingDivisor{}};
+    tm.x_div.set(p.umma_x_stages >= 2 ? p.umma_x_stages : 2);  // (unused without the tcgen05 products)
     volatile int* stop = &stop_flag;
     if (threadIdx.x >= kConsumers) {
         if (threadIdx.x == kConsumers) produce(p, s, stop);
