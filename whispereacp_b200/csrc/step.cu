@@ -2278,6 +2278,9 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
     const int H = p.heads, S = op.splits;
     const int units = cross_units(op);
     const int items = p.rows * H * S;
+    // The op's fields in registers: the op list is in global memory, and the
+    // ring's waits (asm with memory clobbers) would have them re-read.
+    const int span = op.span, chunk = op.chunk, key_count = op.key_count;
     float* const q_home = reinterpret_cast<float*>(work);
     float* q = q_home;
     float* wmax = q_home + 64;
@@ -2345,9 +2348,9 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
             const bool two = per == 2 && t + 1 < count;
             const WT* ra = reinterpret_cast<const WT*>(unit_at(p, s, s.next));
             const WT* rb = two ? reinterpret_cast<const WT*>(unit_at(p, s, s.next + 1)) : ra;
-            const int k0 = (split * op.span + t) * op.chunk;
-            const int na = min(op.chunk, op.key_count - k0);
-            const int nb = two ? min(op.chunk, op.key_count - k0 - op.chunk) : 0;
+            const int k0 = (split * span + t) * chunk;
+            const int na = min(chunk, key_count - k0);
+            const int nb = two ? min(chunk, key_count - k0 - chunk) : 0;
             Trace tr = trace_of(p.profile);
             tr.begin();
             for (int n0 = 16 * warp; n0 < max(na, nb); n0 += 16 * kWarps) {
