@@ -1252,6 +1252,10 @@ private:
         // the prompt step to the steps after it.
         CUDA_CHECK(cudaMemsetAsync(state_.get<int>() + kAbort, 0, 2 * sizeof(int), stream_));
         CUDA_CHECK(cudaMemsetAsync(barrier_.get(), 0, barrier_.bytes(), stream_));
+        // The cross attention's (row, head) counters: a launch whose splits
+        // join together counts them up from zero.
+        CUDA_CHECK(cudaMemsetAsync(counters_.get(), 0,
+                                   (size_t)windows_ * token_capacity_ * shape_.heads * sizeof(unsigned), stream_));
         try {
             launch_decode(half, p, kMaxCrossChunk, grid, stream_);
         } catch (const std::runtime_error& e) {

@@ -198,10 +198,26 @@ __device__ __forceinline__ void record_timeout(const StepParams& p, int kind, lo
     if (atomicExch(p.state + kAbort, 1) == 0) atomicAdd(p.barrier, kAbortBias);
 }
 
-__device__ bool grid_barrier(const StepParams& p, unsigned& epoch) {
+// The op list is read-only for the whole launch, and a grid barrier's
+// acquire leaves nothing of it in L1: read from global memory after the
+// barrier, an op's fields would cost a round trip to L2 before its first
+// load of data could issue.  So while thread 0 waits at the barrier, threads
+// 1.. copy the next op into a shared-memory slot with non-coherent loads,
+// and the op after the barrier reads its fields from there.
+constexpr int kOpWords = (int)(sizeof(StepOp) / sizeof(unsigned long long));
+static_assert(sizeof(StepOp) % sizeof(unsigned long long) == 0, "StepOp copies as 8-byte words");
+static_assert(kOpWords < kConsumers, "a consumer thread a word of the op");
+__device__ __forceinline__ void copy_op(const StepOp* from, StepOp* to, int word) {
+    if (word >= 0 && word < kOpWords)
+        reinterpret_cast<unsigned long long*>(to)[word] =
+            __ldg(reinterpret_cast<const unsigned long long*>(from) + word);
+}
+
+__device__ bool grid_barrier(const StepParams& p, unsigned& epoch, const StepOp* next, StepOp* next_slot) {
     __shared__ int aborted;
     consumer_sync();
     ++epoch;
+    if (threadIdx.x != 0) copy_op(next, next_slot, (int)threadIdx.x - 1);
     if (threadIdx.x == 0) {
         asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p.barrier), "r"(1u) : "memory");
         const unsigned target = epoch * gridDim.x;
@@ -369,9 +385,23 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
     const ulonglong2* schedule = reinterpret_cast<const ulonglong2*>(p.schedule) + first;
     unsigned long long u = 0;
     bool go = count > 0;
+    // The schedule is read kScheduleBatch entries at a time, all of their
+    // loads in flight together: one entry at a time, the walk would wait a
+    // round trip to L2 per entry (every grid barrier's acquire empties L1)
+    // and fall behind the consumers.
+    constexpr unsigned kScheduleBatch = 8;
+    ulonglong2 batch[kScheduleBatch];
     for (int step = 0; go && step < p.steps; ++step) {
         for (unsigned i = 0; i < count; ++i) {
-            const ulonglong2 e = __ldg(schedule + i);
+            if (i % kScheduleBatch == 0) {
+#pragma unroll
+                for (unsigned j = 0; j < kScheduleBatch; ++j)
+                    batch[j] = i + j < count ? __ldg(schedule + i + j) : make_ulonglong2(0ull, 0ull);
+            }
+            ulonglong2 e = batch[0];
+#pragma unroll
+            for (unsigned j = 1; j < kScheduleBatch; ++j)
+                if (i % kScheduleBatch == j) e = batch[j];
             if (e.y & kPrefetchOnly) {
                 // Not a unit: an L2 prefetch of data an op ahead reads straight
                 // from memory (its parameters, a fused out-projection's columns).
@@ -447,15 +477,18 @@ struct Addends {
 template <int N>
 __device__ __forceinline__ void add_addends(const Addends& a, size_t row, int d, int c0, int step, float (&v)[N]) {
     const float* rowp = a.base + row * d;
+    // Eight partial rows a batch for a few values a thread (every load of a
+    // base.en-sized op in flight at once); one for many (a row's own loads
+    // are then plenty in flight).  The bias and the first batch are loaded
+    // before the first addition, which waits for the caller's loads of v:
+    // one round trip to L2 for the row and its addends, not two.
+    constexpr int kBatch = N <= 8 ? 8 : 1;
+    float bias[N];
 #pragma unroll
     for (int i = 0; i < N; ++i) {
         const int c = c0 + i * step;
-        if (c < d) v[i] += __ldg(a.bias + c);
+        bias[i] = c < d ? __ldg(a.bias + c) : 0.f;
     }
-    // Eight partial rows a batch for a few values a thread (every load of a
-    // base.en-sized op in flight at once); one for many (a row's own loads
-    // are then plenty in flight).
-    constexpr int kBatch = N <= 8 ? 8 : 1;
     for (int j0 = 0; j0 < a.count; j0 += kBatch) {
         float t[kBatch][N];
 #pragma unroll
@@ -465,10 +498,20 @@ __device__ __forceinline__ void add_addends(const Addends& a, size_t row, int d,
                 const int c = c0 + i * step;
                 t[jj][i] = j0 + jj < a.count && c < d ? ld_cg(rowp + (size_t)(j0 + jj) * a.stride + c) : 0.f;
             }
+        if (j0 == 0) {
+#pragma unroll
+            for (int i = 0; i < N; ++i)
+                if (c0 + i * step < d) v[i] += bias[i];
+        }
 #pragma unroll
         for (int jj = 0; jj < kBatch; ++jj)
 #pragma unroll
             for (int i = 0; i < N; ++i) v[i] += t[jj][i];
+    }
+    if (a.count <= 0) {
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+            if (c0 + i * step < d) v[i] += bias[i];
     }
 }
 
@@ -962,7 +1005,7 @@ constexpr uint32_t kTmemColumns = 256;
 constexpr int kLoadWarp = 5;      // lane 0 fetches the activation blocks
 constexpr int kMaxXStages = 4;
 constexpr int kIssueWarp = 4;  // not one of the epilogue warps 0..3
-constexpr int kJoinBatch = 8;  // split partials a thread loads before summing
+constexpr int kJoinLoads = 16;  // split partials a thread loads before summing
 
 __device__ __forceinline__ void stage_arrive(const Stream& s, unsigned long long index, unsigned count) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_address(s.empty + s.div.slot(index))),
@@ -1046,10 +1089,14 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
         }
         s.next += (unsigned long long)((nkb + p.umma_blocks - 1) / p.umma_blocks);
         tm.x_next += (unsigned long long)nkb;
-        // Partials are [split][row][weight row]: a warp's lanes (consecutive
-        // weight rows) store one row's 128 contiguous bytes at a time.
-        const int ncols = m_tiles * 128;
-        float* partial = ks > 1 ? p.partial_d + (size_t)u.split * row_stride * ncols : nullptr;
+        // Partials are [split][weight tile][row][128 weight rows]: an item's
+        // block is contiguous, and a warp's lanes (consecutive weight rows)
+        // store one row's 128 bytes at a time.  (Rows of the whole width
+        // apart -- a power of two of bytes for every Whisper width -- the
+        // stores crowded a few L2 slices.)
+        const size_t split_stride = (size_t)m_tiles * row_stride * 128;
+        float* partial = ks > 1 ? p.partial_d + (size_t)u.split * split_stride + ((size_t)m * row_stride + r0) * 128
+                                : nullptr;
         if (warp < 4) {
             Trace tr = trace_of(p.profile);
             tr.begin();
@@ -1063,10 +1110,10 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
                 uint32_t v[32];
                 tmem_load32(tm.base + ((uint32_t)(32 * warp) << 16) + (uint32_t)c0, v);
                 if (partial) {
-                    float* col = partial + (size_t)(r0 + c0) * ncols + n;
+                    float* col = partial + (size_t)c0 * 128 + 32 * warp + lane;
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        if (c0 + j < rows) col[(size_t)j * ncols] = __uint_as_float(v[j]);
+                        if (c0 + j < rows) col[j * 128] = __uint_as_float(v[j]);
                 } else if (n < op.n) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
@@ -1103,25 +1150,33 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
             }
             consumer_sync();
             if (join_ok) {
-                // Four adjacent weight rows a thread, and up to kJoinBatch
-                // splits' loads in flight before any sum: a few L2 round trips
-                // per element rather than one per split.
+                // Four adjacent weight rows a thread.  Every split's partials
+                // of them and their biases are loaded before any sum (up to
+                // kJoinLoads splits at once: one round trip to L2 for 16
+                // splits or fewer) and summed in split order.
                 const int elems = rows * 128;
                 const int per = ((elems + ks - 1) / ks + 3) & ~3;
                 const int f1 = min((u.split + 1) * per, elems);
-                const size_t split_stride = (size_t)row_stride * ncols;
+                const float* tile = p.partial_d + ((size_t)m * row_stride + r0) * 128;
                 for (int f = u.split * per + 4 * threadIdx.x; f < f1; f += 4 * kThreads) {
                     const int t = f >> 7, nl = f & 127;
-                    const float* at = p.partial_d + (size_t)(r0 + t) * ncols + m * 128 + nl;
+                    float b[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int n = m * 128 + nl + e;
+                        b[e] = op.bias && n < op.n ? __ldg(op.bias + n) : 0.f;
+                    }
                     float sum[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int sp0 = 0; sp0 < ks; sp0 += kJoinBatch) {
-                        float4 v[kJoinBatch];
+                    for (int k0 = 0; k0 < ks; k0 += kJoinLoads) {
+                        float4 v[kJoinLoads];
 #pragma unroll
-                        for (int k = 0; k < kJoinBatch; ++k)
-                            if (sp0 + k < ks) v[k] = __ldcg(reinterpret_cast<const float4*>(at + (sp0 + k) * split_stride));
+                        for (int k = 0; k < kJoinLoads; ++k)
+                            v[k] = k0 + k < ks
+                                       ? __ldcg(reinterpret_cast<const float4*>(tile + (k0 + k) * split_stride + f))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                        for (int k = 0; k < kJoinBatch; ++k)
-                            if (sp0 + k < ks) {
+                        for (int k = 0; k < kJoinLoads; ++k)
+                            if (k0 + k < ks) {
                                 sum[0] += v[k].x;
                                 sum[1] += v[k].y;
                                 sum[2] += v[k].z;
@@ -1131,8 +1186,7 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const int n = m * 128 + nl + e;
-                        if (n < op.n)
-                            emit_output<WT>(p, op, position, n, r0 + t, sum[e] + (op.bias ? __ldg(op.bias + n) : 0.f));
+                        if (n < op.n) emit_output<WT>(p, op, position, n, r0 + t, sum[e] + b[e]);
                     }
                 }
             }
@@ -1511,15 +1565,19 @@ __device__ void logits_umma(const StepParams& p, const StepOp& op, int position,
 // after this one adds the heads' partials in head order, with the bias).
 // The head's columns are chunks 2 head and 2 head + 1 of every 16-row tile
 // of the fragment-packed weight, read straight from memory (which CTA joins
-// a (row, head) is known only at run time, so they are not on the stream):
-// each warp takes tiles warp, warp + 7, ..., six tiles' fragments in flight
-// at once, a as the one input row of swap-AB m16n8k16 products.
+// a (row, head) is known only at run time, so they are not on the stream).
+// The CTA takes the output tiles first, first + step, ... (all of them when
+// one CTA projects the head; a share when several do); its warps take those
+// in turn, six tiles' fragments in flight at once, a as the one input row of
+// swap-AB m16n8k16 products.
 template <typename WT>
-__device__ void head_out_projection(const StepParams& p, const StepOp& op, int r, int head, const WT* a) {
+__device__ void head_out_projection(const StepParams& p, const StepOp& op, int r, int head, const WT* a,
+                                    int first = 0, int step = 1) {
     Trace tr = trace_of(p.profile);
     tr.begin();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
-    const int d = p.width, chunks = p.kpd / 32, tiles = (d + 15) / 16;
+    const int d = p.width, chunks = p.kpd / 32;
+    const int tiles = ((d + 15) / 16 - first + step - 1) / step;  // this CTA's
     const uint4 zero = make_uint4(0, 0, 0, 0);
     const uint4 x0 = gq == 0 ? *reinterpret_cast<const uint4*>(a + 8 * tq) : zero;
     const uint4 x1 = gq == 0 ? *reinterpret_cast<const uint4*>(a + 32 + 8 * tq) : zero;
@@ -1532,8 +1590,8 @@ __device__ void head_out_projection(const StepParams& p, const StepOp& op, int r
         uint4 w[kBatch][4];
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
-            const int t = t0 + i * kWarps;
-            if (t < tiles) {
+            const int t = first + (t0 + i * kWarps) * step;
+            if (t0 + i * kWarps < tiles) {
                 const uint4* src =
                     reinterpret_cast<const uint4*>(wbase + (((size_t)t * chunks + 2 * head) * 32 + lane) * 32);
                 w[i][0] = ld_nc4(src);
@@ -1546,8 +1604,8 @@ __device__ void head_out_projection(const StepParams& p, const StepOp& op, int r
         }
 #pragma unroll
         for (int i = 0; i < kBatch; ++i) {
-            const int t = t0 + i * kWarps;
-            if (t >= tiles) break;
+            const int t = first + (t0 + i * kWarps) * step;
+            if (t0 + i * kWarps >= tiles) break;
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
             const uint32_t a0[4] = {w[i][0].x, w[i][1].x, w[i][0].y, w[i][1].y};
             const uint32_t a1[4] = {w[i][0].z, w[i][1].z, w[i][0].w, w[i][1].w};
@@ -1767,8 +1825,14 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
     float* result = fold + kFold;
     float* scores = result + 64;
     const int D = p.head_width;
-    for (int item = blockIdx.x; item < p.rows * p.heads; item += gridDim.x) {
-        const int r = item / p.heads, head = item % p.heads;
+    // A fused out-projection with CTAs to spare: `shares` CTAs a (row, head),
+    // each attending in full (the same sums in the same order) and projecting
+    // its share of the output tiles, so no CTA reads all of the head's
+    // columns of the out-projection.
+    const int pairs = p.rows * p.heads;
+    const int shares = op.out_weight && pairs < (int)gridDim.x ? min((int)gridDim.x / pairs, (p.width + 15) / 16) : 1;
+    for (int item = blockIdx.x; item < pairs * shares; item += gridDim.x) {
+        const int share = item / pairs, r = (item % pairs) / p.heads, head = item % p.heads;
         const int b = r / p.tokens, t = r % p.tokens;
         const int keys = position + t + 1;
         Trace trs = trace_of(p.profile);
@@ -1801,7 +1865,7 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
             __shared__ __align__(16) WT attended[128];
             for (int c = threadIdx.x; c < 64; c += kThreads) store_split(attended + c, 64, result[c] / l);
             consumer_sync();
-            head_out_projection<WT>(p, op, r, head, attended);
+            head_out_projection<WT>(p, op, r, head, attended, share, shares);
             continue;
         }
         WT* out = static_cast<WT*>(p.attn16);
@@ -2000,13 +2064,19 @@ __device__ __forceinline__ void cross_values(const WT* rows, int n, int D, const
 
 // The last split of a (row, head), one warp: joins the splits' partials
 // [max, sum, D values] with every load of a lane in flight at once.
+// `staged`: the partials already in shared memory (a cooperative join).
+__device__ __forceinline__ float join_load(const float* at, bool staged) {
+    return staged ? *at : ld_cg(at);
+}
 template <typename WT>
-__device__ void cross_join(const StepParams& p, const StepOp& op, int r, int head, WT* to_shared = nullptr) {
+__device__ void cross_join(const StepParams& p, const StepOp& op, int r, int head, WT* to_shared = nullptr,
+                           const float* staged = nullptr) {
     const int lane = threadIdx.x & 31;
     const int D = p.head_width, S = op.splits;
-    const float* part = p.partial + ((size_t)r * p.heads + head) * S * (D + 2);
-    const float m_own = lane < S ? ld_cg(part + (size_t)lane * (D + 2)) : -INFINITY;
-    const float l_own = lane < S ? ld_cg(part + (size_t)lane * (D + 2) + 1) : 0.f;
+    const bool sh = staged != nullptr;
+    const float* part = sh ? staged : p.partial + ((size_t)r * p.heads + head) * S * (D + 2);
+    const float m_own = lane < S ? join_load(part + (size_t)lane * (D + 2), sh) : -INFINITY;
+    const float l_own = lane < S ? join_load(part + (size_t)lane * (D + 2) + 1, sh) : 0.f;
     const float mx = warp_max(m_own);
     const float f_own = m_own == -INFINITY ? 0.f : __expf(m_own - mx);
     const float l = warp_sum(l_own * f_own);
@@ -2016,8 +2086,8 @@ __device__ void cross_join(const StepParams& p, const StepOp& op, int r, int hea
     for (int sp = 0; sp < S; ++sp) {
         const float f = __shfl_sync(0xffffffffu, f_own, sp);
         const float* ps = part + (size_t)sp * (D + 2) + 2;
-        if (c0 < D) o[0] += ld_cg(ps + c0) * f;
-        if (c1 < D) o[1] += ld_cg(ps + c1) * f;
+        if (c0 < D) o[0] += join_load(ps + c0, sh) * f;
+        if (c1 < D) o[1] += join_load(ps + c1, sh) * f;
     }
     const float a0 = o[0] / l + (op.value_bias && c0 < D ? __ldg(op.value_bias + head * D + c0) : 0.f);
     const float a1 = o[1] / l + (op.value_bias && c1 < D ? __ldg(op.value_bias + head * D + c1) : 0.f);
@@ -2137,8 +2207,9 @@ constexpr int kCrossQueryOffset = 2304;
 // self attention's out-projection partials (its residual, Decoder.cpp:80-91);
 // keep_sum: this CTA stores the sums as the new residual rows.  The head's
 // four 16-row weight tiles come off the weight stream ahead of the item's
-// keys, one tile to each of the first four warps.  Work area at `area`:
-// [xs: 2 planes x 8 x pitch 16-bit].
+// keys.  Work area at `area`: [xs: 2 planes x 8 x pitch 16-bit]; after the
+// query, the same area holds a cooperative join's partials (kMaxCrossSplits
+// x 66 floats).
 template <typename WT>
 __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int head, bool keep_sum, Stream& s,
                             unsigned char* area, float* q) {
@@ -2157,7 +2228,9 @@ __device__ bool cross_query(const StepParams& p, const StepOp& op, int r, int he
                         (size_t)8 * pitch, nullptr, add);
     consumer_sync();
     // Warp j < tiles owns q tile j (one unit: a stage holds a whole tile)
-    // over all of K, so no partial sums cross warps.
+    // over all of K, so no partial sums cross warps.  (Spreading the tiles'
+    // chunks over all seven warps, with a reduction after, measured slower:
+    // each warp then waits for every tile.)
     if (warp < tiles) {
         const unsigned long long index = s.next + warp;
         const unsigned char* unit = owned_unit_at(p, s, index);
@@ -2271,13 +2344,17 @@ constexpr int kCrossQueryBatch = 32;
 constexpr int kCrossPairStages = 3;
 
 template <typename WT>
-__device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
+__device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work,
+                                    unsigned use) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t4 = lane & 3;
     const bool row0 = lane < 4, pair = lane < 8;
     const int H = p.heads, S = op.splits;
     const int units = cross_units(op);
     const int items = p.rows * H * S;
+    // A fused out-projection with every item on a CTA of its own: the
+    // splits join together (below) instead of the last to finish alone.
+    const bool cooperative = op.out_weight != nullptr && S > 1 && items <= (int)gridDim.x;
     // The op's fields in registers: the op list is in global memory, and the
     // ring's waits (asm with memory clobbers) would have them re-read.
     const int span = op.span, chunk = op.chunk, key_count = op.key_count;
@@ -2440,6 +2517,59 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
             part[1] = L;
         }
         consumer_sync();
+        if (cooperative) {
+            // Every split of the (row, head) joins: the splits meet at the
+            // pair's counter (monotonic over the launch: `use` cross ops have
+            // passed it before this one), each joins the partials itself --
+            // the same sums in the same order as a single joiner -- and
+            // projects its share of the output tiles.  Each split is the one
+            // item of its CTA and every CTA is resident, so all of them
+            // arrive; the wait is bounded all the same.
+            if (threadIdx.x == 0) {
+                unsigned* counter = p.combine_counters + (size_t)r * H + head;
+                asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(counter), "r"(1u) : "memory");
+                const unsigned target = (unsigned)S * (use + 1u);
+                const unsigned long long start = global_ns();
+                int ok = 1;
+                for (unsigned spin = 1; ld_acquire(counter) < target; ++spin) {
+                    if ((spin & 15) != 0) continue;
+                    if (ld_volatile(p.state + kAbort)) { ok = 0; break; }
+                    if (global_ns() - start > kWaitTimeoutNs) {
+                        record_timeout(p, kWaitJoin, (long long)item);
+                        ok = 0;
+                        break;
+                    }
+                }
+                is_last = ok;
+            }
+            consumer_sync();
+            if (!is_last) return;
+            // Every split's partial into shared memory with all of them in
+            // flight at once (the query's tile is free by now): one round
+            // trip to L2, where a warp reading them in turn takes several.
+            {
+                constexpr int kPer = (kMaxCrossSplits * 66 + kThreads - 1) / kThreads;
+                float* staged = reinterpret_cast<float*>(work + kCrossQueryOffset);
+                const float* from = p.partial + ((size_t)r * H + head) * S * 66;
+                float v[kPer];
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) {
+                    const int i = threadIdx.x + k * kThreads;
+                    v[k] = i < S * 66 ? ld_cg(from + i) : 0.f;
+                }
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) {
+                    const int i = threadIdx.x + k * kThreads;
+                    if (i < S * 66) staged[i] = v[k];
+                }
+                consumer_sync();
+                if (warp == 0) cross_join<WT>(p, op, r, head, attended, staged);
+            }
+            consumer_sync();
+            trj.end(kTrJoin);
+            head_out_projection<WT>(p, op, r, head, attended, split, S);
+            continue;
+        }
         if (threadIdx.x == 0) {
             unsigned* counter = p.combine_counters + (size_t)r * H + head;
             is_last = arrive_acq_rel(counter) == (unsigned)(S - 1);
@@ -2460,8 +2590,9 @@ __device__ void cross_attention_mma(const StepParams& p, const StepOp& op, Strea
 }
 
 template <typename WT>
-__device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work) {
-    if (p.head_width == 64) cross_attention_mma<WT>(p, op, s, work);
+__device__ void op_cross_attention(const StepParams& p, const StepOp& op, Stream& s, unsigned char* work,
+                                   unsigned use) {
+    if (p.head_width == 64) cross_attention_mma<WT>(p, op, s, work, use);
     else cross_attention_cores<WT>(p, op, s, work);
 }
 
@@ -2574,12 +2705,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
     }
 
     unsigned epoch = 0;
+    __shared__ __align__(16) StepOp op_slot[2];
+    copy_op(p.ops, op_slot, (int)threadIdx.x);
+    consumer_sync();
+    int slot = 0;
+    unsigned cross_uses = 0;  // cross-attention ops run so far in this launch
     const bool stamp = p.profile != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
     for (int step = 0; step < p.steps; ++step) {
         const int position = ld_volatile(p.state + kPosition);
         if (stamp && step == 0) p.profile[0] = global_ns();
         for (int i = 0; i < p.n_ops; ++i) {
-            const StepOp& op = p.ops[i];
+            const StepOp& op = op_slot[slot];
             if (threadIdx.x == 0) prefetch_rows(p, op, position);
             Trace tro = trace_of(p.profile);
             tro.begin();
@@ -2598,7 +2734,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
                 else
                     op_self_attention<WT>(p, op, position, work);
                 break;
-            case kOpCrossAttention: op_cross_attention<WT>(p, op, s, work); break;
+            case kOpCrossAttention: op_cross_attention<WT>(p, op, s, work, cross_uses++); break;
             case kOpLogits: {
                 Trace trl = trace_of(p.profile);
                 trl.begin();
@@ -2614,7 +2750,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(StepParams p) 
             tro.end(kTrOther);
             Trace trb = trace_of(p.profile);
             trb.begin();
-            const bool passed = grid_barrier(p, epoch);
+            const bool passed = grid_barrier(p, epoch, p.ops + (i + 1 < p.n_ops ? i + 1 : 0), op_slot + (slot ^ 1));
+            slot ^= 1;
             trb.end(kTrBarrier);
             if (!passed) {
                 trace_flush(p);
@@ -2653,8 +2790,10 @@ size_t work_bytes(const StepParams& p, int max_chunk) {
         const size_t logits = ring + (size_t)8 * p.out_rows;
         work = std::max({attention, logits, (size_t)4 * p.kpd * sizeof(WT)});
     } else {
-        // A fused cross query's tile sits past the cross attention's own area.
-        work = std::max(product + kCrossQueryOffset, attention);
+        // A fused cross query's tile sits past the cross attention's own
+        // area, and a cooperative join's partials after it.
+        work = std::max({product + kCrossQueryOffset, attention,
+                         (size_t)kCrossQueryOffset + sizeof(float) * kMaxCrossSplits * 66});
     }
     return (work + 127) / 128 * 128;
 }
