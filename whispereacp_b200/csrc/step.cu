@@ -385,23 +385,9 @@ __device__ void produce(const StepParams& p, Stream& s, const volatile int* stop
     const ulonglong2* schedule = reinterpret_cast<const ulonglong2*>(p.schedule) + first;
     unsigned long long u = 0;
     bool go = count > 0;
-    // The schedule is read kScheduleBatch entries at a time, all of their
-    // loads in flight together: one entry at a time, the walk would wait a
-    // round trip to L2 per entry (every grid barrier's acquire empties L1)
-    // and fall behind the consumers.
-    constexpr unsigned kScheduleBatch = 8;
-    ulonglong2 batch[kScheduleBatch];
     for (int step = 0; go && step < p.steps; ++step) {
         for (unsigned i = 0; i < count; ++i) {
-            if (i % kScheduleBatch == 0) {
-#pragma unroll
-                for (unsigned j = 0; j < kScheduleBatch; ++j)
-                    batch[j] = i + j < count ? __ldg(schedule + i + j) : make_ulonglong2(0ull, 0ull);
-            }
-            ulonglong2 e = batch[0];
-#pragma unroll
-            for (unsigned j = 1; j < kScheduleBatch; ++j)
-                if (i % kScheduleBatch == j) e = batch[j];
+            const ulonglong2 e = __ldg(schedule + i);
             if (e.y & kPrefetchOnly) {
                 // Not a unit: an L2 prefetch of data an op ahead reads straight
                 // from memory (its parameters, a fused out-projection's columns).
