@@ -1081,6 +1081,34 @@ private:
         return partial_bytes;
     }
 
+    // Single-token steps of the tensor-core path: a split q/k/v product's
+    // join moves into the self attention after it (StepOp::defer_join), which
+    // sums its (row, head)'s partials in split order -- the same sums the
+    // join would make -- so the product ends at its partials, without a
+    // meeting of its splits.  Only where the self attention runs a warp per
+    // (row, head) over 64-wide heads, and with one token a row, so no item
+    // reads a key another item of the op writes.
+    void defer_qkv_joins(std::vector<StepOp>& ops, const StepParams& p, int grid) const {
+        if (!p.umma || p.tokens != 1 || p.head_width != 64 || p.max_positions > kSelfWarpKeys ||
+            (long long)p.rows * p.heads < grid)
+            return;
+        const int groups = (p.rows + p.umma_rows - 1) / p.umma_rows;
+        for (size_t i = 0; i + 1 < ops.size(); ++i) {
+            StepOp& qkv = ops[i];
+            StepOp& self = ops[i + 1];
+            if (qkv.kind != kOpProduct || qkv.epilogue != kEpQkv || qkv.ksplit <= 1 ||
+                self.kind != kOpSelfAttention || self.out_weight)
+                continue;
+            const int m_tiles = (qkv.n + 127) / 128, row_stride = groups * p.umma_rows;
+            qkv.defer_join = 1;
+            self.qkv_partial = p.partial_d;
+            self.qkv_split_stride = (long long)m_tiles * row_stride * 128;
+            self.qkv_row_stride = row_stride;
+            self.qkv_splits = qkv.ksplit;
+            self.qkv_bias = qkv.bias;
+        }
+    }
+
     // The weight-stream schedule of every CTA (schedule.h), into device memory.
     void upload_schedule(StepParams& p, const std::vector<StepOp>& ops, int grid) {
         build_schedule(p, ops, grid, decode_tile_rows(p), schedule_host_, offsets_host_);
@@ -1236,6 +1264,7 @@ private:
         const size_t partial_bytes = split_products(ops, p, grid);
         if (partial_d_.bytes() < partial_bytes) partial_d_.allocate(partial_bytes);
         p.partial_d = partial_d_.get<float>();
+        defer_qkv_joins(ops, p, grid);
         if (umma_) {
             const size_t counter_bytes = ops.size() * kSplitSlots * sizeof(unsigned);
             if (split_counters_.bytes() < counter_bytes) split_counters_.allocate(counter_bytes);

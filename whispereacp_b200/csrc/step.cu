@@ -1110,7 +1110,7 @@ __device__ void product_umma(const StepParams& p, const StepOp& op, int position
             tr.end(kTrEpilogue);
         }
         tm.phase ^= 1u;
-        if (ks > 1) {
+        if (ks > 1 && !op.defer_join) {
             // The tile's splits (each on its own CTA: a split product's items
             // fit one wave) meet here; then each joins a contiguous share of
             // the tile's (row, weight row) elements, summing the partials in
@@ -1867,7 +1867,7 @@ __device__ void op_self_attention(const StepParams& p, const StepOp& op, int pos
 // score row; values: four keys a pass, a 16-byte piece a lane, eight passes'
 // loads together, the four key slots joined at the end.  Keys and values
 // come through L2 (this launch's q/k/v op wrote the newest ones).
-constexpr int kSelfWarpKeys = 512;  // score row of a warp (>= max_positions)
+
 
 template <typename WT>
 __device__ void self_attention_warps(const StepParams& p, const StepOp& op, int position, unsigned char* work) {
@@ -1885,14 +1885,64 @@ __device__ void self_attention_warps(const StepParams& p, const StepOp& op, int 
         const int slot = lane >> 2, qd = lane & 3;
         float q[16];
         const float* qrow = p.q + (size_t)r * p.width + head * 64 + 16 * qd;
+        if (op.qkv_partial) {
+            // The q/k/v product's join for this (row, head): its 192 rows'
+            // partials (q, k, v: rows 192 head ..), three pairs a lane, every
+            // split's loads in flight before the sums, which run in split
+            // order and add the bias last, as the product's join would.  k and
+            // v go to the caches at the row's position; q to this warp's
+            // score row, which the scores overwrite later.
+            const int S = op.qkv_splits;
+            float2 sum[3] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            for (int k0 = 0; k0 < S; k0 += kDeferLoads) {
+                float2 v[kDeferLoads][3];
+#pragma unroll
+                for (int k = 0; k < kDeferLoads; ++k)
+#pragma unroll
+                    for (int j = 0; j < 3; ++j) {
+                        const int n = head * 192 + 2 * (lane + 32 * j);
+                        const float* at = op.qkv_partial + (size_t)(k0 + k) * op.qkv_split_stride +
+                                          ((size_t)(n >> 7) * op.qkv_row_stride + r) * 128 + (n & 127);
+                        v[k][j] = k0 + k < S ? __ldcg(reinterpret_cast<const float2*>(at)) : make_float2(0.f, 0.f);
+                    }
+#pragma unroll
+                for (int k = 0; k < kDeferLoads; ++k)
+                    if (k0 + k < S)
+#pragma unroll
+                        for (int j = 0; j < 3; ++j) {
+                            sum[j].x += v[k][j].x;
+                            sum[j].y += v[k][j].y;
+                        }
+            }
+#pragma unroll
+            for (int j = 0; j < 3; ++j) {
+                const int i = 2 * (lane + 32 * j), n = head * 192 + i;  // i: 0..191 within the head
+                const float2 bias = __ldg(reinterpret_cast<const float2*>(op.qkv_bias + n));
+                const float x = sum[j].x + bias.x, y = sum[j].y + bias.y;
+                if (i < 64) {
+                    sc[i] = x;
+                    sc[i + 1] = y;
+                } else {
+                    WT* cache = const_cast<WT*>(i < 128 ? K : V) + (size_t)(position + t) * op.key_stride + (i & 63);
+                    cache[0] = Half16<WT>::from_float(x);
+                    cache[1] = Half16<WT>::from_float(y);
+                }
+            }
+            __syncwarp();
+            qrow = sc + 16 * qd;
+        }
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(qrow + i));
+            const float4 v = op.qkv_partial ? *reinterpret_cast<const float4*>(qrow + i)
+                                            : __ldcg(reinterpret_cast<const float4*>(qrow + i));
             q[i] = v.x * p.scale;
             q[i + 1] = v.y * p.scale;
             q[i + 2] = v.z * p.scale;
             q[i + 3] = v.w * p.scale;
         }
+        // (The scores below overwrite the score row only after every lane
+        // has its q.)
+        __syncwarp();
         float mx = -INFINITY;
         for (int j0 = 0; j0 < keys; j0 += 32) {
             uint4 ka[4], kb[4];

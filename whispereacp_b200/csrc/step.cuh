@@ -41,6 +41,10 @@ constexpr int kStepWarps = 7;
 // (row, head).
 constexpr int kMaxCrossUnitKeys = 256;
 constexpr int kMaxCrossSplits = 32;
+// Keys of the score row of a self-attention warp (>= max_positions).
+constexpr int kSelfWarpKeys = 512;
+// Splits of a deferred q/k/v join a warp loads before summing.
+constexpr int kDeferLoads = 8;
 // Join counters per op of a split tensor-core product.
 constexpr int kSplitSlots = 128;
 // Most stages of a CTA's weight-stream ring (as many as shared memory holds).
@@ -157,6 +161,18 @@ struct StepOp {
     // tile's splits meet, and each sums its share of the rows in split order
     // and applies the epilogue.
     int ksplit;
+    // A split q/k/v product whose join is left to the self attention after
+    // it (single-token steps of the tensor-core path): the product stops at
+    // its partials; the self attention sums the partials of its (row, head)
+    // -- qkv_splits of them, qkv_split_stride floats apart, rows
+    // qkv_row_stride apart in a weight tile's block, in split order, then
+    // qkv_bias -- appends k and v to the caches and attends with q.
+    int defer_join;
+    const float* qkv_partial;
+    long long qkv_split_stride;
+    int qkv_row_stride;
+    int qkv_splits;
+    const float* qkv_bias;
 };
 
 struct StepParams {
