@@ -1,5 +1,6 @@
 """The C ABI library: it loads without a GPU and exports every entry point
-include/wsp_decoder.h declares, with no call that needs a device."""
+include/wsp_decoder.h and include/wsp_encoder.h declare, with no call that
+needs a device."""
 import ctypes
 import os
 import re
@@ -7,13 +8,15 @@ import re
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "wsp_decoder.h")
+HEADERS = [os.path.join(ROOT, "include", name) for name in ("wsp_decoder.h", "wsp_encoder.h")]
 
 
 def declared_functions():
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(wsp_[a-z_]+)\s*\(", text)))
+    names = set()
+    for header in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", open(header).read(), flags=re.S)
+        names |= set(re.findall(r"\b(wsp_[a-z_]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_header_declares_the_decoder_entry_points():
@@ -39,9 +42,18 @@ def test_abi_version_and_error_text_without_a_device():
     assert isinstance(lib.wsp_last_error(), bytes)
 
 
+def test_header_declares_the_encoder_entry_points():
+    names = declared_functions()
+    for required in ("wsp_encoder_create", "wsp_encoder_set_tensor", "wsp_encoder_set_filters",
+                     "wsp_encoder_log_mel", "wsp_encoder_encode", "wsp_encoder_encode_samples"):
+        assert required in names
+
+
 def test_null_arguments_are_refused_before_any_device_work():
     from whispereacp_b200._native import WSP_INVALID_ARGUMENT, library
     lib = library()
+    assert lib.wsp_encoder_create(None, 0, 1, None) == WSP_INVALID_ARGUMENT
+    assert lib.wsp_encoder_encode(None, None, None) == WSP_INVALID_ARGUMENT
     assert lib.wsp_decoder_create(None, 0, 1, 1, None) == WSP_INVALID_ARGUMENT
     assert b"NULL" in lib.wsp_last_error()
     assert lib.wsp_decoder_step(None, None, 1, None, None, None) == WSP_INVALID_ARGUMENT

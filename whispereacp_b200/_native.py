@@ -58,7 +58,13 @@ class CGeneration(ctypes.Structure):
                 ("stop_at_end_of_text", ctypes.c_int32)]
 
 
-# Every entry point include/wsp_decoder.h declares, with its ctypes signature.
+class CEncoderShape(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "mel_bins", "width", "heads", "layers", "feed_forward_width", "input_frames")]
+
+
+# Every entry point include/wsp_decoder.h and include/wsp_encoder.h declare,
+# with its ctypes signature.
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 SIGNATURES = {
@@ -90,6 +96,14 @@ SIGNATURES = {
     "wsp_decoder_phase_ms": ([_P, ctypes.POINTER(ctypes.c_float)], _I),
     "wsp_argmax": ([_P, _P, _P, _I, _I, _P], _I),
     "wsp_argmax_no_alloc": ([_P, _P, _P, _I, _I, _P], _I),
+    "wsp_encoder_create": ([ctypes.POINTER(CEncoderShape), _I, _I, ctypes.POINTER(_P)], _I),
+    "wsp_encoder_destroy": ([_P], None),
+    "wsp_encoder_set_tensor": ([_P, ctypes.c_char_p, _I, ctypes.POINTER(ctypes.c_int64), _I, _P], _I),
+    "wsp_encoder_set_filters": ([_P, _P], _I),
+    "wsp_encoder_check_weights": ([_P], _I),
+    "wsp_encoder_log_mel": ([_P, _P, _I, _P], _I),
+    "wsp_encoder_encode": ([_P, _P, _P], _I),
+    "wsp_encoder_encode_samples": ([_P, _P, _I, _P], _I),
 }
 
 _lib = None

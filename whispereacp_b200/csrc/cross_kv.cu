@@ -279,6 +279,32 @@ __device__ void store_tiles(const CrossKvArgs& a, uint64_t* acc_full, uint64_t* 
             tmem_load32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(acc * kAccColumns + c0), v);
             const int n0 = t.weight_tile * kCrossTileRows + c0;
             if (!row_ok || n0 >= a.columns) continue;
+            if (a.linear_out) {
+                // Row `row`'s 32 columns n0..: bias, GELU, residual, as
+                // float4s (columns is a multiple of 4).
+                float* out_row = a.linear_out + (size_t)row * a.columns;
+                const float* res_row = a.residual ? a.residual + (size_t)row * a.columns : nullptr;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const int n = n0 + j;
+                    if (n >= a.columns) break;
+                    float x[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        x[e] = __uint_as_float(v[j + e]) + (a.bias ? __ldg(a.bias + n + e) : 0.f);
+                        if (a.gelu) x[e] = gelu_exact(x[e]);
+                    }
+                    if (res_row) {
+                        const float4 r = *reinterpret_cast<const float4*>(res_row + n);
+                        x[0] += r.x;
+                        x[1] += r.y;
+                        x[2] += r.z;
+                        x[3] += r.w;
+                    }
+                    *reinterpret_cast<float4*>(out_row + n) = make_float4(x[0], x[1], x[2], x[3]);
+                }
+                continue;
+            }
             if (a.head_width == 64) {
                 const int group = n0 / 128, piece0 = (n0 % 128) / 8;
                 WT* block = out + (cache_block(a, t.window, group) * a.row_stride + row) * 128;
@@ -388,6 +414,17 @@ void launch_typed(const CrossKvArgs& a, int sm_count, cudaStream_t stream) {
 size_t cross_kv_shared_bytes() { return 1024 + (size_t)kStages * kStageBytes; }
 
 void launch_cross_kv(bool half, const CrossKvArgs& a, int sm_count, cudaStream_t stream) {
+    if (a.linear_out) {
+        if (a.windows != 1 || a.rows <= 0 || a.rows > a.row_stride || a.width <= 0 || a.width % 4 != 0 ||
+            a.kblocks != (a.width + 63) / 64 || a.columns <= 0 || a.columns % 4 != 0 ||
+            (reinterpret_cast<uintptr_t>(a.encoder) & 15) != 0 || (reinterpret_cast<uintptr_t>(a.weight) & 15) != 0 ||
+            (reinterpret_cast<uintptr_t>(a.linear_out) & 15) != 0 ||
+            (reinterpret_cast<uintptr_t>(a.residual) & 15) != 0)
+            throw std::runtime_error("tensor-core product: arguments out of range");
+        if (half) launch_typed<__half>(a, sm_count, stream);
+        else launch_typed<__nv_bfloat16>(a, sm_count, stream);
+        return;
+    }
     if (a.windows <= 0 || a.rows <= 0 || a.rows > a.row_stride || a.width <= 0 || a.width % 4 != 0 ||
         a.kblocks != (a.width + 63) / 64 || a.columns <= 0 || a.head_width <= 0 || a.groups <= 0 ||
         a.heads <= 0 || a.groups % a.heads != 0 ||

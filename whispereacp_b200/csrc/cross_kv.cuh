@@ -51,12 +51,22 @@ struct CrossKvArgs {
     int groups;             // L * H
     int heads;              // H
     int* status;            // nonzero on return: a bounded wait gave up (which one)
+    // The linear form (the encoder's products): with linear_out set, the
+    // product of `windows` (1) x `rows` rows is written row-major to
+    // linear_out [rows][columns] as gelu?(acc + bias[n]) (+ residual[row][n]
+    // when residual is set, which may be linear_out itself) instead of into
+    // the cross cache; head_width, groups and heads are then unused.
+    float* linear_out;
+    const float* bias;
+    const float* residual;
+    int gelu;
 };
 
 // Shared memory one CTA of the kernel asks for.
 size_t cross_kv_shared_bytes();
 
-// One launch over every window: persistent, at most one CTA per SM.
+// One launch over every window (or the linear form's rows): persistent, at
+// most one CTA per SM.
 // half: fp16 storage (else bf16).  Throws std::runtime_error on a launch
 // failure.
 void launch_cross_kv(bool half, const CrossKvArgs& args, int sm_count, cudaStream_t stream);
