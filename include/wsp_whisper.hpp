@@ -19,11 +19,15 @@
  * tokens between the two, which the reference leaves unimplemented
  * (Whisper.h:193-201) -- is setLanguage(code, translate).
  *
- * The mel front end and the encoder are outside this library: transcribe
- * takes the encoder's output rows ([windows, max_source_positions, d_model]
- * fp32) where the reference's transcribe takes samples; transcribeText
- * decodes the ids with the tokenizer (byte-level BPE, special tokens
- * dropped), as Whisper::transcribeText does (:1497-1507).
+ * `transcribe_samples` takes a recording (16 kHz samples, one 30 s window
+ * at most) through the log-mel spectrogram and the encoder on CUDA
+ * (wsp_encoder.hpp) -- the filterbank is preprocessor_config.json's
+ * mel_filters (Model/PreprocessorConfig.cpp:107-135) -- then the greedy
+ * search, as Whisper::transcribe does; `transcribe` takes encoder rows
+ * ([windows, max_source_positions, d_model] fp32) for a caller with its own
+ * encoder.  The _text forms decode the ids with the tokenizer (byte-level
+ * BPE, special tokens dropped), as Whisper::transcribeText does
+ * (:1497-1507).
  *
  * Errors: wsp::ModelError (a missing file or field, a shape the decoder does
  * not support, a token outside the vocabulary) and the ABI's others.
@@ -32,6 +36,7 @@
 #define WSP_WHISPER_HPP
 
 #include "wsp_decoder.hpp"
+#include "wsp_encoder.hpp"
 
 #include <cstdint>
 #include <cstdio>
@@ -305,6 +310,68 @@ struct ModelConfig {
 };
 
 // ---------------------------------------------------------------------------
+// preprocessor_config.json: PreprocessorConfig (Model/PreprocessorConfig.cpp:
+// 107-135), the filterbank mel-major [feature_size][n_fft / 2 + 1].
+
+struct PreprocessorConfig {
+    int sample_rate = 0, fft_size = 0, hop = 0, mel_bins = 0, chunk_seconds = 0, window_samples = 0, max_frames = 0;
+    std::vector<float> mel_filters;
+
+    static PreprocessorConfig from_json(std::string_view text) {
+        const json::Value v = json::parse(text, "preprocessor_config.json");
+        if (v.kind != json::Value::object) throw ModelError("preprocessor_config.json is not a JSON object");
+        auto field = [&](const char* name) {
+            const json::Value* f = v.find(name);
+            const std::string what = std::string("preprocessor_config.json field '") + name + "'";
+            if (!f) throw ModelError(what + " is missing");
+            if (f->kind != json::Value::number) throw ModelError(what + " is not a number");
+            if (f->n != (double)(int64_t)f->n) throw ModelError(what + " is not a whole 64-bit integer");
+            return (int)f->n;
+        };
+        PreprocessorConfig c;
+        c.sample_rate = field("sampling_rate");
+        c.fft_size = field("n_fft");
+        c.hop = field("hop_length");
+        c.mel_bins = field("feature_size");
+        c.chunk_seconds = field("chunk_length");
+        c.window_samples = field("n_samples");
+        c.max_frames = field("nb_max_frames");
+        if (c.sample_rate <= 0 || c.hop <= 0 || c.mel_bins <= 0)
+            throw ModelError("preprocessor_config.json has a non-positive rate, hop or mel bin count");
+        if (c.fft_size <= 0 || c.fft_size % 2 != 0)
+            throw ModelError("preprocessor_config.json n_fft is not a positive even number");
+        const json::Value* m = v.find("mel_filters");
+        if (!m) throw ModelError("preprocessor_config.json field 'mel_filters' is missing");
+        if (m->kind != json::Value::array) throw ModelError("preprocessor_config.json mel_filters is not an array");
+        const int columns = c.fft_size / 2 + 1;
+        int rows = (int)m->items.size(), cols = -1;
+        std::vector<float> values;
+        for (const json::Value& row : m->items) {
+            if (row.kind != json::Value::array)
+                throw ModelError("preprocessor_config.json mel_filters has a row that is not an array");
+            if (cols < 0) cols = (int)row.items.size();
+            else if ((int)row.items.size() != cols) throw ModelError("preprocessor_config.json mel_filters is ragged");
+            for (const json::Value& x : row.items) {
+                if (x.kind != json::Value::number)
+                    throw ModelError("preprocessor_config.json mel_filters is not a number");
+                values.push_back((float)x.n);
+            }
+        }
+        if (rows == c.mel_bins && cols == columns) {
+            c.mel_filters = std::move(values);
+        } else if (rows == columns && cols == c.mel_bins) {
+            c.mel_filters.resize(values.size());
+            for (int r = 0; r < rows; ++r)
+                for (int q = 0; q < cols; ++q) c.mel_filters[(size_t)q * rows + r] = values[(size_t)r * cols + q];
+        } else {
+            throw ModelError("preprocessor_config.json mel_filters is not " + std::to_string(c.mel_bins) + " x " +
+                             std::to_string(columns));
+        }
+        return c;
+    }
+};
+
+// ---------------------------------------------------------------------------
 // tokenizer.json: the vocabulary's spellings and the special tokens, and
 // decoding of ids back to text (Tokenizer.h:27-80, SpecialTokens.h:17-43).
 
@@ -476,11 +543,7 @@ public:
             return path;
         };
         config_ = ModelConfig::from_json(read_file(require("config.json")));
-        // The front end's settings: read and checked for shape only, the mel
-        // front end being outside this library.
-        if (json::parse(read_file(require("preprocessor_config.json")), "preprocessor_config.json").kind !=
-            json::Value::object)
-            throw ModelError("preprocessor_config.json is not a JSON object");
+        preprocessor_ = PreprocessorConfig::from_json(read_file(require("preprocessor_config.json")));
         tokenizer_ = Tokenizer::from_json(read_file(require("tokenizer.json")));
         weights_ = std::make_unique<SafeTensors>(SafeTensors::from_file(require("model.safetensors")));
         loaded_ = true;
@@ -492,14 +555,42 @@ public:
 
     // Whisper::prepare: the decoder on a CUDA device, its tensors uploaded
     // and the generation config set.  `windows` windows decode in lockstep.
+    // With the checkpoint's encoder tensors, the front end too: the
+    // spectrogram's shapes are Whisper's (16 kHz, n_fft 400, hop 160; 80 or
+    // 128 mel bins, as config.json and the filterbank agree), which is what
+    // Whisper::requireWhisperShapes asks (Whisper.cpp:169-200).
     void prepare(int device = 0, int windows = 1, wsp_dtype storage = WSP_FLOAT16) {
         require_loaded();
-        decoder_ = std::make_unique<CudaDecoder>(config_.decoder_shape(), device, windows, storage);
-        for (const SafeTensors::Tensor& t : weights_->tensors())
-            if (t.name.rfind("model.decoder.", 0) == 0) decoder_->upload(t.name, t.data, t.type, t.shape);
-        decoder_->checkWeights();
+        decoder_.reset();
+        encoder_.reset();
+        auto decoder = std::make_unique<CudaDecoder>(config_.decoder_shape(), device, windows, storage);
+        bool has_encoder = false;
+        for (const SafeTensors::Tensor& t : weights_->tensors()) {
+            if (t.name.rfind("model.decoder.", 0) == 0) decoder->upload(t.name, t.data, t.type, t.shape);
+            if (t.name.rfind("model.encoder.conv1.", 0) == 0) has_encoder = true;
+        }
+        decoder->checkWeights();
+        if (has_encoder) {
+            if (preprocessor_.mel_bins != config_.mel_bins)
+                throw ModelError("this model wants " + std::to_string(config_.mel_bins) +
+                                 " mel bins and preprocessor_config.json publishes " +
+                                 std::to_string(preprocessor_.mel_bins));
+            if (preprocessor_.sample_rate != 16000 || preprocessor_.fft_size != 400 || preprocessor_.hop != 160)
+                throw ModelError("preprocessor_config.json describes a front end other than Whisper's "
+                                 "(16 kHz, n_fft 400, hop 160)");
+            const EncoderShape shape{config_.mel_bins, config_.width, config_.encoder_heads, config_.encoder_layers,
+                                     config_.encoder_ffn, 2 * config_.max_source_positions};
+            auto encoder = std::make_unique<CudaEncoder>(shape, device, storage);
+            for (const SafeTensors::Tensor& t : weights_->tensors())
+                if (t.name.rfind("model.encoder.", 0) == 0) encoder->upload(t.name, t.data, t.type, t.shape);
+            encoder->setFilters(preprocessor_.mel_filters.data());
+            encoder->checkWeights();
+            encoder_ = std::move(encoder);
+        }
+        decoder_ = std::move(decoder);
         apply_generation_config();
     }
+    bool has_front_end() const { return encoder_ != nullptr; }
     bool is_prepared() const { return decoder_ != nullptr; }
 
     const ModelConfig& config() const { return config_; }
@@ -568,6 +659,35 @@ public:
         return out;
     }
 
+    // Whisper::transcribe on recordings: one per window the decoder was
+    // prepared with, each 16 kHz samples of at most one 30 s window (a
+    // longer one is a ModelError, as in the reference), through the
+    // spectrogram and the encoder, then the greedy search.
+    std::vector<std::vector<uint32_t>> transcribe_samples(const std::vector<std::vector<float>>& recordings) {
+        require_prepared();
+        if (!encoder_) throw ModelError("this model has no encoder tensors: transcribe its encoder rows instead");
+        const int windows = decoder_->windows();
+        if ((int)recordings.size() != windows)
+            throw ModelError("this Whisper decodes " + std::to_string(windows) + " windows at once and was given " +
+                             std::to_string(recordings.size()) + " recordings");
+        const size_t per = (size_t)encoder_->positions() * config_.width;
+        std::vector<float> rows(per * windows);
+        for (int b = 0; b < windows; ++b)
+            encoder_->encodeSamples(recordings[b].data(), (int)recordings[b].size(), rows.data() + per * b);
+        return transcribe(rows.data());
+    }
+    std::vector<std::string> transcribe_samples_text(const std::vector<std::vector<float>>& recordings) {
+        std::vector<std::string> out;
+        for (const auto& ids : transcribe_samples(recordings)) out.push_back(tokenizer_.decode(ids));
+        return out;
+    }
+
+    CudaEncoder& encoder() {
+        require_prepared();
+        if (!encoder_) throw ModelError("this model has no encoder tensors");
+        return *encoder_;
+    }
+
     CudaDecoder& decoder() {
         require_prepared();
         return *decoder_;
@@ -626,9 +746,11 @@ private:
     }
 
     ModelConfig config_;
+    PreprocessorConfig preprocessor_;
     Tokenizer tokenizer_;
     std::unique_ptr<SafeTensors> weights_;
     std::unique_ptr<CudaDecoder> decoder_;
+    std::unique_ptr<CudaEncoder> encoder_;
     bool loaded_ = false;
     std::vector<uint32_t> prompt_;
     std::vector<float> first_mask_, later_mask_;

@@ -12,6 +12,10 @@
 //       set the audio context, transcribe the fp32 rows in ENCODER
 //       ([WINDOWS, max_source_positions, d_model]) and print each window's
 //       ids and the hex bytes of its text
+//   whisper_test samples DIR AUDIO WINDOWS COUNT
+//       load, prepare with WINDOWS windows, transcribe the recordings in
+//       AUDIO (WINDOWS x COUNT fp32 samples) through the spectrogram and the
+//       encoder, and print each window's ids and the hex bytes of its text
 #include "wsp_whisper.hpp"
 
 #include <cstdio>
@@ -116,11 +120,44 @@ int transcribe(char** argv) {
     return 0;
 }
 
+int samples(char** argv) {
+    wsp::Whisper whisper;
+    whisper.load(argv[2]);
+    const int windows = std::stoi(argv[4]), count = std::stoi(argv[5]);
+    std::vector<std::vector<float>> recordings((size_t)windows, std::vector<float>((size_t)count));
+    std::ifstream in(argv[3], std::ios::binary);
+    for (auto& r : recordings) in.read(reinterpret_cast<char*>(r.data()), (std::streamsize)(r.size() * sizeof(float)));
+    if (!in) {
+        std::printf("short audio file\n");
+        return 1;
+    }
+    whisper.prepare(0, windows);
+    if (!whisper.has_front_end()) {
+        std::printf("no front end\n");
+        return 1;
+    }
+    const auto ids = whisper.transcribe_samples(recordings);
+    const auto texts = whisper.transcribe_samples_text(recordings);
+    for (int b = 0; b < windows; ++b) {
+        print_ids("ids", ids[b]);
+        print_hex("text", texts[b]);
+    }
+    try {
+        recordings.pop_back();
+        whisper.transcribe_samples(recordings);
+        std::printf("accepted too few recordings\n");
+        return 1;
+    } catch (const wsp::ModelError&) {
+    }
+    std::printf("ok\n");
+    return 0;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
     if (argc < 3) {
-        std::printf("usage: whisper_test inspect|refuse|transcribe DIR ...\n");
+        std::printf("usage: whisper_test inspect|refuse|transcribe|samples DIR ...\n");
         return 2;
     }
     const std::string mode = argv[1];
@@ -128,6 +165,7 @@ int main(int argc, char** argv) {
         if (mode == "inspect") return inspect(argc, argv);
         if (mode == "refuse") return refuse(argv);
         if (mode == "transcribe" && argc >= 7) return transcribe(argv);
+        if (mode == "samples" && argc >= 6) return samples(argv);
     } catch (const std::exception& e) {
         std::printf("error: %s\n", e.what());
         return 1;

@@ -140,6 +140,11 @@ def test_audio_context_for_samples(program, repo):
     (lambda d: edit_tokenizer(d, lambda t: t["model"].pop("merges")), "tokenizer.json has no 'merges'"),
     (lambda d: open(os.path.join(d, "config.json"), "w").write("{\"d_model\": 12,"), "config.json is not valid JSON"),
     (lambda d: truncate(os.path.join(d, "model.safetensors")), "do not fit its shape or the file"),
+    (lambda d: edit_preprocessor(d, lambda c: c.pop("hop_length")),
+     "preprocessor_config.json field 'hop_length' is missing"),
+    (lambda d: edit_preprocessor(d, lambda c: c["mel_filters"][3].pop()), "mel_filters is ragged"),
+    (lambda d: edit_preprocessor(d, lambda c: c["mel_filters"].pop()), "mel_filters is not 80 x 201"),
+    (lambda d: edit_preprocessor(d, lambda c: c.update(n_fft=401)), "n_fft is not a positive even number"),
 ])
 def test_load_refuses_with_the_reference_messages(program, tmp_path, change, message):
     repo = R.write_repo(str(tmp_path / "repo"), width=64, layers=1, seed=3)
@@ -150,6 +155,13 @@ def test_load_refuses_with_the_reference_messages(program, tmp_path, change, mes
 
 def edit_config(directory, edit):
     path = os.path.join(directory, "config.json")
+    config = json.load(open(path))
+    edit(config)
+    json.dump(config, open(path, "w"))
+
+
+def edit_preprocessor(directory, edit):
+    path = os.path.join(directory, "preprocessor_config.json")
     config = json.load(open(path))
     edit(config)
     json.dump(config, open(path, "w"))
@@ -166,6 +178,14 @@ def truncate(path):
     size = os.path.getsize(path)
     with open(path, "r+b") as f:
         f.truncate(size - 64)
+
+
+def test_a_transposed_filterbank_is_read_mel_major(program, tmp_path):
+    """PreprocessorConfig accepts mel_filters as [bins][mels] too
+    (PreprocessorConfig.cpp:66-76)."""
+    repo = R.write_repo(str(tmp_path / "repo"), width=64, layers=1, seed=5)
+    edit_preprocessor(repo.directory, lambda c: c.update(mel_filters=np.asarray(c["mel_filters"]).T.tolist()))
+    run(program, "inspect", repo.directory)
 
 
 def test_without_end_of_text_the_decoder_start_comes_from_the_tokenizer(program, tmp_path):
@@ -223,3 +243,35 @@ def test_transcribe_through_the_header(program, repo, tmp_path, storage, context
                 decided += 1
             chunk = [token]
     assert decided > 0
+
+
+@pytest.mark.gpu
+def test_transcribe_samples_through_the_header(program, repo, tmp_path):
+    """Whisper::transcribe on recordings: the header's spectrogram, encoder and
+    greedy search give the ids the Python bindings give by the same route
+    (Encoder.encode_samples, then Decoder.transcribe), window by window."""
+    from oracle import frontend as FE
+    from whispereacp_b200 import Decoder, Encoder, EncoderShape
+
+    windows, count = 2, 9000
+    audio = np.stack([FE.synthetic_audio(count, seed=70 + b) for b in range(windows)])
+    path = tmp_path / "audio.bin"
+    path.write_bytes(np.ascontiguousarray(audio, np.float32).tobytes())
+    f = fields(run(program, "samples", repo.directory, path, windows, count))
+    assert f["ok"] == [""]
+    got = [ids_of(v) for v in f["ids"]]
+
+    encoder = Encoder(EncoderShape.from_config(repo.config))
+    encoder.load_weights(repo.encoder)
+    encoder.set_filters(repo.filters)
+    rows = np.stack([encoder.encode_samples(audio[b]) for b in range(windows)])
+    first, later = R.masks(repo)
+    prompt = [repo.token("<|startoftranscript|>"), repo.token("<|notimestamps|>")]
+    decoder = Decoder(repo.shape, windows=windows)
+    decoder.load_weights(repo.tensors)
+    decoder.set_generation(prompt, first, later, maximum_tokens=repo.shape.max_positions - 2,
+                           end_of_text=repo.token("<|endoftext|>"))
+    expected = decoder.transcribe(rows)
+    for b in range(windows):
+        assert got[b] == [int(x) for x in expected[b]]
+        assert bytes.fromhex(f["text"][b]) == R.decode(repo.texts, repo.first_added, got[b])

@@ -16,8 +16,9 @@ import os
 
 import numpy as np
 
+from oracle import frontend as FE
 from oracle import oracle as O
-from tests.helpers import stored_tensors
+from tests.helpers import round_to, stored_tensors
 from whispereacp_b200 import synthetic as S
 from whispereacp_b200.decoder import DecoderShape
 
@@ -110,9 +111,11 @@ def write_repo(directory: str, width: int = 128, heads: int = 2, layers: int = 2
     config.update(overrides)
     with open(os.path.join(directory, "config.json"), "w") as f:
         json.dump(config, f, indent=2)
+    filters = FE.synthetic_filters(80)
     with open(os.path.join(directory, "preprocessor_config.json"), "w") as f:
         json.dump({"feature_size": 80, "hop_length": 160, "n_fft": 400, "n_samples": 480000,
-                   "sampling_rate": 16000, "chunk_length": 30}, f)
+                   "sampling_rate": 16000, "chunk_length": 30, "nb_max_frames": 3000,
+                   "mel_filters": filters.astype(np.float64).tolist()}, f)
     tokenizer = {
         "version": "1.0", "truncation": None, "padding": None,
         "added_tokens": [{"id": first_added + k, "content": t, "single_word": False, "lstrip": False,
@@ -132,12 +135,18 @@ def write_repo(directory: str, width: int = 128, heads: int = 2, layers: int = 2
                          vocabulary_size=v, max_positions=target_positions, cross_positions=source_positions)
     tensors = stored_tensors(S.normal_weights(shape, seed=seed), storage)
     stored = {k: np.ascontiguousarray(t, np.float32) for k, t in tensors.items()}
-    # What a checkpoint holds besides the decoder: encoder tensors and an
-    # integer buffer, which the loader reads past.
-    stored["model.encoder.conv1.weight"] = np.zeros((width, 80, 3), np.float32)
+    # The encoder (its matrices fp16 values in fp32 containers, as a
+    # checkpoint's), and an integer buffer the loader reads past.
+    encoder = FE.synthetic_encoder_tensors(80, width, config["encoder_layers"], config["encoder_ffn_dim"],
+                                           source_positions, seed=seed + 1)
+    encoder = {k: (round_to(storage, v) if v.ndim > 1 and "embed_positions" not in k else v) for k, v in encoder.items()}
+    stored.update(encoder)
     stored["model.encoder.position_ids"] = np.arange(source_positions, dtype=np.int64)
     save_file(stored, os.path.join(directory, "model.safetensors"))
-    return Repo(directory, shape, tensors, texts, first_added, config)
+    repo = Repo(directory, shape, tensors, texts, first_added, config)
+    repo.encoder = encoder
+    repo.filters = filters
+    return repo
 
 
 def masks(repo: Repo) -> tuple[np.ndarray, np.ndarray]:
