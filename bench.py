@@ -52,6 +52,8 @@ def parse_args():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-batch1", action="store_true", help="skip the extra base.en batch-1 timing")
+    p.add_argument("--no-audio", action="store_true",
+                   help="skip the base.en audio -> log-mel -> encoder -> greedy tokens timing")
     p.add_argument("--tokens", type=int, default=0,
                    help="tokens per window (default: the config's); smaller for profiler captures")
     p.add_argument("--windows", type=int, default=0,
@@ -238,6 +240,54 @@ def batch1_line(args, local, flush, peak):
             "roofline_frac": per_step / (ms * 1e-3) / 1e9 / peak}
 
 
+def audio_line(args, local):
+    """Configuration C2 end to end on one GPU: 30 s of audio (three seeded
+    sinusoids and N(0, 0.05) noise) through the log-mel spectrogram and the
+    base.en encoder (random-init weights), then 224 greedy tokens: host
+    samples in, token ids out, through the public calls."""
+    import ctypes
+    import torch
+    from whispereacp_b200 import synthetic as FE
+    from whispereacp_b200 import Decoder, Encoder, EncoderShape, synthetic as S
+    run = S.CONFIGS["base_en_b1"]
+    shape = run.shape
+    eshape = EncoderShape(80, shape.width, shape.heads, shape.layers, shape.feed_forward_width, 3000)
+    encoder = Encoder(eshape, device=local)
+    encoder.load_weights(FE.synthetic_encoder_tensors(80, shape.width, shape.layers, shape.feed_forward_width, 1500,
+                                                      seed=1, scale=0.02))
+    encoder.set_filters(FE.synthetic_filters(80))
+    decoder = Decoder(shape, windows=1, device=local, storage=run.storage)
+    decoder.load_weights(S.normal_weights(shape, seed=0))
+    first, later = S.suppression_masks(shape.vocabulary_size)
+    decoder.set_generation(run.prompt, first, later, maximum_tokens=run.steps, end_of_text=S.END_OF_TEXT,
+                           stop_at_end_of_text=False)
+    audio = torch.from_numpy(FE.synthetic_audio(480000)).pin_memory()
+    rows = torch.empty((1500, shape.width), dtype=torch.float32, device=f"cuda:{local}")
+    lib = encoder._lib
+    from whispereacp_b200._native import check
+
+    def once():
+        t0 = time.perf_counter()
+        check(lib.wsp_encoder_encode_samples(encoder._handle, ctypes.c_void_p(audio.data_ptr()), 480000,
+                                             ctypes.c_void_p(rows.data_ptr())))
+        t1 = time.perf_counter()
+        ids = decoder.transcribe(rows.data_ptr())[0]
+        t2 = time.perf_counter()
+        return (t1 - t0) * 1e3, (t2 - t1) * 1e3, len(ids)
+
+    for _ in range(2):
+        once()
+    samples = [once() for _ in range(max(3, min(args.steps, 5)))]
+    front = statistics.median(x[0] for x in samples)
+    decode = statistics.median(x[1] for x in samples)
+    encoder.close()
+    decoder.close()
+    return {"workload": "base.en: 30 s of audio -> log-mel -> encoder -> 224 greedy tokens, 1 window",
+            "ms_per_window": front + decode, "frontend_ms": front, "decode_ms": decode,
+            "tokens_per_s": samples[0][2] / ((front + decode) * 1e-3),
+            "timing": "host clock around the public calls (pinned host samples in, token ids out), median"}
+
+
 def run_ours(args, run):
     import torch
     from whispereacp_b200 import Decoder, synthetic as S
@@ -313,6 +363,7 @@ def run_ours(args, run):
 
     peak, peak_kind = peaks()
     extra = batch1_line(args, local, flush, peak) if rank == 0 and not args.no_batch1 else None
+    audio = audio_line(args, local) if rank == 0 and not args.no_audio else None
     if world > 1:
         torch.distributed.barrier()
     tokens = run.windows * tokens_per_window
@@ -367,6 +418,8 @@ def run_ours(args, run):
         if extra is not None:
             result["batch1"] = extra
             result["batch1_ms_per_token_step"] = extra["ms_per_token_step"]
+        if audio is not None:
+            result["audio_to_tokens"] = audio
         if not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
             result["cpu_baseline"] = cpu_baseline_port(run, tensors_for_oracle(tensors, run.storage),

@@ -123,70 +123,7 @@ def encode(tensors: dict, mel: np.ndarray, heads: int, layers: int) -> np.ndarra
 
 # ------------------------------------------------------------ test inputs
 
-def encoder_tensor_names(layers: int) -> list[str]:
-    e = "model.encoder."
-    names = [e + "conv1.weight", e + "conv1.bias", e + "conv2.weight", e + "conv2.bias",
-             e + "embed_positions.weight", e + "layer_norm.weight", e + "layer_norm.bias"]
-    for i in range(layers):
-        p = f"{e}layers.{i}."
-        names += [p + s for s in ("self_attn_layer_norm.weight", "self_attn_layer_norm.bias",
-                                  "self_attn.q_proj.weight", "self_attn.q_proj.bias", "self_attn.k_proj.weight",
-                                  "self_attn.v_proj.weight", "self_attn.v_proj.bias", "self_attn.out_proj.weight",
-                                  "self_attn.out_proj.bias", "final_layer_norm.weight", "final_layer_norm.bias",
-                                  "fc1.weight", "fc1.bias", "fc2.weight", "fc2.bias")]
-    return names
-
-
-def encoder_extents(name: str, mel_bins: int, width: int, ffn: int, positions: int) -> tuple[int, ...]:
-    tail = name.split(".", 2)[2] if name.startswith("model.encoder.") else name
-    if tail.startswith("layers."):
-        tail = tail.split(".", 2)[2]
-    table = {
-        "conv1.weight": (width, mel_bins, 3), "conv2.weight": (width, width, 3),
-        "embed_positions.weight": (positions, width),
-        "self_attn.q_proj.weight": (width, width), "self_attn.k_proj.weight": (width, width),
-        "self_attn.v_proj.weight": (width, width), "self_attn.out_proj.weight": (width, width),
-        "fc1.weight": (ffn, width), "fc1.bias": (ffn,), "fc2.weight": (width, ffn),
-    }
-    return table.get(tail, (width,))
-
-
-def synthetic_encoder_tensors(mel_bins: int, width: int, layers: int, ffn: int, positions: int,
-                              seed: int = 7, scale: float = 0.05) -> dict[str, np.ndarray]:
-    """Seeded weights in the ranges a trained encoder's sit in: matrices and
-    biases N(0, scale), LayerNorm gains 1 + N(0, scale), offsets N(0, scale),
-    the positional rows N(0, 0.5)."""
-    rng = np.random.Generator(np.random.PCG64(seed))
-    out = {}
-    for name in encoder_tensor_names(layers):
-        shape = encoder_extents(name, mel_bins, width, ffn, positions)
-        values = rng.normal(0.0, 0.5 if "embed_positions" in name else scale, size=shape)
-        if name.endswith("norm.weight"):
-            values = 1.0 + values
-        out[name] = values.astype(np.float32)
-    return out
-
-
-def synthetic_filters(mel_bins: int, bins: int = 201, seed: int = 5) -> np.ndarray:
-    """Triangular filters over the bins, like a mel filterbank's shape."""
-    centres = np.linspace(1.0, bins - 2.0, mel_bins + 2)
-    b = np.arange(bins, dtype=np.float64)
-    out = np.zeros((mel_bins, bins))
-    for m in range(mel_bins):
-        lo, mid, hi = centres[m], centres[m + 1], centres[m + 2]
-        up = (b - lo) / max(mid - lo, 1e-9)
-        down = (hi - b) / max(hi - mid, 1e-9)
-        out[m] = np.maximum(0.0, np.minimum(up, down)) * 2.0 / max(hi - lo, 1e-9)
-    return out.astype(np.float32)
-
-
-def synthetic_audio(count: int, seed: int = 3) -> np.ndarray:
-    """Three seeded sinusoids (100-4000 Hz) and N(0, 0.05) noise at 16 kHz,
-    clipped to [-1, 1]."""
-    rng = np.random.Generator(np.random.PCG64(seed))
-    t = np.arange(count) / 16000.0
-    x = np.zeros(count)
-    for _ in range(3):
-        x += rng.uniform(0.1, 0.4) * np.sin(2 * math.pi * rng.uniform(100, 4000) * t + rng.uniform(0, 2 * math.pi))
-    x += rng.normal(0.0, 0.05, count)
-    return np.clip(x, -1.0, 1.0).astype(np.float32)
+# The seeded inputs live with the package's other synthetic inputs (the
+# bench draws them too); re-exported here under the names the tests use.
+from whispereacp_b200.synthetic import (encoder_extents, encoder_tensor_names,  # noqa: E402,F401
+                                        synthetic_audio, synthetic_encoder_tensors, synthetic_filters)
