@@ -720,6 +720,8 @@ private:
         const size_t Rf = std::min<size_t>(R, kInlineNormRows);
         out_partials_.allocate(2 * H * Rf * d * 4);
         hidden_mid_.allocate(Rf * d * 4);
+        hidden_alt_.allocate(Rf * d * 4);
+        ffn_partials_.allocate((size_t)kFfnParts * Rf * d * 4);
         const size_t grid = (size_t)kMaxBlocksPerSm * sm_count_;
         candidate_values_.allocate(R * grid * 4);
         candidate_indices_.allocate(R * grid * 4);
@@ -778,6 +780,7 @@ private:
     static constexpr int kMaxBlocksPerSm = 2;
     static constexpr int kStaticSharedBytes = 2048;
     static constexpr int kMinStages = 3;
+    static constexpr int kFfnParts = 4;  // K parts of a few-row fc2
 
     // The step: recordDecoderStep (Decoder.cpp:151-177) with decoderLayer
     // (Decoder.cpp:73-115), lowered onto the ops of step.cuh.
@@ -826,6 +829,17 @@ private:
         const bool fuse_out = !umma_ && R <= kInlineNormRows && d == 64 * H && (long long)R * H < grid;
         float* self_partials = out_partials_.get<float>();
         float* cross_partials = self_partials + (size_t)H * std::min(R, kInlineNormRows) * d;
+        // With the out-projections fused, fc2 (a few tiles of a long K) also
+        // splits its K over kFfnParts items a tile, each writing its sums
+        // apart; the next layer's LayerNorm prologue adds the parts and the
+        // bias to h, keeping the new residual rows in hidden_alt_ (which the
+        // cross attention then reads), so no CTA reads rows another rewrites
+        // in the same op.  The last layer's fc2 adds to h itself: the logits
+        // read h.
+        const int ffn_tiles = (d + 15) / 16 * ((R + 7) / 8);
+        const bool split_ffn = fuse_out && kpf != kpd && (kpf / 32) % kFfnParts == 0 &&
+                               (long long)ffn_tiles * kFfnParts <= grid;
+        float* ffn_partials = ffn_partials_.get<float>();
         std::vector<StepOp> ops;
         StepOp e{};
         e.kind = kOpEmbed;
@@ -851,6 +865,14 @@ private:
             qkv.self_keys = self_keys_.get<char>() + l * self_layer;
             qkv.self_values = self_values_.get<char>() + l * self_layer;
             qkv.prefetch_keys = fuse_out ? 1 : 0;
+            if (split_ffn && l > 0) {
+                // The previous layer's fc2 parts and bias, added to h.
+                qkv.addends = ffn_partials;
+                qkv.addend_count = kFfnParts;
+                qkv.addend_stride = (long long)R * d;
+                qkv.addend_bias = layers_[l - 1].fc2_b.get<float>();
+                qkv.sum_out = hidden_alt_.get<float>();
+            }
             ops.push_back(qkv);
             StepOp self{};
             self.kind = kOpSelfAttention;
@@ -885,6 +907,7 @@ private:
                 cross.addend_stride = (long long)R * d;
                 cross.addend_bias = W.o_b.get<float>();
                 cross.sum_out = hidden_mid_.get<float>();
+                if (split_ffn && l > 0) cross.norm_input = hidden_alt_.get<float>();
             } else {
                 StepOp cq = product(kEpStore, W.qc_w, H * (int)round16(D), kpd, W.qc_b);
                 cq.slice = D;
@@ -937,6 +960,11 @@ private:
             down.ld_input = kpf;
             down.out = hidden_.get();
             down.ld_out = d;
+            if (split_ffn && l + 1 < shape_.layers) {
+                down.epilogue = kEpPartial;
+                down.kparts = kFfnParts;
+                down.out = ffn_partials;
+            }
             ops.push_back(down);
         }
         // Final layer norm and the tied logits with the masked argmax
@@ -1418,7 +1446,7 @@ private:
     bool cross_weights_dirty_ = false;
     DeviceBuffer ring_, ring_prompt_, state_, masks_;
     DeviceBuffer hidden_, queries_, normalised_, attended_, feed_forward_, partial_, partial_d_, split_counters_;
-    DeviceBuffer out_partials_, hidden_mid_;
+    DeviceBuffer out_partials_, hidden_mid_, hidden_alt_, ffn_partials_;
     DeviceBuffer candidate_values_, candidate_indices_, row_tokens_, counters_;
     DeviceBuffer barrier_, ended_, profile_;
     DeviceBuffer logits_staging_, hidden_staging_;

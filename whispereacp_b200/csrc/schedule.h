@@ -27,14 +27,14 @@ inline int schedule_round16(int n) { return (n + 15) / 16 * 16; }
 // product's tile (8 * NT of the launch).
 inline int op_items(const StepParams& p, const StepOp& op, int rt) {
     switch (op.kind) {
-    case kOpProduct: return ((op.n + 15) / 16) * schedule_row_tiles(p.rows, rt);
+    case kOpProduct: return ((op.n + 15) / 16) * schedule_row_tiles(p.rows, rt) * (op.kparts > 1 ? op.kparts : 1);
     case kOpLogits: return ((p.vocabulary + 15) / 16) * schedule_row_tiles(p.out_rows, rt);
     }
     return 0;
 }
 
 // Weight region `region` of item `item` of an op; false when there is none.
-inline bool item_region(const StepParams& p, const StepOp& op, int item, int region, Region& out) {
+inline bool item_region(const StepParams& p, const StepOp& op, int item, int region, int rt, Region& out) {
     switch (op.kind) {
     case kOpProduct:
     case kOpLogits: {
@@ -42,8 +42,14 @@ inline bool item_region(const StepParams& p, const StepOp& op, int item, int reg
         const int n = op.kind == kOpProduct ? op.n : p.vocabulary;
         const int kp = op.kind == kOpProduct ? op.kp : p.kpd;
         const void* w = op.kind == kOpProduct ? op.weight : p.token_table;
-        const int tile = item % ((n + 15) / 16);
-        out = Region{static_cast<const unsigned char*>(w) + (size_t)tile * (kp / 32) * 1024, 1, kp / 32, 1};
+        const int n_tiles = (n + 15) / 16, tile = item % n_tiles;
+        // A split product's item: part item / (tiles x row tiles), its share
+        // of the tile's chunks (contiguous in the fragment-packed layout).
+        const int parts = op.kind == kOpProduct && op.kparts > 1 ? op.kparts : 1;
+        const int part = item / (n_tiles * schedule_row_tiles(p.rows, rt));
+        const int chunks = kp / 32 / parts;
+        out = Region{static_cast<const unsigned char*>(w) + ((size_t)tile * (kp / 32) + (size_t)part * chunks) * 1024,
+                     1, chunks, 1};
         return true;
     }
     }
@@ -212,7 +218,8 @@ inline void build_schedule(const StepParams& p, const std::vector<StepOp>& ops, 
             const int items = op_items(p, op, rt);
             for (int item = cta; item < items; item += grid) {
                 Region r;
-                for (int region = 0; item_region(p, op, item, region, r); ++region) append_region(r, stage_chunks, units);
+                for (int region = 0; item_region(p, op, item, region, rt, r); ++region)
+                    append_region(r, stage_chunks, units);
             }
         }
         offsets.push_back((unsigned)units.size());

@@ -898,20 +898,28 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
     const bool normalise = op.gamma != nullptr;
     const int n_tiles = (op.n + 15) / 16;
     const int r_tiles = (p.rows + RT - 1) / RT;
+    // A split product (kEpPartial): kparts items a tile, each over its share
+    // of K, reading its 16-bit input rows straight from memory.
+    const int parts = op.kparts > 1 ? op.kparts : 1;
+    const int kps = op.kp / parts;
     int cached_tile = -1;
 
-    for (int item = blockIdx.x; item < n_tiles * r_tiles; item += gridDim.x) {
-        const int r_tile = item / n_tiles, n_tile = item % n_tiles;
+    for (int item = blockIdx.x; item < n_tiles * r_tiles * parts; item += gridDim.x) {
+        const int part = item / (n_tiles * r_tiles), rest = item % (n_tiles * r_tiles);
+        const int r_tile = rest / n_tiles, n_tile = rest % n_tiles;
         const int r0 = r_tile * RT, n0 = n_tile * 16;
         const int rows_valid = min(RT, p.rows - r0);
         // This thread's outputs' biases, loaded now so the epilogue does not
-        // wait on memory for them.
+        // wait on memory for them.  (A part's sums go out without it: the
+        // op that adds the parts adds the bias.)
         constexpr int kOuts = (16 * RT + kThreads - 1) / kThreads;
         float bias_of[kOuts];
 #pragma unroll
         for (int k = 0; k < kOuts; ++k) {
             const int n = n0 + (threadIdx.x + k * kThreads) / RT;
-            bias_of[k] = op.bias && threadIdx.x + k * kThreads < 16 * RT && n < op.n ? __ldg(op.bias + n) : 0.f;
+            bias_of[k] = op.bias && op.epilogue != kEpPartial && threadIdx.x + k * kThreads < 16 * RT && n < op.n
+                             ? __ldg(op.bias + n)
+                             : 0.f;
         }
         float acc[NT][4];
         bool ok;
@@ -942,8 +950,8 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
             }
             ok = product_tile<WT, NT, true>(p, s, op.kp, xs, pitch, xs_lo, rows_valid, acc);
         } else {
-            const WT* X = static_cast<const WT*>(op.input16) + (size_t)r0 * op.ld_input;
-            ok = product_tile<WT, NT, false>(p, s, op.kp, X, op.ld_input, lo_plane(p, op.ld_input), rows_valid, acc);
+            const WT* X = static_cast<const WT*>(op.input16) + (size_t)r0 * op.ld_input + (size_t)part * kps;
+            ok = product_tile<WT, NT, false>(p, s, kps, X, op.ld_input, lo_plane(p, op.ld_input), rows_valid, acc);
         }
         if (!ok) return;
         Trace tre = trace_of(p.profile);
@@ -956,6 +964,10 @@ __device__ void op_product(const StepParams& p, const StepOp& op, int position, 
             const int nl = o / RT, rl = o % RT;
             const int n = n0 + nl, r = r0 + rl;
             if (n >= op.n || rl >= rows_valid) continue;
+            if (op.epilogue == kEpPartial) {
+                static_cast<float*>(op.out)[((size_t)part * p.rows + r) * op.ld_out + n] = product_sum(red, RT, nl, rl);
+                continue;
+            }
             emit_output<WT>(p, op, position, n, r, product_sum(red, RT, nl, rl) + bias_of[k]);
         }
         consumer_sync();

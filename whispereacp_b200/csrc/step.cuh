@@ -59,7 +59,7 @@ enum OpKind : int {
     kOpNone = 5,
     kOpNorm = 6,
 };
-enum EpilogueKind : int { kEpQkv = 0, kEpStore = 1, kEpResidual = 2, kEpGelu = 3 };
+enum EpilogueKind : int { kEpQkv = 0, kEpStore = 1, kEpResidual = 2, kEpGelu = 3, kEpPartial = 4 };
 
 // state words (int): position, error bits, abort, steps done, all windows
 // ended, and where the first bounded wait gave up: its kind (WaitKind), CTA,
@@ -168,6 +168,11 @@ struct StepOp {
     // qkv_row_stride apart in a weight tile's block, in split order, then
     // qkv_bias -- appends k and v to the caches and attends with q.
     int defer_join;
+    // A few-row product split over its inner size (mma.sync form): kparts
+    // items a tile, each over kp / kparts of K, writing its sums without the
+    // bias (kEpPartial) to out [part][R][ld_out]; the LayerNorm prologue of
+    // the op that reads them adds the parts in order (its addends).
+    int kparts;
     const float* qkv_partial;
     long long qkv_split_stride;
     int qkv_row_stride;
