@@ -690,8 +690,8 @@ __device__ __forceinline__ void product_chunk(const unsigned char* unit, int c, 
                                               int k0, const bool (&x_ok)[NT], float (&acc)[NT][4]) {
     const int lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
-    const uint4* w = reinterpret_cast<const uint4*>(unit + ((size_t)c * 32 + lane) * 32);
-    const uint4 lo = w[0], hi = w[1];
+    const unsigned char* w = unit + (size_t)c * 1024 + lane * 16;
+    const uint4 lo = *reinterpret_cast<const uint4*>(w), hi = *reinterpret_cast<const uint4*>(w + 512);
     uint4 B[NT], L[NT];
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
@@ -728,9 +728,10 @@ __device__ __forceinline__ void product_chunk_pair(const unsigned char* unit, in
                                                    float (&acc)[NT][4], float (&acc2)[NT][4]) {
     const int lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
-    const uint4* w = reinterpret_cast<const uint4*>(unit + ((size_t)c * 32 + lane) * 32);
-    const uint4* w2 = reinterpret_cast<const uint4*>(unit + ((size_t)c2 * 32 + lane) * 32);
-    const uint4 lo = w[0], hi = w[1], lo2 = w2[0], hi2 = w2[1];
+    const unsigned char* w = unit + (size_t)c * 1024 + lane * 16;
+    const unsigned char* w2 = unit + (size_t)c2 * 1024 + lane * 16;
+    const uint4 lo = *reinterpret_cast<const uint4*>(w), hi = *reinterpret_cast<const uint4*>(w + 512);
+    const uint4 lo2 = *reinterpret_cast<const uint4*>(w2), hi2 = *reinterpret_cast<const uint4*>(w2 + 512);
     uint4 B[NT], B2[NT], L[NT], L2[NT];
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
@@ -1590,12 +1591,11 @@ __device__ void head_out_projection(const StepParams& p, const StepOp& op, int r
         for (int i = 0; i < kBatch; ++i) {
             const int t = first + (t0 + i * kWarps) * step;
             if (t0 + i * kWarps < tiles) {
-                const uint4* src =
-                    reinterpret_cast<const uint4*>(wbase + (((size_t)t * chunks + 2 * head) * 32 + lane) * 32);
-                w[i][0] = ld_nc4(src);
-                w[i][1] = ld_nc4(src + 1);
-                w[i][2] = ld_nc4(src + 64);  // the next chunk: 32 lanes x 32 bytes on
-                w[i][3] = ld_nc4(src + 65);
+                const unsigned char* src = wbase + ((size_t)t * chunks + 2 * head) * 1024 + lane * 16;
+                w[i][0] = ld_nc4(reinterpret_cast<const uint4*>(src));
+                w[i][1] = ld_nc4(reinterpret_cast<const uint4*>(src + 512));
+                w[i][2] = ld_nc4(reinterpret_cast<const uint4*>(src + 1024));  // the next chunk
+                w[i][3] = ld_nc4(reinterpret_cast<const uint4*>(src + 1536));
             } else {
                 w[i][0] = w[i][1] = w[i][2] = w[i][3] = zero;
             }

@@ -72,15 +72,16 @@ enum WaitKind : int { kWaitGrid = 1, kWaitUnit = 2, kWaitEmpty = 3, kWaitDrain =
 enum ErrorBit : int { kErrToken = 1, kErrBarrierTimeout = 2 };
 
 // Weight matrices are stored fragment-packed: the 16-row tiles of an [n, kp]
-// matrix one after another, each as kp/32 chunks of 1 KB, and inside a chunk
-// lane l = 4*(row%8) + (k%32)/8 of an m16n8k16 A fragment owns 32 bytes --
-// rows row%8 then row%8 + 8, eight k each.  A tile is one contiguous block a
-// bulk copy moves whole, and a warp reads a chunk as 32 consecutive 32-byte
-// pieces, conflict-free.
+// matrix one after another, each as kp/32 chunks of 1 KB.  In a chunk, lane
+// l = 4*(row%8) + (k%32)/8 of an m16n8k16 A fragment owns two 16-byte
+// pieces -- eight k of row row%8 at byte 16 l, eight k of row row%8 + 8 at
+// 512 + 16 l -- so each of a warp's two 16-byte loads of a chunk reads 512
+// contiguous bytes, free of bank conflicts.  A tile is one contiguous block a
+// bulk copy moves whole.
 __host__ __device__ inline size_t packed_offset(int n, int k, int chunks) {
     const int tile = n >> 4, row = n & 15, chunk = k >> 5, kk = k & 31;
     const int lane = (row & 7) * 4 + (kk >> 3);
-    return (((size_t)tile * chunks + chunk) * 32 + lane) * 16 + (row >> 3) * 8 + (kk & 7);
+    return (((size_t)tile * chunks + chunk) * 2 + (row >> 3)) * 256 + lane * 8 + (kk & 7);
 }
 
 // With many rows (the tensor-core products), weights and 16-bit activations
