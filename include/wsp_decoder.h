@@ -296,12 +296,13 @@ int wsp_argmax(const float* logits, const float* mask, uint32_t* indices, int ro
  * 51866); more is WSP_INVALID_ARGUMENT before anything is launched.  Nothing
  * in the scratch has to start at zero.
  *
- * Each call looks the scratch's address up in the current context
- * (cudaGetSymbolAddress, which allocates nothing once the module is
- * loaded), so no address outlives a cudaDeviceReset.  The first call in a
- * context may load the library's module: make it during set-up, before any
- * stream capture.  The call works on the current device; logits, mask and
- * indices are device pointers there.
+ * The first call on a device looks the scratch's address up
+ * (cudaGetSymbolAddress) with that device current and remembers it: make
+ * that first call during set-up, before any stream capture.  The address
+ * lives as long as the device's context: after cudaDeviceReset (or anything
+ * else that destroys the primary context) the remembered address is stale,
+ * so do not call this entry point again in that process.  The call works
+ * on the current device; logits, mask and indices are device pointers there.
  * It queues two kernels on `stream` (NULL: the legacy stream) and returns
  * without waiting; indices hold the result once the stream has passed them.
  *

@@ -1712,8 +1712,10 @@ int wsp_argmax_no_alloc(const float* logits, const float* mask, uint32_t* indice
                                        " row groups (rows x ceil(length / 2048)); " + std::to_string(row_count) +
                                        " rows of " + std::to_string(row_length) + " need " +
                                        std::to_string((long long)row_count * groups));
+        int device = 0;
+        wsp::cuda_check(cudaGetDevice(&device), "cudaGetDevice");
         void* scratch = nullptr;
-        wsp::cuda_check(wsp::no_alloc_argmax_scratch(&scratch), "cudaGetSymbolAddress (argmax scratch)");
+        wsp::cuda_check(wsp::no_alloc_argmax_scratch(device, &scratch), "cudaGetSymbolAddress (argmax scratch)");
         float* values = static_cast<float*>(scratch);
         uint32_t* candidates = reinterpret_cast<uint32_t*>(values + wsp::kNoAllocArgmaxCandidates);
         wsp::launch_argmax_rows(logits, mask, indices, row_count, row_length, values, candidates, groups,

@@ -4,6 +4,7 @@
 #include "kernels.cuh"
 
 #include <algorithm>
+#include <mutex>
 #include <stdexcept>
 
 namespace wsp {
@@ -80,12 +81,20 @@ __global__ void __launch_bounds__(kThreads) argmax_partial_kernel(const float* l
 // start at zero: the partial pass writes every slot the final pass reads.
 static __device__ __align__(256) unsigned char no_alloc_scratch[kNoAllocArgmaxCandidates * 8];
 
-// The scratch's address in the current context, looked up on every call (the
-// lookup allocates nothing once the module is loaded), so that no address
-// outlives a device reset or a context torn down and made again.
-cudaError_t no_alloc_argmax_scratch(void** scratch) {
-    *scratch = nullptr;
-    return cudaGetSymbolAddress(scratch, no_alloc_scratch);
+cudaError_t no_alloc_argmax_scratch(int device, void** scratch) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex lock;
+    static void* addresses[kMaxDevices] = {};
+    if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> guard(lock);
+    if (addresses[device] == nullptr) {
+        void* address = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&address, no_alloc_scratch);
+        if (e != cudaSuccess) return e;
+        addresses[device] = address;
+    }
+    *scratch = addresses[device];
+    return cudaSuccess;
 }
 
 void launch_argmax_final(const ArgmaxFinalArgs& a, cudaStream_t stream) {

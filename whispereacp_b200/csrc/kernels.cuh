@@ -34,8 +34,9 @@ int argmax_groups_per_row(int length);
 // (value, index) candidate pairs, rows x argmax_groups_per_row(length).
 constexpr int kNoAllocArgmaxCandidates = 65536;
 
-// The current device's address of that scratch (kNoAllocArgmaxCandidates
-// floats, then as many uint32 indices), from cudaGetSymbolAddress.
-cudaError_t no_alloc_argmax_scratch(void** scratch);
+// This device's address of that scratch (kNoAllocArgmaxCandidates floats,
+// then as many uint32 indices), looked up with cudaGetSymbolAddress the first
+// time a device asks, with that device current, and remembered after.
+cudaError_t no_alloc_argmax_scratch(int device, void** scratch);
 
 }  // namespace wsp
