@@ -1086,6 +1086,35 @@ private:
         }
     }
 
+    // The tensor-core path: a split residual product (the out-projections,
+    // fc2) followed by a norm op over every row leaves its join to that norm
+    // (StepOp::defer_join): the norm's CTA for a row sums the row's partials
+    // in split order, adds the bias and then the residual row -- the sums the
+    // join and its atomic add would make -- writes the new residual row back
+    // to h and normalises it.  The product ends at its partials, without a
+    // meeting of its splits.
+    void defer_residual_joins(std::vector<StepOp>& ops, const StepParams& p) const {
+        if (!p.umma) return;
+        const int groups = (p.rows + p.umma_rows - 1) / p.umma_rows, row_stride = groups * p.umma_rows;
+        for (size_t i = 0; i + 1 < ops.size(); ++i) {
+            StepOp& product = ops[i];
+            StepOp& norm = ops[i + 1];
+            if (product.kind != kOpProduct || product.epilogue != kEpResidual || product.ksplit <= 1 ||
+                product.defer_join || !product.bias || product.out != static_cast<void*>(p.h) ||
+                product.ld_out != p.width || norm.kind != kOpNorm || !norm.norm_umma || norm.addend_count > 0 ||
+                norm.norm_rows != p.rows || norm.norm_step != 1 || norm.norm_offset != 0)
+                continue;
+            const int m_tiles = (product.n + 127) / 128;
+            product.defer_join = 1;
+            norm.addends = p.partial_d;
+            norm.addend_count = product.ksplit;
+            norm.addend_stride = (long long)m_tiles * row_stride * 128;
+            norm.addend_tile_rows = row_stride;
+            norm.addend_bias = product.bias;
+            norm.sum_out = p.h;
+        }
+    }
+
     // The weight-stream schedule of every CTA (schedule.h), into device memory.
     void upload_schedule(StepParams& p, const std::vector<StepOp>& ops, int grid) {
         build_schedule(p, ops, grid, decode_tile_rows(p), schedule_host_, offsets_host_);
@@ -1242,6 +1271,7 @@ private:
         if (partial_d_.bytes() < partial_bytes) partial_d_.allocate(partial_bytes);
         p.partial_d = partial_d_.get<float>();
         defer_qkv_joins(ops, p, grid);
+        defer_residual_joins(ops, p);
         if (umma_) {
             const size_t counter_bytes = ops.size() * kSplitSlots * sizeof(unsigned);
             if (split_counters_.bytes() < counter_bytes) split_counters_.allocate(counter_bytes);

@@ -456,6 +456,7 @@ struct Addends {
     long long stride = 0;
     const float* bias = nullptr;
     float* sum_out = nullptr;
+    int tile_rows = 0;  // > 0: a tensor-core product's split partials (StepOp::addend_tile_rows)
 };
 
 // v[i] (element c0 + i*step of row `row`, i < N, columns below d) plus the
@@ -474,6 +475,41 @@ __device__ __forceinline__ void add_addends(const Addends& a, size_t row, int d,
     for (int i = 0; i < N; ++i) {
         const int c = c0 + i * step;
         bias[i] = c < d ? __ldg(a.bias + c) : 0.f;
+    }
+    if (a.tile_rows > 0) {
+        // A tensor-core product's split partials: element (row, c) of split j
+        // at j * stride + ((c / 128) * tile_rows + row) * 128 + c % 128.
+        // The splits sum in order from zero, the bias is added to that sum
+        // and the result to the row -- the product's join (its sum plus
+        // bias, added to the residual row), bit for bit.
+        float sum[N];
+        int at[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const int c = c0 + i * step;
+            sum[i] = 0.f;
+            at[i] = ((c >> 7) * a.tile_rows + (int)row) * 128 + (c & 127);
+        }
+        for (int j0 = 0; j0 < a.count; j0 += kBatch) {
+            float t[kBatch][N];
+#pragma unroll
+            for (int jj = 0; jj < kBatch; ++jj)
+#pragma unroll
+                for (int i = 0; i < N; ++i)
+                    t[jj][i] = j0 + jj < a.count && c0 + i * step < d
+                                   ? ld_cg(a.base + (size_t)(j0 + jj) * a.stride + at[i])
+                                   : 0.f;
+#pragma unroll
+            for (int jj = 0; jj < kBatch; ++jj)
+                if (j0 + jj < a.count) {
+#pragma unroll
+                    for (int i = 0; i < N; ++i) sum[i] += t[jj][i];
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i)
+            if (c0 + i * step < d) v[i] += sum[i] + bias[i];
+        return;
     }
     for (int j0 = 0; j0 < a.count; j0 += kBatch) {
         float t[kBatch][N];
@@ -654,15 +690,18 @@ __device__ void op_norm(const StepParams& p, const StepOp& op, unsigned char* wo
     WT* out = static_cast<WT*>(op.out);
     const size_t lo = lo_plane(p, op.ld_out);
     WT* row16 = reinterpret_cast<WT*>(work);  // the block layout: a row (hi, lo) first, then its pieces
+    Addends add;
+    if (op.addend_count > 0)
+        add = Addends{op.addends, op.addend_count, op.addend_stride, op.addend_bias, op.sum_out, op.addend_tile_rows};
     for (int row = blockIdx.x; row < op.norm_rows; row += gridDim.x) {
         consumer_sync();
         if (!op.norm_umma) {
             layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, row, 1, op.norm_step, op.norm_offset,
-                                out + (size_t)row * op.ld_out, op.ld_out, lo, op.norm_hidden);
+                                out + (size_t)row * op.ld_out, op.ld_out, lo, op.norm_hidden, add);
             continue;
         }
         layer_norm_tile<WT>(p, p.h, op.gamma, op.beta, row, 1, op.norm_step, op.norm_offset, row16, op.ld_out,
-                            (size_t)op.ld_out, op.norm_hidden);
+                            (size_t)op.ld_out, op.norm_hidden, add);
         consumer_sync();
         for (int c = 8 * threadIdx.x; c < op.ld_out; c += 8 * kThreads) {
             WT* at = out + act_offset(row, c, p.act_rows);

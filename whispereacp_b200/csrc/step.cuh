@@ -142,11 +142,15 @@ struct StepOp {
     // op after it adds them, so the out-projection is no op of its own.
     const void* out_weight;
     float* out_partial;
-    // LayerNorm prologues: the rows normalised are norm_input (p.h when
-    // null) plus, with addend_count > 0, addend_bias and addends + j *
-    // addend_stride (row-major [R][d]) for j = 0 .. addend_count-1 in that
-    // order; the CTA that holds a row tile's first weight tile writes those
-    // sums, the new residual rows, to sum_out.
+    // LayerNorm prologues and norm ops: the rows normalised are norm_input
+    // (p.h when null) plus, with addend_count > 0, addend_bias and addends +
+    // j * addend_stride (row-major [R][d]) for j = 0 .. addend_count-1 in
+    // that order; the CTA that holds a row tile's first weight tile (a norm
+    // op: the row's CTA) writes those sums, the new residual rows, to
+    // sum_out.  With addend_tile_rows > 0 the addends are a tensor-core
+    // product's split partials instead ([split][weight tile][row][128],
+    // addend_tile_rows rows a tile), summed in split order and then added
+    // with the bias: the product's own join, moved into the norm after it.
     const float* norm_input;
     const float* addends;
     int addend_count;
@@ -156,15 +160,18 @@ struct StepOp {
     // q/k/v products (a few rows): prefetch into L2 the self keys and values
     // the self attention after it reads.
     int prefetch_keys;
+    int addend_tile_rows;
     // Tensor-core products: K splits of each tile's inner size.  With more
     // than one (only when all the items fit one wave of CTAs), each item
     // writes fp32 partials to p.partial_d [split][n_pad][rows_pad], the
     // tile's splits meet, and each sums its share of the rows in split order
     // and applies the epilogue.
     int ksplit;
-    // A split q/k/v product whose join is left to the self attention after
-    // it (single-token steps of the tensor-core path): the product stops at
-    // its partials; the self attention sums the partials of its (row, head)
+    // A split product whose join is left to the op after it: a q/k/v
+    // product's to the self attention (single-token steps of the tensor-core
+    // path), a residual product's to the norm op (addend_tile_rows above).
+    // The product stops at its partials.  The self attention sums the
+    // partials of its (row, head)
     // -- qkv_splits of them, qkv_split_stride floats apart, rows
     // qkv_row_stride apart in a weight tile's block, in split order, then
     // qkv_bias -- appends k and v to the caches and attends with q.
