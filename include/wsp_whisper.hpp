@@ -662,8 +662,16 @@ public:
     // Whisper::transcribe on recordings: one per window the decoder was
     // prepared with, each 16 kHz samples of at most one 30 s window (a
     // longer one is a ModelError, as in the reference), through the
-    // spectrogram and the encoder, then the greedy search.
+    // spectrogram and the encoder, then the greedy search.  Whole windows
+    // only: with a reduced audio context the reference's encoder itself
+    // computes that many positions from the first twice as many mel frames
+    // (Whisper.h:382-402), which this front end does not do yet, so a
+    // reduced context here is a ModelError rather than a different answer.
     std::vector<std::vector<uint32_t>> transcribe_samples(const std::vector<std::vector<float>>& recordings) {
+        if (audio_context_ != 0 && audio_context_ < config_.max_source_positions)
+            throw ModelError("the CUDA front end encodes whole windows, and this Whisper has an audio context of " +
+                             std::to_string(audio_context_) + " positions: transcribe encoder rows of that context "
+                             "instead, or set the context back to zero");
         require_prepared();
         if (!encoder_) throw ModelError("this model has no encoder tensors: transcribe its encoder rows instead");
         const int windows = decoder_->windows();

@@ -12,6 +12,9 @@
 //       set the audio context, transcribe the fp32 rows in ENCODER
 //       ([WINDOWS, max_source_positions, d_model]) and print each window's
 //       ids and the hex bytes of its text
+//   whisper_test context-samples DIR CONTEXT
+//       load, set the audio context, and print the ModelError that
+//       transcribe_samples raises for a reduced one (exit 1 if none)
 //   whisper_test samples DIR AUDIO WINDOWS COUNT
 //       load, prepare with WINDOWS windows, transcribe the recordings in
 //       AUDIO (WINDOWS x COUNT fp32 samples) through the spectrogram and the
@@ -120,6 +123,20 @@ int transcribe(char** argv) {
     return 0;
 }
 
+int context_samples(char** argv) {
+    wsp::Whisper whisper;
+    whisper.load(argv[2]);
+    whisper.set_audio_context(std::stoi(argv[3]));
+    try {
+        whisper.transcribe_samples({});
+    } catch (const wsp::ModelError& e) {
+        std::printf("refused: %s\n", e.what());
+        return 0;
+    }
+    std::printf("accepted\n");
+    return 1;
+}
+
 int samples(char** argv) {
     wsp::Whisper whisper;
     whisper.load(argv[2]);
@@ -157,7 +174,7 @@ int samples(char** argv) {
 
 int main(int argc, char** argv) {
     if (argc < 3) {
-        std::printf("usage: whisper_test inspect|refuse|transcribe|samples DIR ...\n");
+        std::printf("usage: whisper_test inspect|refuse|transcribe|samples|context-samples DIR ...\n");
         return 2;
     }
     const std::string mode = argv[1];
@@ -166,6 +183,7 @@ int main(int argc, char** argv) {
         if (mode == "refuse") return refuse(argv);
         if (mode == "transcribe" && argc >= 7) return transcribe(argv);
         if (mode == "samples" && argc >= 6) return samples(argv);
+        if (mode == "context-samples" && argc >= 4) return context_samples(argv);
     } catch (const std::exception& e) {
         std::printf("error: %s\n", e.what());
         return 1;

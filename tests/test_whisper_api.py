@@ -126,6 +126,19 @@ def test_audio_context_for_samples(program, repo):
     assert ids_of(f["context"][0]) == [448, 1152, 1500]
 
 
+def test_a_reduced_audio_context_is_not_run_through_the_front_end(program, repo):
+    """The reference's encoder computes a reduced context's positions itself
+    (Whisper.h:382-402); the CUDA front end encodes whole windows, so
+    transcribe_samples refuses a reduced context instead of answering
+    differently.  Zero and the whole window pass that check (and then stop
+    at the missing prepare)."""
+    out = run(program, "context-samples", repo.directory, 16)
+    assert "encodes whole windows" in out and "audio context of 16 positions" in out
+    for whole in (0, repo.config["max_source_positions"]):
+        out = run(program, "context-samples", repo.directory, whole)
+        assert "has not been prepared" in out, out
+
+
 @pytest.mark.parametrize("change,message", [
     (lambda d: os.remove(os.path.join(d, "tokenizer.json")), "has no tokenizer.json"),
     (lambda d: os.remove(os.path.join(d, "preprocessor_config.json")), "has no preprocessor_config.json"),
